@@ -1,0 +1,346 @@
+// ref_engine_harness.cpp -- drives the reference C++ engine's memory-layer step.
+//
+// TEST INFRASTRUCTURE ONLY.  This translation unit #includes the reference
+// engine's own sources where they lie (REF_ENGINE_SRC points at
+// <reference>/src/cpp/engine/src) and is built by oracle/Makefile into
+// oracle/_ref/.  Nothing from the reference is copied into this repository.
+//
+// The reference step functions are file-static (deltagrid_math.cpp:174,
+// deltagrid_fxp.cpp:181), which is why they are reached by inclusion.  The
+// harness builds one memory layer with seeded random weights, runs T steps
+// and exports, per step, the kernel-level inputs the engine computed (routed
+// wk/wq/idx, v, beta, alpha) and its read-out y_t, plus the final state.  The
+// oracle restatement (dg_oracle.c) must reproduce y and the state from those
+// inputs.  A second entry point times the engine for the CPU baseline.
+//
+// Engine modes: 0 = dense (Slots == Dh), 1 = dense with slot projection,
+// 2 = sparse PKM (two axes, top_k).
+
+#include "deltagrid_auth.cpp"
+#include "deltagrid_math.cpp"
+#include "deltagrid_math_fxp.cpp"
+#include "deltagrid_fxp.cpp"
+
+#include <chrono>
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+namespace {
+
+struct Rng {
+    uint64_t s;
+    explicit Rng(uint64_t seed) : s(seed * 0x9E3779B97F4A7C15ull + 0x2545F4914F6CDD1Dull) {}
+    uint64_t next() {
+        s ^= s >> 12; s ^= s << 25; s ^= s >> 27;
+        return s * 0x2545F4914F6CDD1Dull;
+    }
+    float uniform() { return (float)((next() >> 40) + 0.5) / 16777216.0f; }
+    float normal() {
+        float u1 = uniform(), u2 = uniform();
+        return std::sqrt(-2.0f * std::log(u1)) * std::cos(6.28318530718f * u2);
+    }
+};
+
+struct F32Layer {
+    DGRuntimeContext ctx;
+    DGMemoryLayerWeights mem;
+    std::vector<std::vector<float>> store;
+    std::vector<float*> axk, axq;
+    std::vector<int32_t> grid;
+    std::vector<int32_t> idxbuf, idxaxes;
+    float* alloc(size_t n, Rng* r = nullptr, float scale = 0.f, float fill = 0.f) {
+        store.emplace_back(n, fill);
+        if (r) for (auto& x : store.back()) x = r->normal() * scale;
+        return store.back().data();
+    }
+};
+
+void build_f32(F32Layer& L, int mode, int H, int Dh, int slots, int G0, int G1, int topk,
+               int dyn, uint64_t seed) {
+    Rng r(seed);
+    std::memset(&L.ctx, 0, sizeof(L.ctx));
+    std::memset(&L.mem, 0, sizeof(L.mem));
+    const int D = H * Dh;
+    DeltaGridBinHeader& hd = L.ctx.header;
+    hd.d_model = D; hd.num_heads = H; hd.num_layers = 1;
+    hd.num_axes = (mode == 2) ? 2 : 0;
+    hd.top_k = (mode == 2) ? topk : 0;
+    hd.actual_slots = (mode == 2) ? G0 * G1 : (mode == 1 ? slots : Dh);
+    hd.flags = (dyn ? DG_FLAG_DYNAMIC_DECAY : 0) | (mode == 1 ? DG_FLAG_HAS_SLOT_PROJ : 0);
+    L.ctx.head_dim = Dh;
+    const int A = (mode == 2) ? topk * topk : hd.actual_slots;
+    L.ctx.active_slots = A;
+    if (mode == 2) {
+        L.grid = {G0, G1};
+        L.ctx.grid_dim = L.grid.data();
+        L.ctx.max_axis_dim = G0 > G1 ? G0 : G1;
+        L.ctx.max_axis_active = topk;
+    }
+    const float ws = 1.0f / std::sqrt((float)D);
+    L.mem.has_memory = 1;
+    L.mem.proj_qkv_beta.f32 = L.alloc((size_t)(3 * D + H) * D, &r, ws);
+    L.mem.q_scale = L.alloc(H, nullptr, 0.f, 1.0f);
+    for (int h = 0; h < H; ++h) L.mem.q_scale[h] = 0.75f + 0.5f * r.uniform();
+    L.mem.beta_bias = L.alloc(H, &r, 0.5f);
+    L.mem.decay = L.alloc(H, nullptr, 0.f, 1.0f);
+    for (int h = 0; h < H; ++h) L.mem.decay[h] = 0.995f + 0.005f * r.uniform();
+    if (dyn) {
+        L.mem.proj_alpha_weight.f32 = L.alloc((size_t)H * D, &r, ws);
+        L.mem.proj_alpha_bias = L.alloc(H, &r, 1.0f);
+    }
+    if (mode == 1) {
+        L.mem.slot_proj_k = L.alloc((size_t)slots * Dh, &r, 1.0f / std::sqrt((float)Dh));
+        L.mem.slot_proj_q = L.alloc((size_t)slots * Dh, &r, 1.0f / std::sqrt((float)Dh));
+    }
+    if (mode == 2) {
+        L.axk = {L.alloc((size_t)G0 * Dh, &r, 1.0f / std::sqrt((float)Dh)),
+                 L.alloc((size_t)G1 * Dh, &r, 1.0f / std::sqrt((float)Dh))};
+        L.axq = {L.alloc((size_t)G0 * Dh, &r, 1.0f / std::sqrt((float)Dh)),
+                 L.alloc((size_t)G1 * Dh, &r, 1.0f / std::sqrt((float)Dh))};
+        L.mem.axes_proj_k = L.axk.data();
+        L.mem.axes_proj_q = L.axq.data();
+    }
+    L.mem.out_proj.f32 = L.alloc((size_t)D * D, &r, ws);
+    L.mem.norm.weight = L.alloc(D, nullptr, 0.f, 1.0f);
+    L.mem.norm.bias = L.alloc(D);
+    DGRuntimeContext& c = L.ctx;
+    c.packed_qkvb_buf = L.alloc(3 * D + H);
+    c.q_buf = L.alloc(D); c.k_buf = L.alloc(D); c.v_buf = L.alloc(D);
+    c.beta_buf = L.alloc(H); c.alpha_buf = L.alloc(H);
+    c.yt_buf = L.alloc(D); c.mem_proj_buf = L.alloc(D); c.mem_out_buf = L.alloc(D);
+    c.wk_buf = L.alloc((size_t)H * A); c.wq_buf = L.alloc((size_t)H * A);
+    L.idxbuf.assign((size_t)H * A, 0);
+    c.active_idx_buf = L.idxbuf.data();
+    const int mx = (mode == 2) ? L.ctx.max_axis_dim : 1;
+    c.sk_buf = L.alloc((size_t)H * mx); c.sq_buf = L.alloc((size_t)H * mx);
+    c.uk_axes_buf = L.alloc((size_t)H * 2 * (topk > 0 ? topk : 1));
+    c.uq_axes_buf = L.alloc((size_t)H * 2 * (topk > 0 ? topk : 1));
+    L.idxaxes.assign((size_t)H * 2 * (topk > 0 ? topk : 1), 0);
+    c.idx_axes_buf = L.idxaxes.data();
+}
+
+struct FxpLayer {
+    DGFxpContext ctx;
+    DGFxpMemoryLayer mem;
+    std::vector<std::vector<int32_t>> store;
+    std::vector<int32_t*> axk, axq;
+    std::vector<int32_t> grid;
+    int32_t* alloc(size_t n, Rng* r = nullptr, float scale = 0.f, int32_t fill = 0) {
+        store.emplace_back(n, fill);
+        if (r) for (auto& x : store.back()) x = DG_FLOAT_TO_FXP(r->normal() * scale);
+        return store.back().data();
+    }
+};
+
+void build_fxp(FxpLayer& L, int mode, int H, int Dh, int slots, int G0, int G1, int topk,
+               int dyn, uint64_t seed) {
+    Rng r(seed);
+    std::memset(&L.ctx, 0, sizeof(L.ctx));
+    std::memset(&L.mem, 0, sizeof(L.mem));
+    const int D = H * Dh;
+    DeltaGridBinHeader& hd = L.ctx.header;
+    hd.d_model = D; hd.num_heads = H; hd.num_layers = 1;
+    hd.num_axes = (mode == 2) ? 2 : 0;
+    hd.top_k = (mode == 2) ? topk : 0;
+    hd.actual_slots = (mode == 2) ? G0 * G1 : (mode == 1 ? slots : Dh);
+    hd.flags = (dyn ? DG_FLAG_DYNAMIC_DECAY : 0) | (mode == 1 ? DG_FLAG_HAS_SLOT_PROJ : 0);
+    L.ctx.head_dim = Dh;
+    const int A = (mode == 2) ? topk * topk : hd.actual_slots;
+    L.ctx.active_slots = A;
+    if (mode == 2) {
+        L.grid = {G0, G1};
+        L.ctx.grid_dim = L.grid.data();
+        L.ctx.max_axis_dim = G0 > G1 ? G0 : G1;
+        L.ctx.max_axis_active = topk;
+    }
+    const float ws = 1.0f / std::sqrt((float)D);
+    L.mem.has_memory = 1;
+    L.mem.proj_qkv_beta = L.alloc((size_t)(3 * D + H) * D, &r, ws);
+    L.mem.q_scale = L.alloc(H);
+    for (int h = 0; h < H; ++h) L.mem.q_scale[h] = DG_FLOAT_TO_FXP(0.75f + 0.5f * r.uniform());
+    L.mem.beta_bias = L.alloc(H, &r, 0.5f);
+    L.mem.decay = L.alloc(H);
+    for (int h = 0; h < H; ++h) L.mem.decay[h] = DG_FLOAT_TO_FXP(0.995f + 0.005f * r.uniform());
+    if (dyn) {
+        L.mem.proj_alpha_w = L.alloc((size_t)H * D, &r, ws);
+        L.mem.proj_alpha_b = L.alloc(H, &r, 1.0f);
+    }
+    if (mode == 1) {
+        L.mem.slot_proj_k = L.alloc((size_t)slots * Dh, &r, 1.0f / std::sqrt((float)Dh));
+        L.mem.slot_proj_q = L.alloc((size_t)slots * Dh, &r, 1.0f / std::sqrt((float)Dh));
+    }
+    if (mode == 2) {
+        L.axk = {L.alloc((size_t)G0 * Dh, &r, 1.0f / std::sqrt((float)Dh)),
+                 L.alloc((size_t)G1 * Dh, &r, 1.0f / std::sqrt((float)Dh))};
+        L.axq = {L.alloc((size_t)G0 * Dh, &r, 1.0f / std::sqrt((float)Dh)),
+                 L.alloc((size_t)G1 * Dh, &r, 1.0f / std::sqrt((float)Dh))};
+        L.mem.axes_proj_k = L.axk.data();
+        L.mem.axes_proj_q = L.axq.data();
+    }
+    L.mem.out_proj = L.alloc((size_t)D * D, &r, ws);
+    L.mem.norm.weight = L.alloc(D, nullptr, 0.f, DG_FXP_ONE);
+    L.mem.norm.bias = L.alloc(D);
+    DGFxpContext& c = L.ctx;
+    c.packed_qkvb_buf = L.alloc(3 * D + H);
+    c.q_buf = L.alloc(D); c.k_buf = L.alloc(D); c.v_buf = L.alloc(D);
+    c.beta_buf = L.alloc(H); c.alpha_buf = L.alloc(H);
+    c.yt_buf = L.alloc(D); c.mem_proj_buf = L.alloc(D); c.mem_out_buf = L.alloc(D);
+    c.wk_buf = L.alloc((size_t)H * A); c.wq_buf = L.alloc((size_t)H * A);
+    c.active_idx_buf = L.alloc((size_t)H * A);
+    const int mx = (mode == 2) ? L.ctx.max_axis_dim : 1;
+    c.sk_buf = L.alloc((size_t)H * mx); c.sq_buf = L.alloc((size_t)H * mx);
+    c.uk_axes_buf = L.alloc((size_t)H * 2 * (topk > 0 ? topk : 1));
+    c.uq_axes_buf = L.alloc((size_t)H * 2 * (topk > 0 ? topk : 1));
+    c.idx_axes_buf = L.alloc((size_t)H * 2 * (topk > 0 ? topk : 1));
+}
+
+}  // namespace
+
+extern "C" {
+
+// Runs T steps of dg_memory_layer_step (deltagrid_math.cpp:174-417) on a
+// seeded random layer.  Per-step exports use layout [T, H, ...]; the state is
+// [H, slots, Dh].  state_init (nullable) seeds the state.  Returns 0 on success.
+int ref_f32_layer_run(int mode, int H, int Dh, int slots, int G0, int G1, int topk, int dyn,
+                      int T, unsigned long long seed, const float* state_init,
+                      float* wk_out, float* wq_out, int32_t* idx_out, float* v_out,
+                      float* beta_out, float* alpha_out, float* y_out, float* state_out) {
+    F32Layer L;
+    build_f32(L, mode, H, Dh, slots, G0, G1, topk, dyn, seed);
+    const int D = H * Dh;
+    const int A = L.ctx.active_slots;
+    const size_t nstate = (size_t)H * L.ctx.header.actual_slots * Dh;
+    std::vector<float> state(nstate, 0.f);
+    if (state_init) std::memcpy(state.data(), state_init, nstate * sizeof(float));
+    std::vector<float> h(D);
+    Rng r(seed ^ 0xABCDEFull);
+    for (int t = 0; t < T; ++t) {
+        for (auto& x : h) x = r.normal();
+        dg_memory_layer_step(&L.ctx, L.mem, h.data(), state.data(), L.ctx.mem_out_buf);
+        std::memcpy(wk_out + (size_t)t * H * A, L.ctx.wk_buf, sizeof(float) * H * A);
+        std::memcpy(wq_out + (size_t)t * H * A, L.ctx.wq_buf, sizeof(float) * H * A);
+        if (idx_out) std::memcpy(idx_out + (size_t)t * H * A, L.ctx.active_idx_buf, sizeof(int32_t) * H * A);
+        std::memcpy(v_out + (size_t)t * D, L.ctx.v_buf, sizeof(float) * D);
+        std::memcpy(beta_out + (size_t)t * H, L.ctx.beta_buf, sizeof(float) * H);
+        std::memcpy(alpha_out + (size_t)t * H, L.ctx.alpha_buf, sizeof(float) * H);
+        std::memcpy(y_out + (size_t)t * D, L.ctx.yt_buf, sizeof(float) * D);
+    }
+    std::memcpy(state_out, state.data(), nstate * sizeof(float));
+    return 0;
+}
+
+// Same for the Q16.16 engine (dg_memory_layer_step_fxp, deltagrid_fxp.cpp:181-413).
+int ref_fxp_layer_run(int mode, int H, int Dh, int slots, int G0, int G1, int topk, int dyn,
+                      int T, unsigned long long seed, const int32_t* state_init,
+                      int32_t* wk_out, int32_t* wq_out, int32_t* idx_out, int32_t* v_out,
+                      int32_t* beta_out, int32_t* alpha_out, int32_t* y_out,
+                      int32_t* state_out, int32_t* k_out, int32_t* q_out) {
+    FxpLayer L;
+    build_fxp(L, mode, H, Dh, slots, G0, G1, topk, dyn, seed);
+    const int D = H * Dh;
+    const int A = L.ctx.active_slots;
+    const size_t nstate = (size_t)H * L.ctx.header.actual_slots * Dh;
+    std::vector<int32_t> state(nstate, 0);
+    if (state_init) std::memcpy(state.data(), state_init, nstate * sizeof(int32_t));
+    std::vector<int32_t> h(D);
+    Rng r(seed ^ 0xABCDEFull);
+    for (int t = 0; t < T; ++t) {
+        for (auto& x : h) x = DG_FLOAT_TO_FXP(r.normal());
+        dg_memory_layer_step_fxp(&L.ctx, L.mem, h.data(), state.data(), L.ctx.mem_out_buf);
+        std::memcpy(wk_out + (size_t)t * H * A, L.ctx.wk_buf, sizeof(int32_t) * H * A);
+        std::memcpy(wq_out + (size_t)t * H * A, L.ctx.wq_buf, sizeof(int32_t) * H * A);
+        if (idx_out) std::memcpy(idx_out + (size_t)t * H * A, L.ctx.active_idx_buf, sizeof(int32_t) * H * A);
+        std::memcpy(v_out + (size_t)t * D, L.ctx.v_buf, sizeof(int32_t) * D);
+        std::memcpy(beta_out + (size_t)t * H, L.ctx.beta_buf, sizeof(int32_t) * H);
+        std::memcpy(alpha_out + (size_t)t * H, L.ctx.alpha_buf, sizeof(int32_t) * H);
+        std::memcpy(y_out + (size_t)t * D, L.ctx.yt_buf, sizeof(int32_t) * D);
+        if (k_out) std::memcpy(k_out + (size_t)t * D, L.ctx.k_buf, sizeof(int32_t) * D);
+        if (q_out) std::memcpy(q_out + (size_t)t * D, L.ctx.q_buf, sizeof(int32_t) * D);
+    }
+    std::memcpy(state_out, state.data(), nstate * sizeof(int32_t));
+    return 0;
+}
+
+// Router weights of the fxp layer built with the same arguments (for routing checks).
+int ref_fxp_router_weights(int H, int Dh, int G0, int G1, int topk, int dyn,
+                           unsigned long long seed, int32_t* wk0, int32_t* wk1,
+                           int32_t* wq0, int32_t* wq1, int32_t* q_scale) {
+    FxpLayer L;
+    build_fxp(L, 2, H, Dh, 0, G0, G1, topk, dyn, seed);
+    std::memcpy(wk0, L.axk[0], sizeof(int32_t) * G0 * Dh);
+    std::memcpy(wk1, L.axk[1], sizeof(int32_t) * G1 * Dh);
+    std::memcpy(wq0, L.axq[0], sizeof(int32_t) * G0 * Dh);
+    std::memcpy(wq1, L.axq[1], sizeof(int32_t) * G1 * Dh);
+    std::memcpy(q_scale, L.mem.q_scale, sizeof(int32_t) * H);
+    return 0;
+}
+
+// CPU baseline: wall time of `steps` calls of dg_memory_layer_step on each of
+// `contexts` independent layers (one per batch row, all heads of a row in one
+// context, OpenMP over heads inside the step as the engine does,
+// deltagrid_math.cpp:220-223).  proj_seconds receives the time of the same
+// number of projection-only calls (qkv/beta projection, out_proj, LayerNorm),
+// which the engine step includes and which lie outside the recurrence.
+double ref_f32_time(int mode, int H, int Dh, int slots, int G0, int G1, int topk, int dyn,
+                    int steps, int contexts, double* proj_seconds) {
+    std::vector<F32Layer> layers(contexts);
+    std::vector<std::vector<float>> states(contexts);
+    for (int c = 0; c < contexts; ++c) {
+        build_f32(layers[c], mode, H, Dh, slots, G0, G1, topk, dyn, 1234 + c);
+        states[c].assign((size_t)H * layers[c].ctx.header.actual_slots * Dh, 0.f);
+    }
+    const int D = H * Dh;
+    std::vector<float> h(D);
+    Rng r(99);
+    for (auto& x : h) x = r.normal();
+    auto t0 = std::chrono::steady_clock::now();
+    for (int s = 0; s < steps; ++s)
+        for (int c = 0; c < contexts; ++c)
+            dg_memory_layer_step(&layers[c].ctx, layers[c].mem, h.data(), states[c].data(),
+                                 layers[c].ctx.mem_out_buf);
+    auto t1 = std::chrono::steady_clock::now();
+    if (proj_seconds) {
+        auto p0 = std::chrono::steady_clock::now();
+        for (int s = 0; s < steps; ++s)
+            for (int c = 0; c < contexts; ++c) {
+                DGRuntimeContext& x = layers[c].ctx;
+                dg_matmul_bias(h.data(), layers[c].mem.proj_qkv_beta, nullptr, x.packed_qkvb_buf, 3 * D + H, D);
+                dg_matmul_bias(x.yt_buf, layers[c].mem.out_proj, nullptr, x.mem_proj_buf, D, D);
+                dg_layernorm(x.mem_proj_buf, D, layers[c].mem.norm.weight, layers[c].mem.norm.bias, x.mem_out_buf);
+            }
+        auto p1 = std::chrono::steady_clock::now();
+        *proj_seconds = std::chrono::duration<double>(p1 - p0).count();
+    }
+    return std::chrono::duration<double>(t1 - t0).count();
+}
+
+// Same timing for the Q16.16 engine step (deltagrid_fxp.cpp:181-413).
+double ref_fxp_time(int mode, int H, int Dh, int slots, int G0, int G1, int topk, int dyn,
+                    int steps, int contexts) {
+    std::vector<FxpLayer> layers(contexts);
+    std::vector<std::vector<int32_t>> states(contexts);
+    for (int c = 0; c < contexts; ++c) {
+        build_fxp(layers[c], mode, H, Dh, slots, G0, G1, topk, dyn, 1234 + c);
+        states[c].assign((size_t)H * layers[c].ctx.header.actual_slots * Dh, 0);
+    }
+    const int D = H * Dh;
+    std::vector<int32_t> h(D);
+    Rng r(99);
+    for (auto& x : h) x = DG_FLOAT_TO_FXP(r.normal());
+    auto t0 = std::chrono::steady_clock::now();
+    for (int s = 0; s < steps; ++s)
+        for (int c = 0; c < contexts; ++c)
+            dg_memory_layer_step_fxp(&layers[c].ctx, layers[c].mem, h.data(), states[c].data(),
+                                     layers[c].ctx.mem_out_buf);
+    auto t1 = std::chrono::steady_clock::now();
+    return std::chrono::duration<double>(t1 - t0).count();
+}
+
+// Top-k known-answer entry (deltagrid_math.cpp:142-168 as shipped).
+void ref_topk_desc(const float* scores, int n, int k, float* vals, int32_t* idx) {
+    dg_topk_descending(scores, n, k, vals, idx);
+}
+
+}  // extern "C"

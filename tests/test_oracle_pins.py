@@ -1,0 +1,138 @@
+"""Pins the CPU oracle (oracle/dg_oracle.c) before anything is checked against it.
+
+* against golden vectors produced by the reference PyTorch layer
+  (tests/golden/make_golden.py: memory.py per-step loops and router);
+* against the reference C++ engine's own exports (golden engine_*.npz, and the
+  live oracle/_ref library when it was built);
+* against the engine's known-answer tests (engine/tests/test_math.cpp:44-53,
+  engine/tests/test_fxp.cpp:6-31).
+"""
+import numpy as np
+import pytest
+
+from conftest import load_golden, rel_err
+from oracle import oracle as O
+
+FP32_TOL = 1e-5
+
+
+@pytest.mark.parametrize("name", ["dense_static_f32.npz", "dense_slotproj_dyn_f32.npz"])
+def test_dense_loop_golden(name):
+    g = load_golden(name)
+    out, s = O.dense_forward(g["v"], g["beta"], g["wk"], g["wq"], g["decay"], g["s_init"],
+                             dynamic=bool(g["dynamic"]))
+    assert rel_err(out, g["y"]) < FP32_TOL
+    assert rel_err(s, g["s_final"]) < FP32_TOL
+
+
+@pytest.mark.parametrize("name", ["pkm_g16_k4_f32.npz", "pkm_g32_k8_f32.npz"])
+def test_pkm_loop_golden(name):
+    g = load_golden(name)
+    out, s = O.pkm_forward(g["v"], g["beta"], g["wk"], g["wq"], g["idx"], g["decay"], g["s_init"],
+                           O.F32, dynamic=bool(g["dynamic"]))
+    assert rel_err(out, g["y"]) < FP32_TOL
+    assert rel_err(s, g["s_final"]) < FP32_TOL
+
+
+@pytest.mark.parametrize("name", ["pkm_g16_k4_f32.npz", "pkm_g32_k8_f32.npz", "router_g128_k8.npz"])
+def test_router_golden(name):
+    g = load_golden(name)
+    top_k = int(round(np.sqrt(g["wk"].shape[-1])))
+    qs = None
+    if "q_scale" in g:
+        qs = np.broadcast_to(g["q_scale"][None, :, None], g["k"].shape[:-1])
+    wk, wq, idx, margin = O.pkm_route(g["k"], g["q"], g["router_k0"], g["router_k1"],
+                                      g["router_q0"], g["router_q1"], top_k, q_scale=qs)
+    ok = margin > 1e-5            # documented near-tie exclusion
+    assert ok.mean() > 0.95
+    np.testing.assert_array_equal(idx[ok], g["idx"][ok])
+    assert rel_err(wk[ok], g["wk"][ok]) < FP32_TOL
+    assert rel_err(wq[ok], g["wq"][ok]) < FP32_TOL
+
+
+def test_topk_tie_order_kat():
+    # engine/tests/test_math.cpp:44-53: equal scores 3.5 at indices 1 and 4 keep index order
+    vals, idx = O.topk_desc([0.1, 3.5, -1.0, 9.2, 3.5, 2.0], 3)
+    assert idx.tolist() == [3, 1, 4]
+    np.testing.assert_allclose(vals, [9.2, 3.5, 3.5], rtol=0, atol=1e-6)
+
+
+def test_fxp_mul_kat():
+    # engine/tests/test_fxp.cpp:6-12: 2.5 * -1.5 = -3.75 in Q16.16
+    a, b = int(2.5 * 65536), int(-1.5 * 65536)
+    assert abs(O.fxp_mul(a, b) / 65536.0 - (-3.75)) < 1e-4
+    # round-half-up on the 2^-16 boundary (deltagrid_math_fxp.h:16-19)
+    assert O.fxp_mul(1, 32768) == 1 and O.fxp_mul(-1, 32768) == 0
+
+
+def test_storage_rounding_matches_numpy_and_torch():
+    torch = pytest.importorskip("torch")
+    rs = np.random.RandomState(0)
+    x = (rs.randn(20000) * np.exp(rs.uniform(-18, 11, 20000))).astype(np.float32)
+    np.testing.assert_array_equal(O.round_to(x, O.F16), x.astype(np.float16).astype(np.float32))
+    np.testing.assert_array_equal(O.round_to(x, O.BF16),
+                                  torch.from_numpy(x).to(torch.bfloat16).float().numpy())
+
+
+def _lanes(e, name, T, H, last):
+    return np.ascontiguousarray(e[name].reshape(T, H, last).transpose(1, 0, 2))
+
+
+@pytest.mark.parametrize("name", ["engine_f32_dense_dyn.npz", "engine_f32_pkm.npz"])
+def test_engine_f32_golden(name):
+    e = load_golden(name)
+    mode, H, Dh = int(e["mode"]), int(e["H"]), int(e["Dh"])
+    T, A = e["wk"].shape[0], e["wk"].shape[-1]
+    wk, wq = _lanes(e, "wk", T, H, A)[None], _lanes(e, "wq", T, H, A)[None]
+    v = _lanes(e, "v", T, H, Dh)[None]
+    beta, alpha = np.ascontiguousarray(e["beta"].T)[None], np.ascontiguousarray(e["alpha"].T)[None]
+    if mode == 2:
+        total = e["state"].shape[1]
+        out, s = O.pkm_forward(v, beta, wk, wq, _lanes(e, "idx", T, H, A)[None].astype(np.int64),
+                               alpha, np.zeros((1, H, total, Dh), np.float32), dynamic=True)
+    else:
+        out, s = O.dense_forward(v, beta, wk, wq, alpha, dynamic=True)
+    assert rel_err(out[0], _lanes(e, "y", T, H, Dh)) < FP32_TOL
+    assert rel_err(s[0], e["state"]) < FP32_TOL
+
+
+@pytest.mark.parametrize("name", ["engine_fxp_dense_dyn.npz", "engine_fxp_slotproj.npz",
+                                  "engine_fxp_pkm.npz"])
+def test_engine_fxp_golden_bit_exact(name):
+    e = load_golden(name)
+    mode, H, Dh = int(e["mode"]), int(e["H"]), int(e["Dh"])
+    T, A = e["wk"].shape[0], e["wk"].shape[-1]
+    wk, wq, v = _lanes(e, "wk", T, H, A), _lanes(e, "wq", T, H, A), _lanes(e, "v", T, H, Dh)
+    beta, alpha = e["beta"].T, e["alpha"].T
+    zero = np.zeros(e["state"].shape, np.int32)
+    if mode == 2:
+        y, s = O.fxp_pkm_forward(wk, wq, _lanes(e, "idx", T, H, A), v, beta, alpha, zero)
+    else:
+        y, s = O.fxp_dense_forward(wk, wq, v, beta, alpha, zero)
+    np.testing.assert_array_equal(y, _lanes(e, "y", T, H, Dh))
+    np.testing.assert_array_equal(s, e["state"])
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference engine library not built")
+def test_fxp_router_matches_engine():
+    H, Dh, G, K, seed = 2, 32, 16, 4, 31
+    e = O.ref_fxp_layer_run(2, H, Dh, 6, seed, G0=G, G1=G, topk=K)
+    (wk0, wk1, wq0, wq1), qs = O.ref_fxp_router_weights(H, Dh, G, G, K, False, seed)
+    for t in range(6):
+        for h in range(H):
+            k = e["k"][t, h * Dh:(h + 1) * Dh]
+            q = e["q"][t, h * Dh:(h + 1) * Dh]
+            wk, wq, idx = O.fxp_pkm_route(k, q, wk0, wk1, wq0, wq1, K, int(qs[h]))
+            np.testing.assert_array_equal(idx, e["idx"][t, h])
+            np.testing.assert_array_equal(wk, e["wk"][t, h])
+            np.testing.assert_array_equal(wq, e["wq"][t, h])
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference engine library not built")
+def test_topk_matches_engine_on_random_ties():
+    rs = np.random.RandomState(3)
+    for _ in range(50):
+        s = rs.randint(0, 6, size=40).astype(np.float32)     # many exact ties
+        a = O.topk_desc(s, 8)
+        b = O.ref_topk_desc(s, 8)
+        np.testing.assert_array_equal(a[1], b[1])
