@@ -1,0 +1,130 @@
+// capi.cu -- extern "C" entry points: argument checks, algorithm choice, launches.
+#include "dg_common.cuh"
+
+namespace dg_host {
+
+static thread_local int g_last_cuda_error = 0;
+
+int record_cuda_error(cudaError_t e) {
+    g_last_cuda_error = (int)e;
+    return DG_ERR_CUDA;
+}
+
+// kernels implemented in the other translation units
+int dense_forward_sequential(int dtype, int B, int H, int T, int S, int Dh, const void* v,
+                             const void* beta, const void* wk, const void* wq, const void* decay,
+                             int dynamic_decay, const void* s_init, void* out, void* s_final,
+                             float* err_out, float* s_final_f, cudaStream_t stream);
+int dense_forward_chunked_tc(int dtype, int B, int H, int T, int S, int Dh, const void* v,
+                             const void* beta, const void* wk, const void* wq, const void* decay,
+                             int dynamic_decay, const void* s_init, void* out, void* s_final,
+                             float* err_out, float* s_final_f, cudaStream_t stream);
+bool dense_chunked_tc_supports(int dtype, int B, int H, int T, int S, int Dh);
+int dense_step(int dtype, int B, int H, int S, int Dh, const void* v, int64_t v_sb, int64_t v_sh,
+               const void* beta, int64_t beta_sb, int64_t beta_sh, const void* wk, int64_t wk_sb,
+               int64_t wk_sh, const void* wq, int64_t wq_sb, int64_t wq_sh, const void* decay,
+               int dynamic_decay, int64_t decay_sb, int64_t decay_sh, const void* s_prev,
+               void* out, void* s_next, cudaStream_t stream);
+int pkm_forward_v1(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v,
+                   const void* beta, const void* wk, const void* wq, const int64_t* idx,
+                   const void* decay, int dynamic_decay, void* state, void* out, void* saved,
+                   int32_t* status, cudaStream_t stream);
+
+}  // namespace dg_host
+
+using namespace dg_host;
+
+static bool valid_dtype(int d) { return d >= DG_DTYPE_F32 && d <= DG_DTYPE_BF16; }
+
+extern "C" {
+
+const char* dg_status_string(int status) {
+    switch (status) {
+    case DG_OK: return "ok";
+    case DG_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case DG_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+    case DG_ERR_MISALIGNED: return "misaligned pointer";
+    case DG_ERR_WORKSPACE: return "workspace missing or too small";
+    case DG_ERR_CUDA: return "CUDA error";
+    case DG_ERR_DEVICE_CHECK: return "device-side check failed";
+    default: return "unknown status";
+    }
+}
+
+int dg_abi_version(void) { return DG_ABI_VERSION; }
+
+int dg_last_cuda_error(void) { return g_last_cuda_error; }
+
+int dg_dense_forward_ex(int dtype, int B, int H, int T, int slots, int dh, const void* v,
+                        const void* beta, const void* wk, const void* wq, const void* decay,
+                        int dynamic_decay, const void* s_init, void* out, void* s_final,
+                        float* err_out, float* s_final_f, int algo, void* stream) {
+    if (!valid_dtype(dtype) || B <= 0 || H <= 0 || T < 0 || slots <= 0 || dh <= 0)
+        return DG_ERR_INVALID_ARGUMENT;
+    if (!v || !beta || !wk || !wq || !decay || !out || !s_final) return DG_ERR_INVALID_ARGUMENT;
+    if ((int64_t)B * H > 65535) return DG_ERR_UNSUPPORTED;      // grid.y limit
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool tc_ok = dense_chunked_tc_supports(dtype, B, H, T, slots, dh);
+    if (algo == DG_DENSE_CHUNKED_TC && !tc_ok) return DG_ERR_UNSUPPORTED;
+    if (algo == DG_DENSE_CHUNKED_TC || (algo == DG_DENSE_AUTO && tc_ok))
+        return dense_forward_chunked_tc(dtype, B, H, T, slots, dh, v, beta, wk, wq, decay,
+                                        dynamic_decay, s_init, out, s_final, err_out, s_final_f, s);
+    if (algo != DG_DENSE_AUTO && algo != DG_DENSE_SEQUENTIAL) return DG_ERR_INVALID_ARGUMENT;
+    return dense_forward_sequential(dtype, B, H, T, slots, dh, v, beta, wk, wq, decay, dynamic_decay,
+                                    s_init, out, s_final, err_out, s_final_f, s);
+}
+
+int dg_dense_forward(int dtype, int B, int H, int T, int slots, int dh, const void* v,
+                     const void* beta, const void* wk, const void* wq, const void* decay,
+                     int dynamic_decay, const void* s_init, void* out, void* s_final,
+                     float* err_out, float* s_final_f, void* stream) {
+    return dg_dense_forward_ex(dtype, B, H, T, slots, dh, v, beta, wk, wq, decay, dynamic_decay,
+                               s_init, out, s_final, err_out, s_final_f, DG_DENSE_AUTO, stream);
+}
+
+int dg_dense_step(int dtype, int B, int H, int slots, int dh, const void* v, int64_t v_sb,
+                  int64_t v_sh, const void* beta, int64_t beta_sb, int64_t beta_sh, const void* wk,
+                  int64_t wk_sb, int64_t wk_sh, const void* wq, int64_t wq_sb, int64_t wq_sh,
+                  const void* decay, int dynamic_decay, int64_t decay_sb, int64_t decay_sh,
+                  const void* s_prev, void* out, void* s_next, void* stream) {
+    if (!valid_dtype(dtype) || B <= 0 || H <= 0 || slots <= 0 || dh <= 0) return DG_ERR_INVALID_ARGUMENT;
+    if (!v || !beta || !wk || !wq || !decay || !s_prev || !out || !s_next) return DG_ERR_INVALID_ARGUMENT;
+    if ((int64_t)B * H > 65535) return DG_ERR_UNSUPPORTED;
+    return dense_step(dtype, B, H, slots, dh, v, v_sb, v_sh, beta, beta_sb, beta_sh, wk, wk_sb, wk_sh,
+                      wq, wq_sb, wq_sh, decay, dynamic_decay, decay_sb, decay_sh, s_prev, out, s_next,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int dg_pkm_forward(int dtype, int B, int H, int T, int active, int64_t total_slots, int dh,
+                   const void* v, const void* beta, const void* wk, const void* wq,
+                   const int64_t* idx, const void* decay, int dynamic_decay, void* state, void* out,
+                   void* saved_s_act, int32_t* dev_status, void* stream) {
+    if (!valid_dtype(dtype) || B <= 0 || H <= 0 || T < 0 || active <= 0 || total_slots <= 0 || dh <= 0)
+        return DG_ERR_INVALID_ARGUMENT;
+    if (!v || !beta || !wk || !wq || !idx || !decay || !state || !out) return DG_ERR_INVALID_ARGUMENT;
+    if ((int64_t)B * H > 65535) return DG_ERR_UNSUPPORTED;
+    if (T == 0) return DG_OK;
+    return pkm_forward_v1(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
+                          dynamic_decay, state, out, saved_s_act, dev_status,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int dg_pkm_step(int dtype, int B, int H, int active, int64_t total_slots, int dh, const void* v,
+                const void* beta, const void* wk, const void* wq, const int64_t* idx,
+                const void* decay, int dynamic_decay, void* state, void* out, int32_t* dev_status,
+                void* stream) {
+    // a decode step is the sequence kernel with T = 1 ([B,H] decay == [B,H,1])
+    return dg_pkm_forward(dtype, B, H, 1, active, total_slots, dh, v, beta, wk, wq, idx, decay,
+                          dynamic_decay, state, out, nullptr, dev_status, stream);
+}
+
+int dg_read_device_status(int32_t* dev_status, int clear, int32_t* host_value, void* stream) {
+    if (!dev_status || !host_value) return DG_ERR_INVALID_ARGUMENT;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(host_value, dev_status, sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && clear) e = cudaMemsetAsync(dev_status, 0, sizeof(int32_t), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return e == cudaSuccess ? DG_OK : record_cuda_error(e);
+}
+
+}  // extern "C"

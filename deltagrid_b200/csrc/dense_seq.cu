@@ -1,0 +1,310 @@
+// dense_seq.cu -- dense delta-rule recurrence on CUDA cores (any dtype, slots <= 1024).
+//
+// Math (src/cpp/delta_kernel.cu:78-112, src/modules/memory.py:524-539), per
+// lane (b,h) and step t:
+//     y_t = wq_t^T S,   r_t = v_t - wk_t^T S,   S = alpha_t S + (beta_t wk_t) r_t^T
+//
+// Layout: one CTA per (lane, tile of CW columns).  Columns of S are independent
+// (column d only needs v_t[d] and the per-step scalars), so the reference puts
+// one thread on a column and loops over all slots (delta_kernel.cu:49).  Here
+// SG threads share a column, each holding SPT slots of it in registers, and
+// the two dot products are finished with an xor-butterfly over those SG lanes.
+// That shortens the dependent FMA chain per step by SG and spreads a lane over
+// ceil(Dh/CW) CTAs.  The per-step inputs (wk, wq, v, beta, alpha) for TT steps
+// are staged in shared memory as fp32 and y/r are staged for coalesced stores.
+// The state stays fp32 for all T and is cast once at the end (delta_kernel.cu:116-121).
+#include "dg_common.cuh"
+
+#include <algorithm>
+
+namespace {
+
+struct DenseSeqParams {
+    const void* v;
+    const void* beta;
+    const void* wk;
+    const void* wq;
+    const void* decay;
+    const void* s_init;
+    void* out;
+    void* s_final;
+    float* err_out;
+    float* s_final_f;
+    int B, H, T, S, Dh;
+    int dynamic_decay;
+    int TT;  // steps staged per shared-memory chunk
+};
+
+// slot m of thread group g, register j: m = 4 * (g + SG * (j / 4)) + (j % 4)
+template <int SG>
+__device__ __forceinline__ int slot_of(int g, int j) {
+    return 4 * (g + SG * (j >> 2)) + (j & 3);
+}
+
+template <typename T, int SG, int SPT, int CW>
+__global__ void __launch_bounds__(CW * SG) dense_seq_kernel(DenseSeqParams p) {
+    constexpr int NT = CW * SG;
+    constexpr int SP = SG * SPT;  // padded slot count
+    extern __shared__ __align__(16) float sm[];
+    const int TT = p.TT;
+    float* wk_s = sm;                  // [TT][SP]
+    float* wq_s = wk_s + TT * SP;      // [TT][SP]
+    float* v_s = wq_s + TT * SP;       // [TT][CW]
+    float* y_s = v_s + TT * CW;        // [TT][CW]
+    float* r_s = y_s + TT * CW;        // [TT][CW]
+    float* ab_s = r_s + TT * CW;       // [TT][2]  (alpha, beta)
+
+    const T* __restrict__ v = static_cast<const T*>(p.v);
+    const T* __restrict__ beta = static_cast<const T*>(p.beta);
+    const T* __restrict__ wk = static_cast<const T*>(p.wk);
+    const T* __restrict__ wq = static_cast<const T*>(p.wq);
+    const T* __restrict__ decay = static_cast<const T*>(p.decay);
+
+    const int tid = threadIdx.x;
+    const int g = tid % SG;
+    const int cl = tid / SG;
+    const int lane = blockIdx.y;             // b * H + h
+    const int h = lane % p.H;
+    const int c0 = blockIdx.x * CW;
+    const int c = c0 + cl;
+    const bool cvalid = c < p.Dh;
+    const int S = p.S, Dh = p.Dh, T_ = p.T;
+
+    float st[SPT];
+#pragma unroll
+    for (int j = 0; j < SPT; ++j) {
+        const int m = slot_of<SG>(g, j);
+        float x = 0.f;
+        if (p.s_init && cvalid && m < S)
+            x = dg::to_f(static_cast<const T*>(p.s_init)[((int64_t)lane * S + m) * Dh + c]);
+        st[j] = x;
+    }
+    const float alpha_static = p.dynamic_decay ? 1.f : dg::to_f(decay[h]);
+
+    for (int t0 = 0; t0 < T_; t0 += TT) {
+        const int nT = min(TT, T_ - t0);
+        __syncthreads();
+        const int64_t wbase = ((int64_t)lane * T_ + t0) * S;
+        for (int i = tid; i < TT * SP; i += NT) {
+            const int tt = i / SP, m = i - tt * SP;
+            const bool ok = tt < nT && m < S;
+            wk_s[i] = ok ? dg::to_f(wk[wbase + (int64_t)tt * S + m]) : 0.f;
+            wq_s[i] = ok ? dg::to_f(wq[wbase + (int64_t)tt * S + m]) : 0.f;
+        }
+        const int64_t vbase = ((int64_t)lane * T_ + t0) * Dh + c0;
+        for (int i = tid; i < TT * CW; i += NT) {
+            const int tt = i / CW, cc = i - tt * CW;
+            v_s[i] = (tt < nT && c0 + cc < Dh) ? dg::to_f(v[vbase + (int64_t)tt * Dh + cc]) : 0.f;
+        }
+        for (int i = tid; i < nT; i += NT) {
+            const int64_t bt = (int64_t)lane * T_ + t0 + i;
+            ab_s[2 * i] = p.dynamic_decay ? dg::to_f(decay[bt]) : alpha_static;
+            ab_s[2 * i + 1] = dg::to_f(beta[bt]);
+        }
+        __syncthreads();
+
+        for (int tt = 0; tt < nT; ++tt) {
+            const float4* wk4 = reinterpret_cast<const float4*>(wk_s + tt * SP);
+            const float4* wq4 = reinterpret_cast<const float4*>(wq_s + tt * SP);
+            float y0 = 0.f, y1 = 0.f, p0 = 0.f, p1 = 0.f;
+#pragma unroll
+            for (int j4 = 0; j4 < SPT / 4; ++j4) {
+                const float4 a = wq4[g + SG * j4];
+                const float4 b = wk4[g + SG * j4];
+                y0 = fmaf(a.x, st[4 * j4 + 0], y0);
+                p0 = fmaf(b.x, st[4 * j4 + 0], p0);
+                y1 = fmaf(a.y, st[4 * j4 + 1], y1);
+                p1 = fmaf(b.y, st[4 * j4 + 1], p1);
+                y0 = fmaf(a.z, st[4 * j4 + 2], y0);
+                p0 = fmaf(b.z, st[4 * j4 + 2], p0);
+                y1 = fmaf(a.w, st[4 * j4 + 3], y1);
+                p1 = fmaf(b.w, st[4 * j4 + 3], p1);
+            }
+            float y = y0 + y1, pr = p0 + p1;
+#pragma unroll
+            for (int o = 1; o < SG; o <<= 1) {
+                y += __shfl_xor_sync(DG_FULL_MASK, y, o);
+                pr += __shfl_xor_sync(DG_FULL_MASK, pr, o);
+            }
+            const float r = v_s[tt * CW + cl] - pr;
+            if (g == 0) {
+                y_s[tt * CW + cl] = y;
+                r_s[tt * CW + cl] = r;
+            }
+            const float al = ab_s[2 * tt], bt = ab_s[2 * tt + 1];
+#pragma unroll
+            for (int j4 = 0; j4 < SPT / 4; ++j4) {
+                const float4 b = wk4[g + SG * j4];
+                st[4 * j4 + 0] = fmaf(al, st[4 * j4 + 0], (bt * b.x) * r);
+                st[4 * j4 + 1] = fmaf(al, st[4 * j4 + 1], (bt * b.y) * r);
+                st[4 * j4 + 2] = fmaf(al, st[4 * j4 + 2], (bt * b.z) * r);
+                st[4 * j4 + 3] = fmaf(al, st[4 * j4 + 3], (bt * b.w) * r);
+            }
+        }
+        __syncthreads();
+        T* __restrict__ out = static_cast<T*>(p.out);
+        for (int i = tid; i < nT * CW; i += NT) {
+            const int tt = i / CW, cc = i - tt * CW;
+            if (c0 + cc < Dh) {
+                const int64_t o = vbase + (int64_t)tt * Dh + cc;
+                out[o] = dg::from_f<T>(y_s[i]);
+                if (p.err_out) p.err_out[o] = r_s[i];
+            }
+        }
+    }
+
+    T* __restrict__ s_final = static_cast<T*>(p.s_final);
+#pragma unroll
+    for (int j = 0; j < SPT; ++j) {
+        const int m = slot_of<SG>(g, j);
+        if (cvalid && m < S) {
+            const int64_t o = ((int64_t)lane * S + m) * Dh + c;
+            s_final[o] = dg::from_f<T>(st[j]);
+            if (p.s_final_f) p.s_final_f[o] = st[j];
+        }
+    }
+}
+
+template <typename T, int SG, int SPT, int CW>
+int launch_seq(DenseSeqParams p, cudaStream_t stream) {
+    constexpr int SP = SG * SPT;
+    constexpr size_t kSmemBudget = 96 * 1024;
+    const size_t per_step = (2 * SP + 3 * CW + 2) * sizeof(float);
+    int TT = (int)std::min<size_t>(64, kSmemBudget / per_step);
+    TT = std::max(1, std::min(TT, p.T));
+    p.TT = TT;
+    const size_t smem = per_step * TT;
+    auto kern = dense_seq_kernel<T, SG, SPT, CW>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return dg_host::record_cuda_error(e);
+    }
+    dim3 grid((p.Dh + CW - 1) / CW, p.B * p.H);
+    kern<<<grid, CW * SG, smem, stream>>>(p);
+    return dg_host::check_launch();
+}
+
+template <typename T>
+int dispatch_seq(const DenseSeqParams& p, cudaStream_t s) {
+    if (p.S <= 8) return launch_seq<T, 2, 4, 64>(p, s);
+    if (p.S <= 16) return launch_seq<T, 4, 4, 32>(p, s);
+    if (p.S <= 32) return launch_seq<T, 4, 8, 32>(p, s);
+    if (p.S <= 64) return launch_seq<T, 8, 8, 16>(p, s);
+    if (p.S <= 128) return launch_seq<T, 8, 16, 16>(p, s);
+    if (p.S <= 256) return launch_seq<T, 16, 16, 16>(p, s);
+    if (p.S <= 512) return launch_seq<T, 16, 32, 16>(p, s);
+    if (p.S <= 1024) return launch_seq<T, 32, 32, 8>(p, s);
+    return DG_ERR_UNSUPPORTED;
+}
+
+// ---------------------------------------------------------------------------
+// single decode step (delta_kernel.cu:223-351): reads S once, writes S_next.
+// Thread (c, g): column c = tid % CW (coalesced rows), slot group g = tid / CW
+// holding slots m = g + NG*i.  Partial dot products are reduced across slot
+// groups through shared memory; s_next may alias s_prev (each element is read
+// and then written by the same thread only).
+// ---------------------------------------------------------------------------
+struct DenseStepParams {
+    const void* v; int64_t v_sb, v_sh;
+    const void* beta; int64_t beta_sb, beta_sh;
+    const void* wk; int64_t wk_sb, wk_sh;
+    const void* wq; int64_t wq_sb, wq_sh;
+    const void* decay; int dynamic_decay; int64_t decay_sb, decay_sh;
+    const void* s_prev; void* out; void* s_next;
+    int B, H, S, Dh;
+};
+
+template <typename T, int CW, int NG, int MAXPER>
+__global__ void __launch_bounds__(CW * NG) dense_step_kernel(DenseStepParams p) {
+    __shared__ float red[2][NG][CW];
+    __shared__ float rr[CW];
+    const int tid = threadIdx.x;
+    const int cl = tid % CW, g = tid / CW;
+    const int lane = blockIdx.y;
+    const int b = lane / p.H, h = lane % p.H;
+    const int c = blockIdx.x * CW + cl;
+    const bool cvalid = c < p.Dh;
+    const int S = p.S, Dh = p.Dh;
+    const T* wk = static_cast<const T*>(p.wk) + b * p.wk_sb + h * p.wk_sh;
+    const T* wq = static_cast<const T*>(p.wq) + b * p.wq_sb + h * p.wq_sh;
+    const T* sp = static_cast<const T*>(p.s_prev) + (int64_t)lane * S * Dh;
+    T* sn = static_cast<T*>(p.s_next) + (int64_t)lane * S * Dh;
+
+    float sv[MAXPER];
+    float y = 0.f, pr = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXPER; ++i) {
+        const int m = g + NG * i;
+        float x = 0.f;
+        if (m < S && cvalid) x = dg::to_f(sp[(int64_t)m * Dh + c]);
+        sv[i] = x;
+        if (m < S) {
+            y = fmaf(dg::to_f(wq[m]), x, y);
+            pr = fmaf(dg::to_f(wk[m]), x, pr);
+        }
+    }
+    red[0][g][cl] = y;
+    red[1][g][cl] = pr;
+    __syncthreads();
+    if (g == 0) {
+        float ys = 0.f, ps = 0.f;
+#pragma unroll
+        for (int k = 0; k < NG; ++k) { ys += red[0][k][cl]; ps += red[1][k][cl]; }
+        if (cvalid) {
+            const T* v = static_cast<const T*>(p.v) + b * p.v_sb + h * p.v_sh;
+            static_cast<T*>(p.out)[(int64_t)lane * Dh + c] = dg::from_f<T>(ys);
+            rr[cl] = dg::to_f(v[c]) - ps;
+        } else {
+            rr[cl] = 0.f;
+        }
+    }
+    __syncthreads();
+    const T* decay = static_cast<const T*>(p.decay);
+    const float al = p.dynamic_decay ? dg::to_f(decay[b * p.decay_sb + h * p.decay_sh]) : dg::to_f(decay[h]);
+    const float bt = dg::to_f(static_cast<const T*>(p.beta)[b * p.beta_sb + h * p.beta_sh]);
+    const float r = rr[cl];
+#pragma unroll
+    for (int i = 0; i < MAXPER; ++i) {
+        const int m = g + NG * i;
+        if (m < S && cvalid) sn[(int64_t)m * Dh + c] = dg::from_f<T>(fmaf(al, sv[i], (bt * dg::to_f(wk[m])) * r));
+    }
+}
+
+template <typename T>
+int dispatch_step(const DenseStepParams& p, cudaStream_t s) {
+    constexpr int CW = 32, NG = 8;
+    dim3 grid((p.Dh + CW - 1) / CW, p.B * p.H);
+    if (p.S <= NG * 4) dense_step_kernel<T, CW, NG, 4><<<grid, CW * NG, 0, s>>>(p);
+    else if (p.S <= NG * 16) dense_step_kernel<T, CW, NG, 16><<<grid, CW * NG, 0, s>>>(p);
+    else if (p.S <= NG * 64) dense_step_kernel<T, CW, NG, 64><<<grid, CW * NG, 0, s>>>(p);
+    else if (p.S <= NG * 128) dense_step_kernel<T, CW, NG, 128><<<grid, CW * NG, 0, s>>>(p);
+    else return DG_ERR_UNSUPPORTED;
+    return dg_host::check_launch();
+}
+
+}  // namespace
+
+namespace dg_host {
+
+int dense_forward_sequential(int dtype, int B, int H, int T, int S, int Dh, const void* v,
+                             const void* beta, const void* wk, const void* wq, const void* decay,
+                             int dynamic_decay, const void* s_init, void* out, void* s_final,
+                             float* err_out, float* s_final_f, cudaStream_t stream) {
+    DenseSeqParams p{v, beta, wk, wq, decay, s_init, out, s_final, err_out, s_final_f,
+                     B, H, T, S, Dh, dynamic_decay, 1};
+    DG_DISPATCH(dtype, Ty, return dispatch_seq<Ty>(p, stream));
+    return DG_ERR_INVALID_ARGUMENT;
+}
+
+int dense_step(int dtype, int B, int H, int S, int Dh, const void* v, int64_t v_sb, int64_t v_sh,
+               const void* beta, int64_t beta_sb, int64_t beta_sh, const void* wk, int64_t wk_sb,
+               int64_t wk_sh, const void* wq, int64_t wq_sb, int64_t wq_sh, const void* decay,
+               int dynamic_decay, int64_t decay_sb, int64_t decay_sh, const void* s_prev,
+               void* out, void* s_next, cudaStream_t stream) {
+    DenseStepParams p{v, v_sb, v_sh, beta, beta_sb, beta_sh, wk, wk_sb, wk_sh, wq, wq_sb, wq_sh,
+                      decay, dynamic_decay, decay_sb, decay_sh, s_prev, out, s_next, B, H, S, Dh};
+    DG_DISPATCH(dtype, Ty, return dispatch_step<Ty>(p, stream));
+    return DG_ERR_INVALID_ARGUMENT;
+}
+
+}  // namespace dg_host

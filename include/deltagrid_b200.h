@@ -1,0 +1,147 @@
+/*
+ * deltagrid_b200.h -- C ABI of the B200 (sm_100a) DeltaGrid recurrence kernels.
+ *
+ * Plain C: raw device pointers, element counts and dtype codes; no torch or
+ * CUDA types.  `stream` is a cudaStream_t passed as void* (NULL = the legacy
+ * default stream).  Every entry point is asynchronous on `stream`, validates
+ * its arguments on the host, and returns DG_OK (0) or a negative dg_status.
+ * Outputs are caller-owned.  No entry point keeps state between calls except
+ * the per-device setup noted where it applies; calls on different streams are
+ * independent.
+ *
+ * Tensor layouts are the reference's (src/cpp/delta_kernel.h): dense, row
+ * major, batch-major [B, H, ...] unless strides are taken explicitly.
+ * Reference paths below are relative to the hsameerc/deltagrid project root.
+ */
+#ifndef DELTAGRID_B200_H
+#define DELTAGRID_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DG_ABI_VERSION 1
+
+/* storage dtypes; the reference dispatches float, double, Half, BFloat16
+   (src/cpp/binding.cpp:90-92).  Arithmetic is fp32 in every case, as there. */
+typedef enum dg_dtype {
+    DG_DTYPE_F32 = 0,
+    DG_DTYPE_F64 = 1,
+    DG_DTYPE_F16 = 2,
+    DG_DTYPE_BF16 = 3
+} dg_dtype;
+
+typedef enum dg_status {
+    DG_OK = 0,
+    DG_ERR_INVALID_ARGUMENT = -1, /* null pointer, non-positive size, unknown dtype */
+    DG_ERR_UNSUPPORTED = -2,      /* shape/dtype combination no kernel covers */
+    DG_ERR_MISALIGNED = -3,       /* a pointer lacks the alignment the kernel needs */
+    DG_ERR_WORKSPACE = -4,        /* workspace missing or smaller than *_workspace_size */
+    DG_ERR_CUDA = -5,             /* CUDA launch/runtime error (dg_last_cuda_error) */
+    DG_ERR_DEVICE_CHECK = -6      /* a kernel's own check tripped (dg_read_device_status) */
+} dg_status;
+
+/* dense-forward algorithm selector for dg_dense_forward_ex */
+typedef enum dg_dense_algo {
+    DG_DENSE_AUTO = 0,       /* chunkwise tensor-core kernel where it applies, else sequential */
+    DG_DENSE_SEQUENTIAL = 1, /* CUDA-core recurrence, S resident for all T (any dtype) */
+    DG_DENSE_CHUNKED_TC = 2  /* chunkwise WY/UT form on tcgen05 (f16/bf16, Dh = 64) */
+} dg_dense_algo;
+
+/* bits written into the optional device status word by kernel self-checks */
+#define DG_DEVCHK_INDEX_RANGE 0x1 /* a slot index was outside [0, total_slots) */
+#define DG_DEVCHK_DUPLICATE 0x2   /* reserved */
+
+const char* dg_status_string(int status);
+int dg_abi_version(void);
+/* cudaError_t value of the most recent DG_ERR_CUDA on this host thread */
+int dg_last_cuda_error(void);
+
+/*
+ * Dense sequence forward.
+ * Replaces launch_delta_grid_forward (src/cpp/delta_kernel.cu:563-622) and the
+ * kernels it launches (:34-122, :127-218); same semantics as
+ * delta_grid_forward_binding (src/cpp/binding.cpp:36-113).
+ *   v [B,H,T,Dh]  beta [B,H,T]  wk,wq [B,H,T,slots]
+ *   decay [H] (dynamic_decay = 0) or [B,H,T] (dynamic_decay = 1)
+ *   s_init [B,H,slots,Dh] or NULL (zero state)
+ *   out [B,H,T,Dh]  s_final [B,H,slots,Dh]      (storage dtype)
+ *   err_out [B,H,T,Dh] fp32 residuals r_t, or NULL
+ *   s_final_f [B,H,slots,Dh] fp32 final state, or NULL
+ * The state stays fp32 for all T and is cast once at the end (delta_kernel.cu:64-121).
+ */
+int dg_dense_forward(int dtype, int B, int H, int T, int slots, int dh,
+                     const void* v, const void* beta, const void* wk, const void* wq,
+                     const void* decay, int dynamic_decay, const void* s_init,
+                     void* out, void* s_final, float* err_out, float* s_final_f,
+                     void* stream);
+
+/* dg_dense_forward with an explicit algorithm (dg_dense_algo). */
+int dg_dense_forward_ex(int dtype, int B, int H, int T, int slots, int dh,
+                        const void* v, const void* beta, const void* wk, const void* wq,
+                        const void* decay, int dynamic_decay, const void* s_init,
+                        void* out, void* s_final, float* err_out, float* s_final_f,
+                        int algo, void* stream);
+
+/*
+ * Dense single decode step with (batch, head) element strides.
+ * Replaces launch_delta_grid_step (src/cpp/delta_kernel.cu:624-695) and the
+ * kernels :223-351; same semantics as delta_grid_step_binding (binding.cpp:130-203).
+ *   v [B,H,Dh] (strides v_sb, v_sh; last dim contiguous)  beta [B,H]
+ *   wk,wq [B,H,slots] (last dim contiguous)
+ *   decay [H] contiguous, or [B,H] with strides (dynamic_decay = 1)
+ *   s_prev, s_next [B,H,slots,Dh] contiguous; s_next may equal s_prev (in place)
+ *   out [B,H,Dh] contiguous
+ */
+int dg_dense_step(int dtype, int B, int H, int slots, int dh,
+                  const void* v, int64_t v_sb, int64_t v_sh,
+                  const void* beta, int64_t beta_sb, int64_t beta_sh,
+                  const void* wk, int64_t wk_sb, int64_t wk_sh,
+                  const void* wq, int64_t wq_sb, int64_t wq_sh,
+                  const void* decay, int dynamic_decay, int64_t decay_sb, int64_t decay_sh,
+                  const void* s_prev, void* out, void* s_next, void* stream);
+
+/*
+ * Sparse Delta-PKM sequence forward, state updated in place.
+ * Replaces launch_delta_grid_pkm_forward (src/cpp/delta_kernel.cu:923-944) and
+ * delta_pkm_sequence_forward_kernel (:862-921); same semantics as
+ * delta_pkm_forward_binding (binding.cpp:375-434).
+ *   v [B,H,T,Dh] beta [B,H,T] wk,wq [B,H,T,active] idx [B,H,T,active] (int64)
+ *   decay [H] or [B,H,T];  state [B,H,total_slots,Dh] (in place)
+ *   out [B,H,T,Dh];  saved_s_act [B,H,T,active,Dh] gathered rows, or NULL
+ *   dev_status: optional device int32; kernels OR DG_DEVCHK_* bits into it.
+ * Touched rows are stored (rounded to the storage dtype) after every step,
+ * as in the reference (delta_kernel.cu:918).  Slot indices outside
+ * [0, total_slots) are skipped (the row reads as zero and is not written) and
+ * flagged in dev_status.  Indices repeated within one step are not supported,
+ * as in the reference.
+ */
+int dg_pkm_forward(int dtype, int B, int H, int T, int active, int64_t total_slots, int dh,
+                   const void* v, const void* beta, const void* wk, const void* wq,
+                   const int64_t* idx, const void* decay, int dynamic_decay,
+                   void* state, void* out, void* saved_s_act, int32_t* dev_status,
+                   void* stream);
+
+/*
+ * Sparse Delta-PKM single decode step, state updated in place.
+ * Replaces launch_delta_grid_pkm_step (src/cpp/delta_kernel.cu:829-847) and
+ * delta_pkm_step_kernel (:776-827); same call as delta_grid_pkm_step_binding
+ * (binding.cpp:319-370).  decay is [H], or [B,H] when dynamic_decay = 1; the
+ * reference kernel reads decay[h] even for a [B,H] tensor (:795), this entry
+ * point uses the per-batch value as the PyTorch path does (memory.py:582-591).
+ */
+int dg_pkm_step(int dtype, int B, int H, int active, int64_t total_slots, int dh,
+                const void* v, const void* beta, const void* wk, const void* wq,
+                const int64_t* idx, const void* decay, int dynamic_decay,
+                void* state, void* out, int32_t* dev_status, void* stream);
+
+/* Reads (and clears when `clear`) a device status word; synchronizes `stream`. */
+int dg_read_device_status(int32_t* dev_status, int clear, int32_t* host_value, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DELTAGRID_B200_H */
