@@ -61,9 +61,13 @@ int dg_dense_forward_ex(int dtype, int B, int H, int T, int slots, int dh, const
                         float* err_out, float* s_final_f, int algo, void* stream) {
     if (!valid_dtype(dtype) || B <= 0 || H <= 0 || T < 0 || slots <= 0 || dh <= 0)
         return DG_ERR_INVALID_ARGUMENT;
-    if (!v || !beta || !wk || !wq || !decay || !out || !s_final) return DG_ERR_INVALID_ARGUMENT;
+    // with T == 0 the per-step tensors are empty (their pointers may be null):
+    // only the state passes through, s_final = s_init (or zeros)
+    if (!decay || !s_final || (T > 0 && (!v || !beta || !wk || !wq || !out)))
+        return DG_ERR_INVALID_ARGUMENT;
     if ((int64_t)B * H > 65535) return DG_ERR_UNSUPPORTED;      // grid.y limit
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (T == 0) algo = DG_DENSE_SEQUENTIAL;
     const bool tc_ok = dense_chunked_tc_supports(dtype, B, H, T, slots, dh);
     if (algo == DG_DENSE_CHUNKED_TC && !tc_ok) return DG_ERR_UNSUPPORTED;
     if (algo == DG_DENSE_CHUNKED_TC || (algo == DG_DENSE_AUTO && tc_ok))
@@ -101,9 +105,10 @@ int dg_pkm_forward(int dtype, int B, int H, int T, int active, int64_t total_slo
                    void* saved_s_act, int32_t* dev_status, void* stream) {
     if (!valid_dtype(dtype) || B <= 0 || H <= 0 || T < 0 || active <= 0 || total_slots <= 0 || dh <= 0)
         return DG_ERR_INVALID_ARGUMENT;
-    if (!v || !beta || !wk || !wq || !idx || !decay || !state || !out) return DG_ERR_INVALID_ARGUMENT;
+    if (!state) return DG_ERR_INVALID_ARGUMENT;
+    if (T == 0) return DG_OK;              // nothing to do; per-step tensors may be empty
+    if (!v || !beta || !wk || !wq || !idx || !decay || !out) return DG_ERR_INVALID_ARGUMENT;
     if ((int64_t)B * H > 65535) return DG_ERR_UNSUPPORTED;
-    if (T == 0) return DG_OK;
     return pkm_forward_v1(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
                           dynamic_decay, state, out, saved_s_act, dev_status,
                           static_cast<cudaStream_t>(stream));
