@@ -54,6 +54,7 @@ typedef enum dg_dense_algo {
 /* bits written into the optional device status word by kernel self-checks */
 #define DG_DEVCHK_INDEX_RANGE 0x1 /* a slot index was outside [0, total_slots) */
 #define DG_DEVCHK_DUPLICATE 0x2   /* reserved */
+#define DG_DEVCHK_TIMEOUT 0x4     /* a bounded wait on an mbarrier gave up (results invalid) */
 
 const char* dg_status_string(int status);
 int dg_abi_version(void);

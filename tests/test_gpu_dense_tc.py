@@ -1,0 +1,87 @@
+"""Chunkwise tensor-core dense forward (tcgen05, algo 2) against the CPU oracle.
+
+The oracle runs the per-step recurrence with an fp32 state on the fp16-quantised
+inputs (delta_kernel.cu:64-121 semantics).  The chunked kernel evaluates the
+same recurrence 64 steps at a time with fp16 MMA operands and fp32
+accumulation; bar: max|a-b|/max|b| <= 1e-3 for y and for the final state.
+"""
+import pytest
+import torch
+
+from conftest import rel_err
+from inputs import dense_inputs, to_np32
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    from deltagrid_b200 import _lib
+    from deltagrid_b200 import hsru_delta_cuda as ext
+
+TC = 2
+
+
+def _both(d, save=False):
+    g = {n: (t.cuda() if t is not None else None) for n, t in d.items()}
+    r = ext.forward(g["q"], g["k"], g["v"], g["beta"], g["wk"], g["wq"], g["decay"], g["s_init"], save, algo=TC)
+    s0 = to_np32(d["s_init"]) if d["s_init"] is not None else None
+    yo, so, eo = O.dense_forward(to_np32(d["v"]), to_np32(d["beta"]), to_np32(d["wk"]), to_np32(d["wq"]),
+                                 to_np32(d["decay"]), s0, want_err=True)
+    return r, (O.round_to(yo, O.F16), so, eo)
+
+
+@pytest.mark.parametrize("S", [128, 256, 384, 512])
+def test_tc_small(S):
+    d = dense_inputs(1, 2, 64, S, 64, torch.float16, seed=S)
+    (out, s, _, _), (yo, so, _) = _both(d)
+    assert rel_err(out.float().cpu().numpy(), yo) < 1e-3
+    assert rel_err(s.float().cpu().numpy(), O.round_to(so, O.F16)) < 1e-3
+
+
+@pytest.mark.parametrize("T", [1, 63, 65, 200, 1000])
+def test_tc_ragged_lengths(T):
+    d = dense_inputs(2, 2, T, 256, 64, torch.float16, seed=T)
+    (out, s, _, _), (yo, so, _) = _both(d)
+    assert rel_err(out.float().cpu().numpy(), yo) < 1e-3
+    assert rel_err(s.float().cpu().numpy(), O.round_to(so, O.F16)) < 1e-3
+
+
+@pytest.mark.parametrize("dyn,static_decay", [(True, 1.0), (False, 0.999)])
+def test_tc_decay_and_initial_state(dyn, static_decay):
+    d = dense_inputs(2, 3, 300, 512, 64, torch.float16, dynamic=dyn, seed=7, s_init=True,
+                     static_decay=static_decay)
+    (out, s, err, sf), (yo, so, eo) = _both(d, save=True)
+    assert rel_err(out.float().cpu().numpy(), yo) < 1e-3
+    assert rel_err(s.float().cpu().numpy(), O.round_to(so, O.F16)) < 1e-3
+    assert rel_err(sf.cpu().numpy(), so) < 1e-3
+    assert rel_err(err.cpu().numpy(), eo) < 1e-3
+
+
+def test_tc_cfg2_geometry_prefix():
+    # slots 512, Dh 64, fp16, wk = normalize(k P^T), wq = q P^T;
+    # full T = 4096 on 4 lanes so the CPU oracle stays quick
+    d = dense_inputs(1, 4, 4096, 512, 64, torch.float16, seed=11)
+    (out, s, _, _), (yo, so, _) = _both(d)
+    assert rel_err(out.float().cpu().numpy(), yo) < 1e-3
+    assert rel_err(s.float().cpu().numpy(), O.round_to(so, O.F16)) < 1e-3
+
+
+def test_tc_matches_sequential_kernel():
+    d = dense_inputs(4, 4, 512, 256, 64, torch.float16, dynamic=True, seed=3, s_init=True)
+    g = {n: (t.cuda() if t is not None else None) for n, t in d.items()}
+    a = (g["q"], g["k"], g["v"], g["beta"], g["wk"], g["wq"], g["decay"], g["s_init"])
+    o1, s1, _, _ = ext.forward(*a, algo=_lib.ALGO_SEQUENTIAL)
+    o2, s2, _, _ = ext.forward(*a, algo=TC)
+    assert rel_err(o2.float().cpu().numpy(), o1.float().cpu().numpy()) < 1e-3
+    assert rel_err(s2.float().cpu().numpy(), s1.float().cpu().numpy()) < 1e-3
+
+
+def test_auto_selects_tc_for_fp16_dh64():
+    d = dense_inputs(1, 1, 64, 512, 64, torch.float16, seed=1)
+    g = {n: (t.cuda() if t is not None else None) for n, t in d.items()}
+    a = (g["q"], g["k"], g["v"], g["beta"], g["wk"], g["wq"], g["decay"])
+    o_auto, _, _, _ = ext.forward(*a)
+    o_tc, _, _, _ = ext.forward(*a, algo=TC)
+    assert torch.equal(o_auto, o_tc)
+    with pytest.raises(RuntimeError, match="unsupported"):
+        ext.forward(*(t.float() for t in a), algo=TC)
