@@ -13,17 +13,20 @@
 // operand, T X and Mqk R as M=128 MMAs whose other 64 rows are a zero tile,
 // and the state update as S/128 M=128 MMAs accumulating into the state.
 //
-// Hardware mapping (one CTA per lane (b,h), 4 warps):
+// Hardware mapping (one CTA per lane (b,h), two warpgroups):
 //   - S (slots x 64, fp32) lives in TMEM for all T steps; it is only rounded to
 //     the storage dtype as an MMA operand copy, streamed 128 slots at a time
 //     TMEM -> registers -> fp16 shared memory.
 //   - wk / wq / v chunks arrive by TMA (3-D maps [lane][T][cols], 128B swizzle;
 //     out-of-range steps of the last chunk read as zeros, which contribute
-//     nothing: beta = 0 and alpha = 1 there).
-//   - T = (I+L)^{-1} is formed in fp32 on CUDA cores by 16x16 block
-//     forward substitution and rounded to the operand dtype.
-//   - thread 0 issues TMA and MMAs; completion is tracked with mbarriers
-//     (tcgen05.commit); every wait is bounded and turns into an error status.
+//     nothing: beta = 0 and alpha = 1 there).  Q of the next chunk is loaded as
+//     soon as [K;Q] S0 has consumed the current one; K and V of the next chunk
+//     are prefetched into L2 and loaded once the state update has read K.
+//   - warpgroup 0 runs the state path (S0 conversion, X, R, Y epilogues) and
+//     its thread 0 issues TMA and MMAs; warpgroup 1 forms L and Mqk from the
+//     Gram MMA and T = (I+L)^{-1} in fp32 (16x16 block substitution), in
+//     parallel with the state path, and hands T over through an mbarrier.
+//   - every mbarrier wait is bounded and turns into an error status.
 //   - y is written per token row; s_final (and the fp32 copy) at the end.
 //
 // Inputs: fp16 (kind::f16).  Dh = 64, slots in {128, 256, 384, 512}.
@@ -59,11 +62,9 @@ struct Layout {
     static constexpr uint32_t TZM = S0 + 2 * 16384;         // [T | Z | Mqk] 3 x 8 KB
     static constexpr uint32_t XR = TZM + 3 * 8192;          // X, then R'
     static constexpr uint32_t VR = XR + 8192;               // V, then R*beta
-    static constexpr uint32_t LT = VR + 8192;               // fp32 [64][65]
-    static constexpr uint32_t PB = LT + 64 * 65 * 4;        // fp32 3 x [16][16]
-    static constexpr uint32_t SC = PB + 3 * 1024;           // beta, aprev, aincl, aend (4 x 64 fp32)
-    static constexpr uint32_t BAR = SC + 4 * 256 + 16;      // 8 mbarriers + tmem base
-    static constexpr uint32_t BYTES = BAR + 8 * 8 + 16;
+    static constexpr uint32_t LT = VR + 8192;               // fp32 [64][68]
+    static constexpr uint32_t BAR = LT + 64 * 68 * 4;       // 12 mbarriers + tmem base
+    static constexpr uint32_t BYTES = BAR + 12 * 8 + 16;
     static constexpr uint32_t ACC1 = NB * 64;               // TMEM column bases
     static constexpr uint32_t ACC2 = ACC1 + 64;
     static constexpr uint32_t ACC3 = ACC2 + 64;
@@ -74,6 +75,8 @@ struct Layout {
 constexpr uint32_t IDESC_KK = tc::make_idesc(128, 64, 0, 0, 0);
 constexpr uint32_t IDESC_KM = tc::make_idesc(128, 64, 0, 0, 1);
 constexpr uint32_t IDESC_MM = tc::make_idesc(128, 64, 0, 1, 1);
+constexpr int LDT = 68;                 // fp32 row stride of the L/T scratch
+constexpr uint32_t BAR_WG0 = 1, BAR_WG1 = 2;   // named barrier ids (0 is __syncthreads)
 
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
@@ -109,72 +112,130 @@ __device__ __forceinline__ void ld_row64(uint32_t taddr, float* x) {
     }
 }
 
-// bounded wait by every thread, then a collective verdict; true = failed
-__device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity) {
-    const bool ok = tc::mbar_wait(bar, parity);
-    const bool failed = __syncthreads_or(!ok) != 0;
-    tc::tc_fence_after();
-    return failed;
+// Per-chunk decay/gate scalars, computed by every warp on its own: lane l holds
+// steps 2l and 2l+1.  a = inclusive product of alpha, ap = exclusive product.
+struct ChunkScalars {
+    float a0, a1;       // a_incl for steps 2l, 2l+1
+    float ap0, ap1;     // aprev for steps 2l, 2l+1
+    float b0, b1;       // beta
+    float atot;         // a_{C-1}
+};
+
+__device__ __forceinline__ ChunkScalars chunk_scalars(const __half* beta, const __half* decay, int dyn,
+                                                      float alpha_static, int64_t lane_base, int t0, int T_,
+                                                      int lane) {
+    ChunkScalars c;
+    const int t = t0 + 2 * lane;
+    const bool ok0 = t < T_, ok1 = t + 1 < T_;
+    const float al0 = ok0 ? (dyn ? __half2float(decay[lane_base + t]) : alpha_static) : 1.f;
+    const float al1 = ok1 ? (dyn ? __half2float(decay[lane_base + t + 1]) : alpha_static) : 1.f;
+    c.b0 = ok0 ? __half2float(beta[lane_base + t]) : 0.f;
+    c.b1 = ok1 ? __half2float(beta[lane_base + t + 1]) : 0.f;
+    float incl = al0 * al1;              // inclusive scan of pair products over lanes
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float v = __shfl_up_sync(DG_FULL_MASK, incl, o);
+        if (lane >= o) incl *= v;
+    }
+    float excl = __shfl_up_sync(DG_FULL_MASK, incl, 1);
+    if (lane == 0) excl = 1.f;
+    c.ap0 = excl;
+    c.a0 = excl * al0;
+    c.ap1 = c.a0;
+    c.a1 = c.a0 * al1;
+    c.atot = __shfl_sync(DG_FULL_MASK, incl, 31);
+    return c;
+}
+// value of step i from the pair registers (all lanes must call)
+__device__ __forceinline__ float pick(float v0, float v1, int i) {
+    const float a = __shfl_sync(DG_FULL_MASK, v0, i >> 1);
+    const float b = __shfl_sync(DG_FULL_MASK, v1, i >> 1);
+    return (i & 1) ? b : a;
 }
 
-// (I + L)^{-1} for strictly lower L (64x64 fp32 at lt, row stride 65), by 16x16
-// blocks: diagonal blocks by forward substitution, off-diagonal blocks by
-//   T_ik = -D_i sum_{j=k}^{i-1} L_ij T_jk   (processed along diagonals i-k = 1, 2, 3).
-// Diagonal inverses overwrite L_ii; T_ik (i > k) is stored in the unused upper block (k, i).
-__device__ void invert_unit_lower(float* lt, float* pb, int tid) {
-    constexpr int LD = 65;
-    auto L = [&](int bi, int bk, int a, int b) -> float& { return lt[(16 * bi + a) * LD + 16 * bk + b]; };
-    auto Tm = [&](int bi, int bk, int a, int b) -> float& {
-        return (bi == bk) ? lt[(16 * bi + a) * LD + 16 * bi + b] : lt[(16 * bk + a) * LD + 16 * bi + b];
-    };
-    // diagonal blocks: thread (blk, col) solves column col of (I + L_bb) x = e_col
-    float x[16];
-    if (tid < 64) {
-        const int blk = tid >> 4, col = tid & 15;
+// (I + L)^{-1} for strictly lower L (64x64 fp32, row stride LDT) in place,
+// by one warpgroup (t = 0..127).  With 16x16 blocks:
+//   D_b = (I + L_bb)^{-1}                 (forward substitution, one warp per block)
+//   E_ij = -D_i L_ij   (i > j)            (all six blocks at once)
+//   T_ik = sum_{j=k}^{i-1} E_ij T_jk      (block rows 1, 2, 3 in order; T_kk = D_k)
+// Results overwrite L block by block; every block is computed into registers
+// and written after a barrier, so reads always see the previous stage.
+__device__ void invert_unit_lower(float* lt, int t) {
+    const int warp = t >> 5, lane = t & 31;
+    auto at = [&](int r, int c) -> float& { return lt[r * LDT + c]; };
+    {   // diagonal blocks
+        const int b = warp, col = lane & 15;
+        float x[16];
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
             float s = (r == col) ? 1.f : 0.f;
 #pragma unroll
-            for (int j = 0; j < r; ++j) s -= L(blk, blk, r, j) * x[j];
+            for (int j = 0; j < r; ++j) s = fmaf(-at(16 * b + r, 16 * b + j), x[j], s);
             x[r] = s;
         }
-    }
-    __syncthreads();
-    if (tid < 64) {
-        const int blk = tid >> 4, col = tid & 15;
+        tc::group_sync(BAR_WG1);
+        if (lane < 16) {
 #pragma unroll
-        for (int r = 0; r < 16; ++r) L(blk, blk, r, col) = x[r];
-    }
-    __syncthreads();
-    // diagonals d = 1..3; targets (i, k = i - d)
-    for (int d = 1; d <= 3; ++d) {
-        const int ntarget = 4 - d;
-        // P_t = sum_{j=k}^{i-1} L_ij T_jk
-        for (int e = tid; e < ntarget * 256; e += 128) {
-            const int t = e >> 8, a = (e >> 4) & 15, b = e & 15;
-            const int i = t + d, k = t;
-            float s = 0.f;
-            for (int j = k; j < i; ++j)
-#pragma unroll
-                for (int m = 0; m < 16; ++m) s += L(i, j, a, m) * Tm(j, k, m, b);
-            pb[t * 256 + a * 16 + b] = s;
+            for (int r = 0; r < 16; ++r) at(16 * b + r, 16 * b + col) = x[r];
         }
-        __syncthreads();
-        // T_ik = -D_i P_t
-        for (int e = tid; e < ntarget * 256; e += 128) {
-            const int t = e >> 8, a = (e >> 4) & 15, b = e & 15;
-            const int i = t + d, k = t;
+        tc::group_sync(BAR_WG1);
+    }
+    {   // E_ij = -D_i L_ij for (1,0) (2,0) (2,1) (3,0) (3,1) (3,2)
+        // block pairs in order (1,0) (2,0) (2,1) (3,0) (3,1) (3,2)
+        auto bi_of = [](int k) { return k == 0 ? 1 : (k < 3 ? 2 : 3); };
+        auto bj_of = [](int k) { return k == 0 ? 0 : (k == 1 ? 0 : (k == 2 ? 1 : (k == 3 ? 0 : (k == 4 ? 1 : 2)))); };
+        float e[12];
+#pragma unroll
+        for (int m = 0; m < 12; ++m) {
+            const int o = t + 128 * m;
+            const int blk = o >> 8, a = (o >> 4) & 15, c = o & 15;
+            const int bi = bi_of(blk), bj = bj_of(blk);
             float s = 0.f;
 #pragma unroll
-            for (int m = 0; m < 16; ++m) s += Tm(i, i, a, m) * pb[t * 256 + m * 16 + b];
-            Tm(i, k, a, b) = -s;
+            for (int q = 0; q < 16; ++q) s = fmaf(at(16 * bi + a, 16 * bi + q), at(16 * bi + q, 16 * bj + c), s);
+            e[m] = -s;
         }
-        __syncthreads();
+        tc::group_sync(BAR_WG1);
+#pragma unroll
+        for (int m = 0; m < 12; ++m) {
+            const int o = t + 128 * m;
+            const int blk = o >> 8, a = (o >> 4) & 15, c = o & 15;
+            at(16 * bi_of(blk) + a, 16 * bj_of(blk) + c) = e[m];
+        }
+        tc::group_sync(BAR_WG1);
+    }
+    // block rows: T_ik = sum_{j=k}^{i-1} E_ij T_jk, with T_kk = D_k in the diagonal block
+#pragma unroll
+    for (int bi = 1; bi < 4; ++bi) {
+        float r[6];
+#pragma unroll
+        for (int m = 0; m < 6; ++m) {
+            if (m < 2 * bi) {
+                const int o = t + 128 * m;
+                const int bk = o >> 8, a = (o >> 4) & 15, c = o & 15;
+                float s = 0.f;
+                for (int bj = bk; bj < bi; ++bj)
+#pragma unroll
+                    for (int q = 0; q < 16; ++q)
+                        s = fmaf(at(16 * bi + a, 16 * bj + q), at(16 * bj + q, 16 * bk + c), s);
+                r[m] = s;
+            }
+        }
+        tc::group_sync(BAR_WG1);
+#pragma unroll
+        for (int m = 0; m < 6; ++m) {
+            if (m < 2 * bi) {
+                const int o = t + 128 * m;
+                const int bk = o >> 8, a = (o >> 4) & 15, c = o & 15;
+                at(16 * bi + a, 16 * bk + c) = r[m];
+            }
+        }
+        tc::group_sync(BAR_WG1);
     }
 }
 
 template <int S>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(256, 1)
     dense_chunk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmq,
                        const __grid_constant__ CUtensorMap tmv, ChunkParams p) {
     using Ly = Layout<S>;
@@ -187,323 +248,329 @@ __global__ void __launch_bounds__(128, 1)
     uint8_t* xr = sm + Ly::XR;
     uint8_t* vr = sm + Ly::VR;
     float* lt = reinterpret_cast<float*>(sm + Ly::LT);
-    float* pb = reinterpret_cast<float*>(sm + Ly::PB);
-    float* s_beta = reinterpret_cast<float*>(sm + Ly::SC);
-    float* s_aprev = s_beta + 64;
-    float* s_aincl = s_aprev + 64;
-    float* s_aend = s_aincl + 64;
-    float* s_atot = s_aend + 64;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ly::BAR);
-    uint64_t* bar_load = bars + 0;
-    uint64_t* bar_acc1 = bars + 1;
-    uint64_t* bar_acc2 = bars + 2;
-    uint64_t* bar_acc3 = bars + 3;
-    uint64_t* bar_acc4 = bars + 4;
-    uint64_t* bar_upd = bars + 5;
-    uint64_t* bar_s0 = bars + 6;     // two buffers
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 8);
+    uint64_t* bar_kv = bars + 0;     // TMA: K slices + V of a chunk
+    uint64_t* bar_q = bars + 1;      // TMA: Q slices of a chunk
+    uint64_t* bar_acc1 = bars + 2;
+    uint64_t* bar_acc2 = bars + 3;
+    uint64_t* bar_acc3 = bars + 4;
+    uint64_t* bar_acc4 = bars + 5;
+    uint64_t* bar_upd = bars + 6;
+    uint64_t* bar_t = bars + 7;      // WG1 -> MMA issuer: T and Mqk tiles of the chunk written
+    uint64_t* bar_s0 = bars + 8;     // two S0 buffers
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int q4 = warp & 3;                       // TMEM lane quarter of this warp
     const int lane_bh = blockIdx.x;
     const int h = lane_bh % p.H;
-    const int T_ = p.T;
+    const int T_ = p.T, NC = p.nchunks;
+    const int64_t lane_base = (int64_t)lane_bh * T_;
     const __half* beta = static_cast<const __half*>(p.beta);
     const __half* decay = static_cast<const __half*>(p.decay);
 
     if (warp == 0) tc::tmem_alloc(tmem_holder, Ly::TMEM_COLS);
     if (tid == 0) {
-        for (int i = 0; i < 8; ++i) tc::mbar_init(bars + i, 1);
+        for (int i = 0; i < 10; ++i) tc::mbar_init(bars + i, 1);
         tc::fence_barrier_init();
         tc::prefetch_tmap(&tmk);
         tc::prefetch_tmap(&tmq);
         tc::prefetch_tmap(&tmv);
     }
-    // zero tile Z (rows 64..127 of [T;Z] and rows 0..63 of [Z;Mqk])
-    for (int i = tid; i < 8192 / 16; i += 128) reinterpret_cast<uint4*>(tzm + 8192)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < 8192 / 16; i += 256) reinterpret_cast<uint4*>(tzm + 8192)[i] = make_uint4(0, 0, 0, 0);
     tc::fence_proxy_async();
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_holder;
-    const uint32_t tq = tmem + ((uint32_t)(32 * warp) << 16);   // this warp's TMEM lane quarter
+    const uint32_t tq = tmem + ((uint32_t)(32 * q4) << 16);
     const float alpha_static = p.dynamic_decay ? 1.f : __half2float(decay[h]);
 
-    // initial state -> TMEM (thread = slot row 128 b + 32 warp + lane)
-    {
-        const __half* s_init = static_cast<const __half*>(p.s_init);
-        for (int b = 0; b < NB; ++b) {
-            const int slot = 128 * b + 32 * warp + lane;
-            uint32_t r0[32], r1[32];
-            if (s_init) {
-                const uint4* src = reinterpret_cast<const uint4*>(s_init + ((int64_t)lane_bh * S + slot) * DH);
+    bool failed = false;
+    if (warp < 4) {
+        // ================= WG0: state path; thread 0 issues TMA and MMAs =================
+        {   // initial state -> TMEM (thread = slot row 128 b + 32 warp + lane)
+            const __half* s_init = static_cast<const __half*>(p.s_init);
+            for (int b = 0; b < NB; ++b) {
+                const int slot = 128 * b + 32 * warp + lane;
+                uint32_t r0[32], r1[32];
+                if (s_init) {
+                    const uint4* src = reinterpret_cast<const uint4*>(s_init + ((int64_t)lane_bh * S + slot) * DH);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint4 v = src[c];
+                    for (int c = 0; c < 8; ++c) {
+                        const uint4 v = src[c];
+                        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 f = unpack_h2(w4[e]);
+                            const int col = 8 * c + 2 * e;
+                            uint32_t* dst = col < 32 ? r0 : r1;
+                            dst[col & 31] = __float_as_uint(f.x);
+                            dst[(col & 31) + 1] = __float_as_uint(f.y);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) { r0[i] = 0u; r1[i] = 0u; }
+                }
+                tc::tmem_st32(tq + 64 * b, r0);
+                tc::tmem_st32(tq + 64 * b + 32, r1);
+            }
+            tc::tmem_wait_st();
+            tc::tc_fence_before();
+        }
+        if (tid == 0 && NC > 0) {
+            tc::mbar_expect_tx(bar_kv, NSL * 8192 + 8192);
+            for (int s = 0; s < NSL; ++s) tc::tma_load_3d(kq + s * SLICE, &tmk, bar_kv, 64 * s, 0, lane_bh);
+            tc::tma_load_3d(vr, &tmv, bar_kv, 0, 0, lane_bh);
+            tc::mbar_expect_tx(bar_q, NSL * 8192);
+            for (int s = 0; s < NSL; ++s) tc::tma_load_3d(kq + s * SLICE + 8192, &tmq, bar_q, 64 * s, 0, lane_bh);
+        }
+        tc::group_sync(BAR_WG0);
+        uint32_t s0_uses[2] = {0u, 0u};
+        const int row = 32 * (warp & 1) + lane;        // token row handled in the epilogues
+        for (int c = 0; c < NC && !failed; ++c) {
+            const int t0 = c * CH;
+            const uint32_t par = (uint32_t)(c & 1);
+            const ChunkScalars cs = chunk_scalars(beta, decay, p.dynamic_decay, alpha_static, lane_base, t0, T_, lane);
+            const float ap_row = pick(cs.ap0, cs.ap1, row);
+            const float b_row = pick(cs.b0, cs.b1, row);
+            const float ae_row = cs.atot / pick(cs.a0, cs.a1, row);
+            // K, V and Q of this chunk in shared memory; previous update done
+            bool bad = !tc::mbar_wait(bar_kv, par) || !tc::mbar_wait(bar_q, par);
+            if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
+            tc::tc_fence_after();
+            if (tid == 0) {
+                for (int s = 0; s < NSL; ++s)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint32_t base = tc::smem_u32(kq + s * SLICE) + 32 * kk;
+                        tc::mma_f16(tmem + Ly::ACC1, tc::make_desc(base, 16, 1024), tc::make_desc(base, 16, 1024),
+                                    IDESC_KK, (s | kk) != 0);
+                    }
+                tc::mma_commit(bar_acc1);
+                if (c + 1 < NC) {          // warm L2 with the next chunk's K and V
+                    for (int s = 0; s < NSL; ++s) tc::tma_prefetch_3d(&tmk, 64 * s, t0 + CH, lane_bh);
+                    tc::tma_prefetch_3d(&tmv, 0, t0 + CH, lane_bh);
+                }
+            }
+            // [K;Q] S0 over 128-slot blocks; S0 streamed TMEM -> fp16 smem (and scaled by atot in TMEM)
+            for (int b = 0; b < NB; ++b) {
+                const int buf = b & 1;
+                bad = false;
+                if (s0_uses[buf] > 0) bad = !tc::mbar_wait(bar_s0 + buf, (s0_uses[buf] - 1) & 1u);
+                tc::tc_fence_after();
+                float x[64];
+                ld_row64(tq + 64 * b, x);
+                st_row_f16(s0b + buf * 16384, 32 * warp + lane, x);
+                if (cs.atot != 1.f) {
+                    uint32_t r0[32], r1[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        r0[i] = __float_as_uint(cs.atot * x[i]);
+                        r1[i] = __float_as_uint(cs.atot * x[32 + i]);
+                    }
+                    tc::tmem_st32(tq + 64 * b, r0);
+                    tc::tmem_st32(tq + 64 * b + 32, r1);
+                    tc::tmem_wait_st();
+                }
+                tc::fence_proxy_async();
+                tc::tc_fence_before();
+                if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
+                if (tid == 0) {
+                    tc::tc_fence_after();
+#pragma unroll
+                    for (int sl = 0; sl < 2; ++sl)
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk) {
+                            const uint32_t a = tc::smem_u32(kq + (2 * b + sl) * SLICE) + 32 * kk;
+                            const uint32_t bb = tc::smem_u32(s0b + buf * 16384) + (sl * 4 + kk) * 2048;
+                            tc::mma_f16(tmem + Ly::ACC2, tc::make_desc(a, 16, 1024), tc::make_desc(bb, 16384, 1024),
+                                        IDESC_KM, (b | sl | kk) != 0);
+                        }
+                    tc::mma_commit(bar_s0 + buf);
+                    if (b == NB - 1) tc::mma_commit(bar_acc2);
+                }
+                s0_uses[buf]++;
+            }
+            if (failed) break;
+            // X = V - aprev o (K S0)  (warps 0-1); then the Q tiles are free for the next chunk
+            bad = !tc::mbar_wait(bar_acc2, par);
+            tc::tc_fence_after();
+            if (tid == 0 && c + 1 < NC) {
+                tc::mbar_expect_tx(bar_q, NSL * 8192);
+                for (int s = 0; s < NSL; ++s)
+                    tc::tma_load_3d(kq + s * SLICE + 8192, &tmq, bar_q, 64 * s, t0 + CH, lane_bh);
+            }
+            if (warp < 2) {
+                float d1[64];
+                ld_row64(tq + Ly::ACC2, d1);
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(vr + tc::sw128(row, cc));
                     const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const float2 f = unpack_h2(w4[e]);
-                        const int col = 8 * c + 2 * e;
-                        uint32_t* dst = col < 32 ? r0 : r1;
-                        dst[col & 31] = __float_as_uint(f.x);
-                        dst[(col & 31) + 1] = __float_as_uint(f.y);
+                        d1[8 * cc + 2 * e] = f.x - ap_row * d1[8 * cc + 2 * e];
+                        d1[8 * cc + 2 * e + 1] = f.y - ap_row * d1[8 * cc + 2 * e + 1];
                     }
                 }
-            } else {
+                st_row_f16(xr, row, d1);
+            }
+            tc::fence_proxy_async();
+            bad = bad || !tc::mbar_wait(bar_t, par);      // T and Mqk of this chunk ready
+            if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
+            if (tid == 0) {                                 // R = [T; 0] X
+                tc::tc_fence_after();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) { r0[i] = 0u; r1[i] = 0u; }
+                for (int kk = 0; kk < 4; ++kk)
+                    tc::mma_f16(tmem + Ly::ACC3, tc::make_desc(tc::smem_u32(tzm) + 32 * kk, 16, 1024),
+                                tc::make_desc(tc::smem_u32(xr) + kk * 2048, 16384, 1024), IDESC_KM, kk != 0);
+                tc::mma_commit(bar_acc3);
             }
-            tc::tmem_st32(tq + 64 * b, r0);
-            tc::tmem_st32(tq + 64 * b + 32, r1);
-        }
-        tc::tmem_wait_st();
-    }
-    tc::tc_fence_before();
-    __syncthreads();
-    tc::tc_fence_after();
-
-    uint32_t s0_uses[2] = {0u, 0u};
-    bool failed = false;
-    for (int c = 0; c < p.nchunks && !failed; ++c) {
-        const int t0 = c * CH;
-        const uint32_t par = (uint32_t)(c & 1);
-        // the previous chunk's update MMA must finish before its K tiles are
-        // overwritten and before the state is read again
-        if (c > 0 && wait_all(bar_upd, par ^ 1u)) { failed = true; break; }
-        if (tid == 0) {
-            tc::mbar_expect_tx(bar_load, NSL * SLICE + 8192);
-            for (int s = 0; s < NSL; ++s) {
-                tc::tma_load_3d(kq + s * SLICE, &tmk, bar_load, 64 * s, t0, lane_bh);
-                tc::tma_load_3d(kq + s * SLICE + 8192, &tmq, bar_load, 64 * s, t0, lane_bh);
-            }
-            tc::tma_load_3d(vr, &tmv, bar_load, 0, t0, lane_bh);
-        }
-        if (tid < CH) {
-            const int t = t0 + tid;
-            const bool ok = t < T_;
-            const int64_t bt = (int64_t)lane_bh * T_ + t;
-            s_beta[tid] = ok ? __half2float(beta[bt]) : 0.f;
-            s_aincl[tid] = ok ? (p.dynamic_decay ? __half2float(decay[bt]) : alpha_static) : 1.f;
-        }
-        __syncthreads();
-        if (tid == 0) {
-            float prod = 1.f;
-            for (int i = 0; i < CH; ++i) {
-                s_aprev[i] = prod;
-                prod *= s_aincl[i];
-                s_aincl[i] = prod;
-            }
-            for (int i = 0; i < CH; ++i) s_aend[i] = prod / s_aincl[i];
-            *s_atot = prod;
-        }
-        if (wait_all(bar_load, par)) { failed = true; break; }
-
-        // ---- G = K K^T, QK = Q K^T (TMEM ACC1: lanes 0-63 G, 64-127 QK) ----
-        if (tid == 0) {
-            for (int s = 0; s < NSL; ++s)
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const uint32_t base = tc::smem_u32(kq + s * SLICE) + 32 * kk;
-                    tc::mma_f16(tmem + Ly::ACC1, tc::make_desc(base, 16, 1024), tc::make_desc(base, 16, 1024),
-                                IDESC_KK, (s | kk) != 0);
-                }
-            tc::mma_commit(bar_acc1);
-        }
-        const float atot = *s_atot;
-
-        // ---- [K;Q] S0 over 128-slot blocks; S0 streamed TMEM -> fp16 smem ----
-        for (int b = 0; b < NB; ++b) {
-            const int buf = b & 1;
-            bool bad = false;
-            if (s0_uses[buf] > 0) bad = !tc::mbar_wait(bar_s0 + buf, (s0_uses[buf] - 1) & 1u);
+            bad = !tc::mbar_wait(bar_acc3, par);
             tc::tc_fence_after();
-            float x[64];
-            ld_row64(tq + 64 * b, x);
-            st_row_f16(s0b + buf * 16384, 32 * warp + lane, x);
-            if (atot != 1.f) {
-                uint32_t r0[32], r1[32];
+            if (warp < 2) {
+                float r[64];
+                ld_row64(tq + Ly::ACC3, r);
+                const int t = t0 + row;
+                if (p.err_out && t < T_) {
+                    float4* dst = reinterpret_cast<float4*>(p.err_out + (lane_base + t) * DH);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    r0[i] = __float_as_uint(atot * x[i]);
-                    r1[i] = __float_as_uint(atot * x[32 + i]);
+                    for (int q = 0; q < 16; ++q) dst[q] = make_float4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
                 }
-                tc::tmem_st32(tq + 64 * b, r0);
-                tc::tmem_st32(tq + 64 * b + 32, r1);
-                tc::tmem_wait_st();
+                float rb[64];
+#pragma unroll
+                for (int j = 0; j < 64; ++j) {
+                    rb[j] = b_row * r[j];
+                    r[j] = ae_row * rb[j];
+                }
+                st_row_f16(vr, row, rb);     // R * beta (V is dead)
+                st_row_f16(xr, row, r);      // R' = a_end * beta * R (X is dead)
             }
             tc::fence_proxy_async();
             tc::tc_fence_before();
-            if (__syncthreads_or(bad)) { failed = true; break; }
-            if (tid == 0) {
+            if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
+            if (tid == 0) {                                 // Mqk (R*beta); S += K^T R'
                 tc::tc_fence_after();
 #pragma unroll
-                for (int sl = 0; sl < 2; ++sl)
+                for (int kk = 0; kk < 4; ++kk)
+                    tc::mma_f16(tmem + Ly::ACC4, tc::make_desc(tc::smem_u32(tzm + 8192) + 32 * kk, 16, 1024),
+                                tc::make_desc(tc::smem_u32(vr) + kk * 2048, 16384, 1024), IDESC_KM, kk != 0);
+                tc::mma_commit(bar_acc4);
+                for (int b = 0; b < NB; ++b)
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const uint32_t a = tc::smem_u32(kq + (2 * b + sl) * SLICE) + 32 * kk;
-                        const uint32_t bb = tc::smem_u32(s0b + buf * 16384) + (sl * 4 + kk) * 2048;
-                        tc::mma_f16(tmem + Ly::ACC2, tc::make_desc(a, 16, 1024), tc::make_desc(bb, 16384, 1024),
-                                    IDESC_KM, (b | sl | kk) != 0);
-                    }
-                tc::mma_commit(bar_s0 + buf);
-                if (b == NB - 1) tc::mma_commit(bar_acc2);
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc::mma_f16(tmem + 64 * b,
+                                    tc::make_desc(tc::smem_u32(kq + 2 * b * SLICE) + kk * 2048, SLICE, 1024),
+                                    tc::make_desc(tc::smem_u32(xr) + kk * 2048, 16384, 1024), IDESC_MM, 1u);
+                tc::mma_commit(bar_upd);
             }
-            s0_uses[buf]++;
+            // Y = aprev o (Q S0) + Mqk R  (warps 2-3)
+            bad = !tc::mbar_wait(bar_acc4, par);
+            tc::tc_fence_after();
+            if (warp >= 2 && !bad) {
+                float y[64], m[64];
+                ld_row64(tq + Ly::ACC2, y);
+                ld_row64(tq + Ly::ACC4, m);
+                const int t = t0 + row;
+                if (t < T_) {
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + (lane_base + t) * DH);
+#pragma unroll
+                    for (int cc = 0; cc < 8; ++cc) {
+                        float o[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) o[e] = fmaf(ap_row, y[8 * cc + e], m[8 * cc + e]);
+                        dst[cc] = make_uint4(pack_h2(o[0], o[1]), pack_h2(o[2], o[3]), pack_h2(o[4], o[5]),
+                                             pack_h2(o[6], o[7]));
+                    }
+                }
+            }
+            // the update must finish before the K / V tiles and the state are reused
+            bad = bad || !tc::mbar_wait(bar_upd, par);
+            tc::tc_fence_after();
+            if (tid == 0 && c + 1 < NC && !bad) {
+                tc::mbar_expect_tx(bar_kv, NSL * 8192 + 8192);
+                for (int s = 0; s < NSL; ++s) tc::tma_load_3d(kq + s * SLICE, &tmk, bar_kv, 64 * s, t0 + CH, lane_bh);
+                tc::tma_load_3d(vr, &tmv, bar_kv, 0, t0 + CH, lane_bh);
+            }
+            if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
         }
-        if (failed) break;
-
-        // ---- L (warps 0-1) and Mqk (warps 2-3) from ACC1 ----
-        if (wait_all(bar_acc1, par)) { failed = true; break; }
-        {
+        if (!failed) {
+            __half* s_fin = static_cast<__half*>(p.s_final);
+            for (int b = 0; b < NB; ++b) {
+                const int slot = 128 * b + 32 * warp + lane;
+                float x[64];
+                ld_row64(tq + 64 * b, x);
+                const int64_t o = ((int64_t)lane_bh * S + slot) * DH;
+                uint4* dst = reinterpret_cast<uint4*>(s_fin + o);
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc)
+                    dst[cc] = make_uint4(pack_h2(x[8 * cc], x[8 * cc + 1]), pack_h2(x[8 * cc + 2], x[8 * cc + 3]),
+                                         pack_h2(x[8 * cc + 4], x[8 * cc + 5]), pack_h2(x[8 * cc + 6], x[8 * cc + 7]));
+                if (p.s_final_f) {
+                    float4* df = reinterpret_cast<float4*>(p.s_final_f + o);
+#pragma unroll
+                    for (int q = 0; q < 16; ++q)
+                        df[q] = make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
+                }
+            }
+        }
+    } else {
+        // ================= WG1: per-chunk T = (I + L)^{-1} and Mqk =================
+        const int t1 = tid - 128;
+        const int row = 32 * (warp & 1) + lane;         // G row (warps 4,5) or QK row (warps 6,7)
+        for (int c = 0; c < NC && !failed; ++c) {
+            const int t0 = c * CH;
+            const uint32_t par = (uint32_t)(c & 1);
+            const ChunkScalars cs = chunk_scalars(beta, decay, p.dynamic_decay, alpha_static, lane_base, t0, T_, lane);
+            const float ap_row = pick(cs.ap0, cs.ap1, row);
+            const float w0 = cs.b0 / cs.a0, w1 = cs.b1 / cs.a1;    // beta_j / a_j
+            const float u0 = 1.f / cs.a0, u1 = 1.f / cs.a1;        // 1 / a_j
+            const bool bad = !tc::mbar_wait(bar_acc1, par);
+            if (tc::group_sync_or(BAR_WG1, bad)) { failed = true; break; }
+            tc::tc_fence_after();
             float g[64];
             ld_row64(tq + Ly::ACC1, g);
-            const int i = 32 * (warp & 1) + lane;
-            const float ap = s_aprev[i];
-            if (warp < 2) {
+            if (warp < 6) {         // L_ij = aprev_i beta_j / a_j (k_i . k_j), j < i
 #pragma unroll
-                for (int j = 0; j < 64; ++j) lt[i * 65 + j] = (j < i) ? (ap / s_aincl[j]) * s_beta[j] * g[j] : 0.f;
-            } else {
-#pragma unroll
-                for (int j = 0; j < 64; ++j) g[j] = (j < i) ? (ap / s_aincl[j]) * g[j] : 0.f;   // beta is in R*beta
-                st_row_f16(tzm + 16384, i, g);
-            }
-        }
-        __syncthreads();
-        invert_unit_lower(lt, pb, tid);
-        if (tid < 64) {
-            const int i = tid;
-            float row[64];
-#pragma unroll
-            for (int j = 0; j < 64; ++j) {
-                const int bi = i >> 4, bj = j >> 4;
-                float v = 0.f;
-                if (j <= i) v = (bi == bj) ? lt[i * 65 + j] : lt[(16 * bj + (i & 15)) * 65 + 16 * bi + (j & 15)];
-                row[j] = v;
-            }
-            st_row_f16(tzm, i, row);
-        }
-        tc::fence_proxy_async();
-
-        // ---- X = V - aprev o (K S0)  (warps 0-1, token rows) ----
-        if (wait_all(bar_acc2, par)) { failed = true; break; }
-        if (warp < 2) {
-            const int i = 32 * warp + lane;
-            float d1[64];
-            ld_row64(tq + Ly::ACC2, d1);
-            const float ap = s_aprev[i];
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-                const uint4 v = *reinterpret_cast<const uint4*>(vr + tc::sw128(i, cc));
-                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = unpack_h2(w4[e]);
-                    d1[8 * cc + 2 * e] = f.x - ap * d1[8 * cc + 2 * e];
-                    d1[8 * cc + 2 * e + 1] = f.y - ap * d1[8 * cc + 2 * e + 1];
+                for (int j = 0; j < 64; ++j) {
+                    const float wj = pick(w0, w1, j);
+                    g[j] = (j < row) ? ap_row * wj * g[j] : 0.f;
                 }
-            }
-            st_row_f16(xr, i, d1);
-        }
-        tc::fence_proxy_async();
-        tc::tc_fence_before();
-        __syncthreads();
-
-        // ---- R = T X  (ACC3 lanes 0-63) ----
-        if (tid == 0) {
-            tc::tc_fence_after();
+                float4* dst = reinterpret_cast<float4*>(lt + row * LDT);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-                tc::mma_f16(tmem + Ly::ACC3, tc::make_desc(tc::smem_u32(tzm) + 32 * kk, 16, 1024),
-                            tc::make_desc(tc::smem_u32(xr) + kk * 2048, 16384, 1024), IDESC_KM, kk != 0);
-            tc::mma_commit(bar_acc3);
-        }
-        if (wait_all(bar_acc3, par)) { failed = true; break; }
-        if (warp < 2) {
-            const int i = 32 * warp + lane;
-            float r[64];
-            ld_row64(tq + Ly::ACC3, r);
-            const int t = t0 + i;
-            if (p.err_out && t < T_) {
-                float4* dst = reinterpret_cast<float4*>(p.err_out + ((int64_t)lane_bh * T_ + t) * DH);
+                for (int q = 0; q < 16; ++q) dst[q] = make_float4(g[4 * q], g[4 * q + 1], g[4 * q + 2], g[4 * q + 3]);
+            } else {                // Mqk_ij = aprev_i / a_j (q_i . k_j), j < i
 #pragma unroll
-                for (int q = 0; q < 16; ++q) dst[q] = make_float4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
-            }
-            const float bi = s_beta[i], ae = s_aend[i];
-            float rb[64];
-#pragma unroll
-            for (int j = 0; j < 64; ++j) {
-                rb[j] = bi * r[j];
-                r[j] = ae * rb[j];
-            }
-            st_row_f16(vr, i, rb);     // R * beta (V is dead)
-            st_row_f16(xr, i, r);      // R' = a_end * beta * R (X is dead)
-        }
-        tc::fence_proxy_async();
-        tc::tc_fence_before();
-        __syncthreads();
-
-        // ---- ACC4 = Mqk (R*beta) (lanes 64-127); S += K^T R' ----
-        if (tid == 0) {
-            tc::tc_fence_after();
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-                tc::mma_f16(tmem + Ly::ACC4, tc::make_desc(tc::smem_u32(tzm + 8192) + 32 * kk, 16, 1024),
-                            tc::make_desc(tc::smem_u32(vr) + kk * 2048, 16384, 1024), IDESC_KM, kk != 0);
-            tc::mma_commit(bar_acc4);
-            for (int b = 0; b < NB; ++b)
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    tc::mma_f16(tmem + 64 * b,
-                                tc::make_desc(tc::smem_u32(kq + 2 * b * SLICE) + kk * 2048, SLICE, 1024),
-                                tc::make_desc(tc::smem_u32(xr) + kk * 2048, 16384, 1024), IDESC_MM, 1u);
-            tc::mma_commit(bar_upd);
-        }
-
-        // ---- Y = aprev o (Q S0) + Mqk R  (warps 2-3, token rows) ----
-        if (wait_all(bar_acc4, par)) { failed = true; break; }
-        if (warp >= 2) {
-            const int i = 32 * (warp - 2) + lane;
-            float y[64], m[64];
-            ld_row64(tq + Ly::ACC2, y);
-            ld_row64(tq + Ly::ACC4, m);
-            const int t = t0 + i;
-            if (t < T_) {
-                const float ap = s_aprev[i];
-                uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + ((int64_t)lane_bh * T_ + t) * DH);
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc) {
-                    float o[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) o[e] = fmaf(ap, y[8 * cc + e], m[8 * cc + e]);
-                    dst[cc] = make_uint4(pack_h2(o[0], o[1]), pack_h2(o[2], o[3]), pack_h2(o[4], o[5]),
-                                         pack_h2(o[6], o[7]));
+                for (int j = 0; j < 64; ++j) {
+                    const float uj = pick(u0, u1, j);
+                    g[j] = (j < row) ? ap_row * uj * g[j] : 0.f;
                 }
+                st_row_f16(tzm + 16384, row, g);
+            }
+            tc::group_sync(BAR_WG1);
+            invert_unit_lower(lt, t1);
+            if (t1 < 64) {
+                float tr[64];
+                const float4* src = reinterpret_cast<const float4*>(lt + t1 * LDT);
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                    const float4 v = src[q];
+                    tr[4 * q] = v.x; tr[4 * q + 1] = v.y; tr[4 * q + 2] = v.z; tr[4 * q + 3] = v.w;
+                }
+                st_row_f16(tzm, t1, tr);
+            }
+            tc::fence_proxy_async();
+            tc::group_sync(BAR_WG1);
+            if (t1 == 0) {
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar_t)) : "memory");
             }
         }
     }
 
-    if (!failed && p.nchunks > 0) failed = wait_all(bar_upd, (uint32_t)((p.nchunks - 1) & 1));
-    if (!failed) {
-        __half* s_fin = static_cast<__half*>(p.s_final);
-        for (int b = 0; b < NB; ++b) {
-            const int slot = 128 * b + 32 * warp + lane;
-            float x[64];
-            ld_row64(tq + 64 * b, x);
-            const int64_t o = ((int64_t)lane_bh * S + slot) * DH;
-            uint4* dst = reinterpret_cast<uint4*>(s_fin + o);
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc)
-                dst[cc] = make_uint4(pack_h2(x[8 * cc], x[8 * cc + 1]), pack_h2(x[8 * cc + 2], x[8 * cc + 3]),
-                                     pack_h2(x[8 * cc + 4], x[8 * cc + 5]), pack_h2(x[8 * cc + 6], x[8 * cc + 7]));
-            if (p.s_final_f) {
-                float4* df = reinterpret_cast<float4*>(p.s_final_f + o);
-#pragma unroll
-                for (int q = 0; q < 16; ++q) df[q] = make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
-            }
-        }
-    } else if (tid == 0) {
-        dg::flag_status(p.status, DG_DEVCHK_TIMEOUT);
-    }
+    if (failed && (tid == 0 || tid == 128)) dg::flag_status(p.status, DG_DEVCHK_TIMEOUT);
     tc::tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -558,7 +625,7 @@ int launch_chunk(const void* v, const void* beta, const void* wk, const void* wq
     auto kern = dense_chunk_kernel<S>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return dg_host::record_cuda_error(e);
-    kern<<<lanes, 128, smem, stream>>>(mk, mq, mv, p);
+    kern<<<lanes, 256, smem, stream>>>(mk, mq, mv, p);
     return dg_host::check_launch();
 }
 
