@@ -63,7 +63,8 @@ struct Layout {
     static constexpr uint32_t XR = TZM + 3 * 8192;          // X, then R'
     static constexpr uint32_t VR = XR + 8192;               // V, then R*beta
     static constexpr uint32_t LT = VR + 8192;               // fp32 [64][68]
-    static constexpr uint32_t BAR = LT + 64 * 68 * 4;       // 12 mbarriers + tmem base
+    static constexpr uint32_t SC1 = LT + 64 * 68 * 4;       // WG1 per-chunk scalars: aprev, beta/a, 1/a
+    static constexpr uint32_t BAR = SC1 + 3 * 64 * 4;       // 12 mbarriers + tmem base
     static constexpr uint32_t BYTES = BAR + 12 * 8 + 16;
     static constexpr uint32_t ACC1 = NB * 64;               // TMEM column bases
     static constexpr uint32_t ACC2 = ACC1 + 64;
@@ -153,83 +154,105 @@ __device__ __forceinline__ float pick(float v0, float v1, int i) {
     return (i & 1) ? b : a;
 }
 
-// (I + L)^{-1} for strictly lower L (64x64 fp32, row stride LDT) in place,
-// by one warpgroup (t = 0..127).  With 16x16 blocks:
-//   D_b = (I + L_bb)^{-1}                 (forward substitution, one warp per block)
-//   E_ij = -D_i L_ij   (i > j)            (all six blocks at once)
-//   T_ik = sum_{j=k}^{i-1} E_ij T_jk      (block rows 1, 2, 3 in order; T_kk = D_k)
-// Results overwrite L block by block; every block is computed into registers
-// and written after a barrier, so reads always see the previous stage.
+// (I + L)^{-1} for strictly lower L (64x64 fp32, row stride LDT), in place, by one
+// warpgroup (t = 0..127).  Two-level blocked inverse of a unit lower-triangular
+// matrix, [[A, 0], [C, D]]^{-1} = [[A^-1, 0], [-D^-1 C A^-1, D^-1]]:
+//   1. the four 16x16 diagonal blocks by forward substitution (one warp each);
+//   2. the 32x32 halves A^-1 and D^-1: off-diagonal 16x16 block -D1^-1 L10 D0^-1;
+//   3. P = C A^-1 and 4. -D^-1 P for the lower-left 32x32 quadrant.
+// Products are register-tiled (each thread a 2x2 or 2x4 output tile) and every
+// stage writes its results after a barrier, so reads always see the previous stage.
+__device__ __forceinline__ float& lt_at(float* lt, int r, int c) { return lt[r * LDT + c]; }
+
 __device__ void invert_unit_lower(float* lt, int t) {
     const int warp = t >> 5, lane = t & 31;
-    auto at = [&](int r, int c) -> float& { return lt[r * LDT + c]; };
-    {   // diagonal blocks
+    {   // 1. diagonal 16x16 blocks: lane = column of the block's inverse
         const int b = warp, col = lane & 15;
         float x[16];
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
-            float s = (r == col) ? 1.f : 0.f;
+            float s0 = (r == col) ? 1.f : 0.f, s1 = 0.f;
 #pragma unroll
-            for (int j = 0; j < r; ++j) s = fmaf(-at(16 * b + r, 16 * b + j), x[j], s);
-            x[r] = s;
+            for (int j = 0; j < r; ++j) {
+                const float l = lt_at(lt, 16 * b + r, 16 * b + j);
+                if (j & 1) s1 = fmaf(-l, x[j], s1); else s0 = fmaf(-l, x[j], s0);
+            }
+            x[r] = s0 + s1;
         }
         tc::group_sync(BAR_WG1);
         if (lane < 16) {
 #pragma unroll
-            for (int r = 0; r < 16; ++r) at(16 * b + r, 16 * b + col) = x[r];
+            for (int r = 0; r < 16; ++r) lt_at(lt, 16 * b + r, 16 * b + col) = x[r];
         }
         tc::group_sync(BAR_WG1);
     }
-    {   // E_ij = -D_i L_ij for (1,0) (2,0) (2,1) (3,0) (3,1) (3,2)
-        // block pairs in order (1,0) (2,0) (2,1) (3,0) (3,1) (3,2)
-        auto bi_of = [](int k) { return k == 0 ? 1 : (k < 3 ? 2 : 3); };
-        auto bj_of = [](int k) { return k == 0 ? 0 : (k == 1 ? 0 : (k == 2 ? 1 : (k == 3 ? 0 : (k == 4 ? 1 : 2)))); };
-        float e[12];
+    {   // 2. half h (64 threads): block (2h+1, 2h) = -D_{2h+1} L_{2h+1,2h} D_{2h}, 2x2 tile per thread
+        const int h = t >> 6, u = t & 63, ti = u >> 3, tj = u & 7;
+        const int r0 = 16 * (2 * h + 1) + 2 * ti, c0 = 16 * (2 * h) + 2 * tj;     // output rows / cols
+        const int k0 = 16 * (2 * h);                                             // inner index base (D_{2h})
+        float p00 = 0.f, p01 = 0.f, p10 = 0.f, p11 = 0.f;
 #pragma unroll
-        for (int m = 0; m < 12; ++m) {
-            const int o = t + 128 * m;
-            const int blk = o >> 8, a = (o >> 4) & 15, c = o & 15;
-            const int bi = bi_of(blk), bj = bj_of(blk);
-            float s = 0.f;
-#pragma unroll
-            for (int q = 0; q < 16; ++q) s = fmaf(at(16 * bi + a, 16 * bi + q), at(16 * bi + q, 16 * bj + c), s);
-            e[m] = -s;
+        for (int k = 0; k < 16; ++k) {
+            const float a0 = lt_at(lt, r0, k0 + k), a1 = lt_at(lt, r0 + 1, k0 + k);
+            const float2 bb = *reinterpret_cast<const float2*>(&lt_at(lt, k0 + k, c0));
+            p00 = fmaf(a0, bb.x, p00); p01 = fmaf(a0, bb.y, p01);
+            p10 = fmaf(a1, bb.x, p10); p11 = fmaf(a1, bb.y, p11);
         }
         tc::group_sync(BAR_WG1);
+        *reinterpret_cast<float2*>(&lt_at(lt, r0, c0)) = make_float2(p00, p01);
+        *reinterpret_cast<float2*>(&lt_at(lt, r0 + 1, c0)) = make_float2(p10, p11);
+        tc::group_sync(BAR_WG1);
+        const int d0 = 16 * (2 * h + 1);                                         // D_{2h+1} diagonal base
+        float q00 = 0.f, q01 = 0.f, q10 = 0.f, q11 = 0.f;
 #pragma unroll
-        for (int m = 0; m < 12; ++m) {
-            const int o = t + 128 * m;
-            const int blk = o >> 8, a = (o >> 4) & 15, c = o & 15;
-            at(16 * bi_of(blk) + a, 16 * bj_of(blk) + c) = e[m];
+        for (int k = 0; k < 16; ++k) {
+            const float a0 = lt_at(lt, r0, d0 + k), a1 = lt_at(lt, r0 + 1, d0 + k);
+            const float2 bb = *reinterpret_cast<const float2*>(&lt_at(lt, d0 + k, c0));
+            q00 = fmaf(a0, bb.x, q00); q01 = fmaf(a0, bb.y, q01);
+            q10 = fmaf(a1, bb.x, q10); q11 = fmaf(a1, bb.y, q11);
         }
+        tc::group_sync(BAR_WG1);
+        *reinterpret_cast<float2*>(&lt_at(lt, r0, c0)) = make_float2(-q00, -q01);
+        *reinterpret_cast<float2*>(&lt_at(lt, r0 + 1, c0)) = make_float2(-q10, -q11);
         tc::group_sync(BAR_WG1);
     }
-    // block rows: T_ik = sum_{j=k}^{i-1} E_ij T_jk, with T_kk = D_k in the diagonal block
+    {   // 3./4. lower-left quadrant: P = C A^-1, then -D^-1 P; 2x4 tile per thread
+        const int ti = t >> 3, tj = t & 7;
+        const int r0 = 32 + 2 * ti, c0 = 4 * tj;
+        float acc[2][4];
 #pragma unroll
-    for (int bi = 1; bi < 4; ++bi) {
-        float r[6];
+        for (int i = 0; i < 2; ++i)
 #pragma unroll
-        for (int m = 0; m < 6; ++m) {
-            if (m < 2 * bi) {
-                const int o = t + 128 * m;
-                const int bk = o >> 8, a = (o >> 4) & 15, c = o & 15;
-                float s = 0.f;
-                for (int bj = bk; bj < bi; ++bj)
-#pragma unroll
-                    for (int q = 0; q < 16; ++q)
-                        s = fmaf(at(16 * bi + a, 16 * bj + q), at(16 * bj + q, 16 * bk + c), s);
-                r[m] = s;
-            }
+            for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+#pragma unroll 8
+        for (int k = 0; k < 32; ++k) {           // C (rows 32..63, cols 0..31) times A^-1 (rows/cols 0..31)
+            const float a0 = lt_at(lt, r0, k), a1 = lt_at(lt, r0 + 1, k);
+            const float4 bb = *reinterpret_cast<const float4*>(&lt_at(lt, k, c0));
+            acc[0][0] = fmaf(a0, bb.x, acc[0][0]); acc[0][1] = fmaf(a0, bb.y, acc[0][1]);
+            acc[0][2] = fmaf(a0, bb.z, acc[0][2]); acc[0][3] = fmaf(a0, bb.w, acc[0][3]);
+            acc[1][0] = fmaf(a1, bb.x, acc[1][0]); acc[1][1] = fmaf(a1, bb.y, acc[1][1]);
+            acc[1][2] = fmaf(a1, bb.z, acc[1][2]); acc[1][3] = fmaf(a1, bb.w, acc[1][3]);
         }
         tc::group_sync(BAR_WG1);
+        *reinterpret_cast<float4*>(&lt_at(lt, r0, c0)) = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+        *reinterpret_cast<float4*>(&lt_at(lt, r0 + 1, c0)) = make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]);
+        tc::group_sync(BAR_WG1);
 #pragma unroll
-        for (int m = 0; m < 6; ++m) {
-            if (m < 2 * bi) {
-                const int o = t + 128 * m;
-                const int bk = o >> 8, a = (o >> 4) & 15, c = o & 15;
-                at(16 * bi + a, 16 * bk + c) = r[m];
-            }
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+#pragma unroll 8
+        for (int k = 0; k < 32; ++k) {           // D^-1 (rows/cols 32..63) times P (rows 32..63, cols 0..31)
+            const float a0 = lt_at(lt, r0, 32 + k), a1 = lt_at(lt, r0 + 1, 32 + k);
+            const float4 bb = *reinterpret_cast<const float4*>(&lt_at(lt, 32 + k, c0));
+            acc[0][0] = fmaf(a0, bb.x, acc[0][0]); acc[0][1] = fmaf(a0, bb.y, acc[0][1]);
+            acc[0][2] = fmaf(a0, bb.z, acc[0][2]); acc[0][3] = fmaf(a0, bb.w, acc[0][3]);
+            acc[1][0] = fmaf(a1, bb.x, acc[1][0]); acc[1][1] = fmaf(a1, bb.y, acc[1][1]);
+            acc[1][2] = fmaf(a1, bb.z, acc[1][2]); acc[1][3] = fmaf(a1, bb.w, acc[1][3]);
         }
+        tc::group_sync(BAR_WG1);
+        *reinterpret_cast<float4*>(&lt_at(lt, r0, c0)) = make_float4(-acc[0][0], -acc[0][1], -acc[0][2], -acc[0][3]);
+        *reinterpret_cast<float4*>(&lt_at(lt, r0 + 1, c0)) = make_float4(-acc[1][0], -acc[1][1], -acc[1][2], -acc[1][3]);
         tc::group_sync(BAR_WG1);
     }
 }
@@ -248,6 +271,7 @@ __global__ void __launch_bounds__(256, 1)
     uint8_t* xr = sm + Ly::XR;
     uint8_t* vr = sm + Ly::VR;
     float* lt = reinterpret_cast<float*>(sm + Ly::LT);
+    float* sc1 = reinterpret_cast<float*>(sm + Ly::SC1);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ly::BAR);
     uint64_t* bar_kv = bars + 0;     // TMA: K slices + V of a chunk
     uint64_t* bar_q = bars + 1;      // TMA: Q slices of a chunk
@@ -524,30 +548,34 @@ __global__ void __launch_bounds__(256, 1)
         for (int c = 0; c < NC && !failed; ++c) {
             const int t0 = c * CH;
             const uint32_t par = (uint32_t)(c & 1);
-            const ChunkScalars cs = chunk_scalars(beta, decay, p.dynamic_decay, alpha_static, lane_base, t0, T_, lane);
-            const float ap_row = pick(cs.ap0, cs.ap1, row);
-            const float w0 = cs.b0 / cs.a0, w1 = cs.b1 / cs.a1;    // beta_j / a_j
-            const float u0 = 1.f / cs.a0, u1 = 1.f / cs.a1;        // 1 / a_j
+            if (warp == 4) {      // chunk scalars for the whole warpgroup
+                const ChunkScalars cs = chunk_scalars(beta, decay, p.dynamic_decay, alpha_static, lane_base, t0, T_, lane);
+                reinterpret_cast<float2*>(sc1)[lane] = make_float2(cs.ap0, cs.ap1);
+                reinterpret_cast<float2*>(sc1 + 64)[lane] = make_float2(cs.b0 / cs.a0, cs.b1 / cs.a1);
+                reinterpret_cast<float2*>(sc1 + 128)[lane] = make_float2(1.f / cs.a0, 1.f / cs.a1);
+            }
             const bool bad = !tc::mbar_wait(bar_acc1, par);
             if (tc::group_sync_or(BAR_WG1, bad)) { failed = true; break; }
             tc::tc_fence_after();
+            const float ap_row = sc1[row];
+            const float* wsel = (warp < 6) ? (sc1 + 64) : (sc1 + 128);   // L: beta_j / a_j; Mqk: 1 / a_j
             float g[64];
             ld_row64(tq + Ly::ACC1, g);
-            if (warp < 6) {         // L_ij = aprev_i beta_j / a_j (k_i . k_j), j < i
 #pragma unroll
-                for (int j = 0; j < 64; ++j) {
-                    const float wj = pick(w0, w1, j);
-                    g[j] = (j < row) ? ap_row * wj * g[j] : 0.f;
+            for (int q = 0; q < 16; ++q) {
+                const float4 w4 = reinterpret_cast<const float4*>(wsel)[q];
+                const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int j = 4 * q + e;
+                    g[j] = (j < row) ? ap_row * wv[e] * g[j] : 0.f;
                 }
+            }
+            if (warp < 6) {         // L_ij = aprev_i beta_j / a_j (k_i . k_j), j < i
                 float4* dst = reinterpret_cast<float4*>(lt + row * LDT);
 #pragma unroll
                 for (int q = 0; q < 16; ++q) dst[q] = make_float4(g[4 * q], g[4 * q + 1], g[4 * q + 2], g[4 * q + 3]);
             } else {                // Mqk_ij = aprev_i / a_j (q_i . k_j), j < i
-#pragma unroll
-                for (int j = 0; j < 64; ++j) {
-                    const float uj = pick(u0, u1, j);
-                    g[j] = (j < row) ? ap_row * uj * g[j] : 0.f;
-                }
                 st_row_f16(tzm + 16384, row, g);
             }
             tc::group_sync(BAR_WG1);
