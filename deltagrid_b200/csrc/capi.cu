@@ -29,6 +29,12 @@ int pkm_forward_v1(int dtype, int B, int H, int T, int A, int64_t total, int Dh,
                    const void* beta, const void* wk, const void* wq, const int64_t* idx,
                    const void* decay, int dynamic_decay, void* state, void* out, void* saved,
                    int32_t* status, cudaStream_t stream);
+bool pkm_pipe_supports(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v,
+                       const void* beta, const void* wk, const void* wq, const void* idx, const void* decay,
+                       int dynamic_decay, const void* state, const void* saved);
+int pkm_forward_pipe(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
+                     const void* wk, const void* wq, const int64_t* idx, const void* decay, int dynamic_decay,
+                     void* state, void* out, int32_t* status, cudaStream_t stream);
 
 }  // namespace dg_host
 
@@ -109,6 +115,12 @@ int dg_pkm_forward(int dtype, int B, int H, int T, int active, int64_t total_slo
     if (T == 0) return DG_OK;              // nothing to do; per-step tensors may be empty
     if (!v || !beta || !wk || !wq || !idx || !decay || !out) return DG_ERR_INVALID_ARGUMENT;
     if ((int64_t)B * H > 65535) return DG_ERR_UNSUPPORTED;
+    // pipelined kernel for long sequences it covers; the one-step-at-a-time
+    // kernel for short ones (decode steps), saved rows and other shapes
+    if (T >= 64 && pkm_pipe_supports(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
+                                     dynamic_decay, state, saved_s_act))
+        return pkm_forward_pipe(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
+                                dynamic_decay, state, out, dev_status, static_cast<cudaStream_t>(stream));
     return pkm_forward_v1(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
                           dynamic_decay, state, out, saved_s_act, dev_status,
                           static_cast<cudaStream_t>(stream));
