@@ -8,7 +8,7 @@
 // Steps depend on each other only through shared rows, and every step's slot
 // indices are inputs (state-independent), so rows can be fetched D steps ahead:
 //   - one CTA per (lane, part of the row); CW column-slice warps own 16-byte
-//     column slices as in pkm_seq.cu, plus one scheduler warp;
+//     column slices as in pkm_seq.cu, plus two scheduler warps;
 //   - at iteration s the column warps consume step s from a shared-memory row
 //     ring (filled by cp.async issued at iteration s - D) and issue the copies
 //     for step s + D after the iteration barrier, which orders all stores of
@@ -18,10 +18,10 @@
 //     earlier step in the window [s+1, s+D-1] that wrote the same slot (whose
 //     store the copy cannot see).  Such rows are not fetched; the consumer takes
 //     them from the writer's ring slot, which holds the rounded values it stored.
-//     The lookup uses a shared open-addressing table slot -> (step, position)
-//     whose entries expire by step stamp; inserts use 64-bit CAS.  If a probe
-//     sequence is full the table overflows: the next D steps then reload their
-//     rows synchronously from global memory (exact, slower).
+//     The lookup uses a shared 8-way set-associative table slot -> (step,
+//     position) whose entries expire by step stamp; inserts use 64-bit CAS.  If
+//     a bucket holds 8 live other slots the table overflows: the next D steps
+//     then reload their rows synchronously from global memory (exact, slower).
 // The per-step dependency chain is the warp reduction; memory latency is
 // hidden by the D steps in flight.
 #include "dg_common.cuh"
@@ -29,9 +29,9 @@
 namespace {
 
 constexpr int MAXA = 64;                 // active rows per step handled here
-constexpr int HBITS = 12;                // hash table: 4096 entries
-constexpr int HSIZE = 1 << HBITS;
-constexpr int PROBES = 8;
+constexpr int WAYS = 8;                  // hash table: 512 buckets x 8 cells (one 64-byte bucket per key)
+constexpr int NBUCKET = 512;
+constexpr int HSIZE = NBUCKET * WAYS;
 
 struct PipeParams {
     const void* v;
@@ -57,7 +57,7 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-__device__ __forceinline__ uint32_t slot_hash(uint32_t x) { return (x * 2654435761u) >> (32 - HBITS); }
+__device__ __forceinline__ uint32_t slot_bucket(uint32_t x) { return (x * 2654435761u) >> 23; }   // 9 bits
 
 template <int NV>
 struct Log2v { static constexpr int v = (NV <= 1) ? 0 : 1 + Log2v<NV / 2>::v; };
@@ -92,7 +92,7 @@ __host__ __device__ constexpr int meta_bytes(int esz, int row_bytes) {
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(544) pkm_pipe_kernel(PipeParams p) {
+__global__ void __launch_bounds__(576) pkm_pipe_kernel(PipeParams p) {
     using V = dg::Vec16<T>;
     constexpr int CPW = V::N;
     constexpr int NV = 2 * CPW;
@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(544) pkm_pipe_kernel(PipeParams p) {
     constexpr int EPB = 16 / sizeof(T);  // beta values per 16-byte block
 
     extern __shared__ __align__(16) uint8_t smem[];
-    const int CW = blockDim.x / 32 - 1;               // column-slice warps
+    const int CW = blockDim.x / 32 - 2;               // column-slice warps
     const int part_bytes = p.Dh * (int)sizeof(T) / p.parts;
     const int row_stride = part_bytes + 16;           // padded: conflict-free 16-byte slices
     const int slot_bytes = MAXA * row_stride;
@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(544) pkm_pipe_kernel(PipeParams p) {
     uint8_t* gstate = reinterpret_cast<uint8_t*>(p.state) + ((int64_t)lane_bh * total * Dh) * (int64_t)sizeof(T) +
                       (int64_t)part * part_bytes;
     const int64_t row_bytes = (int64_t)Dh * sizeof(T);
-    const bool is_sched = warp == CW;
+    const bool is_sched = warp >= CW;              // two scheduler warps
 
     for (int i = tid; i < HSIZE; i += blockDim.x) tbl[i] = 0ull;
     if (tid == 0) *sync_until = -1;
@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(544) pkm_pipe_kernel(PipeParams p) {
     const int col_off = 16 * warp;            // this warp's slice inside the row part
 
     // prologue: metadata for steps 0..D-1
-    if (is_sched)
+    if (warp == CW)
         for (int j = 0; j < D; ++j) issue_meta(j);
 
     for (int s = -D; s < T_; ++s) {
@@ -250,66 +250,75 @@ __global__ void __launch_bounds__(544) pkm_pipe_kernel(PipeParams p) {
                 }
             }
         }
-        // ---------------- scheduler: metadata and hazards for step s + D ----------------
+        // ---------------- scheduler warps: metadata and hazards for step s + D ----------------
+        // Warp CW issues the metadata copies; warps CW and CW+1 each take 32 rows.
+        // A table cell holds key (slot + 1) in the low word and the writer stamp
+        // (step << 6 | position) in the high word; a key's cell lives in bucket
+        // slot_bucket(slot), and a cell is reusable once its writer step <= s.
         if (is_sched) {
-            issue_meta(s + 2 * D);
-            cp_wait<D>();                 // metadata of step s + D has landed
-            __syncwarp();
+            const int sw = warp - CW;
+            if (sw == 0) {
+                issue_meta(s + 2 * D);
+                cp_wait<D>();             // metadata of step s + D has landed
+            }
+            asm volatile("bar.sync 1, 64;" ::: "memory");
             const int u = s + D;
+            const int m = 32 * sw + lane;
             if (u < T_) {
                 uint8_t* ms = meta_slot(u);
                 const int64_t* midx = reinterpret_cast<const int64_t*>(ms);
                 int16_t* mfwd = reinterpret_cast<int16_t*>(ms + off_fwd);
-                uint32_t key[2];
-                bool have[2];
+                bool have = false;
+                uint32_t key = 0;
+                unsigned long long* bk = nullptr;
+                int16_t f = -1;
+                if (m < A) {
+                    const int64_t x = midx[m];
+                    if (x >= 0 && x < total) {
+                        have = true;
+                        key = (uint32_t)x + 1u;
+                        bk = tbl + WAYS * slot_bucket((uint32_t)x);
+                        const ulonglong2* b2 = reinterpret_cast<const ulonglong2*>(bk);
+                        unsigned long long c[WAYS];
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const int m = lane + 32 * i;
-                    have[i] = false;
-                    key[i] = 0;
-                    int16_t f = -1;
-                    if (m < A) {
-                        const int64_t x = midx[m];
-                        if (x >= 0 && x < total) {
-                            have[i] = true;
-                            key[i] = (uint32_t)x + 1u;
-                            const uint32_t hh = slot_hash((uint32_t)x);
-                            for (int q = 0; q < PROBES; ++q) {
-                                const unsigned long long e = tbl[(hh + q) & (HSIZE - 1)];
-                                const uint32_t k = (uint32_t)e;
-                                if (k == 0u) break;
-                                if (k == key[i]) {
-                                    const uint32_t st = (uint32_t)(e >> 32);
-                                    const int w = (int)(st >> 6);
-                                    if (u - w >= 1 && u - w <= D - 1) f = (int16_t)(((w % RR) << 6) | (st & 63));
-                                    break;
-                                }
+                        for (int q = 0; q < WAYS / 2; ++q) { const ulonglong2 v2 = b2[q]; c[2 * q] = v2.x; c[2 * q + 1] = v2.y; }
+#pragma unroll
+                        for (int q = 0; q < WAYS; ++q) {
+                            if ((uint32_t)c[q] == key) {
+                                const uint32_t st = (uint32_t)(c[q] >> 32);
+                                const int w = (int)(st >> 6);
+                                if (u - w >= 1 && u - w <= D - 1) f = (int16_t)(((w % RR) << 6) | (st & 63));
                             }
-                        } else {
-                            dg::flag_status(p.status, DG_DEVCHK_INDEX_RANGE);
                         }
+                    } else {
+                        dg::flag_status(p.status, DG_DEVCHK_INDEX_RANGE);
                     }
-                    if (m < MAXA) mfwd[m] = f;
                 }
-                __syncwarp();
-#pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    if (!have[i]) continue;
-                    const int m = lane + 32 * i;
-                    const unsigned long long ne = (unsigned long long)key[i] |
+                mfwd[m] = f;
+                asm volatile("bar.sync 1, 64;" ::: "memory");     // all lookups of step u before its inserts
+                if (have) {
+                    const unsigned long long ne = (unsigned long long)key |
                                                   ((unsigned long long)(((uint32_t)u << 6) | (uint32_t)m) << 32);
-                    const uint32_t hh = slot_hash(key[i] - 1u);
                     bool placed = false;
-                    for (int q = 0; q < PROBES && !placed; ++q) {
-                        unsigned long long* cell = tbl + ((hh + q) & (HSIZE - 1));
-                        for (int tries = 0; tries < 4 && !placed; ++tries) {
-                            const unsigned long long e = *cell;
-                            const uint32_t k = (uint32_t)e;
-                            const int w = (int)((uint32_t)(e >> 32) >> 6);
-                            const bool reusable = (k == 0u) || (k == key[i]) || (w <= s);
-                            if (!reusable) break;
-                            if (atomicCAS(cell, e, ne) == e) placed = true;
+                    for (int tries = 0; tries < 2 * WAYS && !placed; ++tries) {
+                        // target: the key's own cell, else the first reusable one
+                        int target = -1;
+                        unsigned long long old = 0;
+#pragma unroll
+                        for (int q = 0; q < WAYS; ++q) {
+                            const unsigned long long e = bk[q];
+                            if ((uint32_t)e == key) { target = q; old = e; }
                         }
+                        if (target < 0) {
+#pragma unroll
+                            for (int q = WAYS - 1; q >= 0; --q) {
+                                const unsigned long long e = bk[q];
+                                const int w = (int)((uint32_t)(e >> 32) >> 6);
+                                if ((uint32_t)e == 0u || w <= s) { target = q; old = e; }
+                            }
+                        }
+                        if (target < 0) break;
+                        placed = atomicCAS(bk + target, old, ne) == old;
                     }
                     if (!placed) atomicMax(sync_until, u + D - 1);
                 }
@@ -344,7 +353,7 @@ template <typename T, int D>
 int launch_pipe(const PipeParams& p, int lanes, cudaStream_t stream) {
     const int part_bytes = p.Dh * (int)sizeof(T) / p.parts;
     const int cw = part_bytes / 16;
-    const int threads = 32 * (cw + 1);
+    const int threads = 32 * (cw + 2);
     const size_t smem = (size_t)(2 * D) * 64 * (part_bytes + 16) +
                         (size_t)(2 * D + 1) * meta_bytes((int)sizeof(T), p.Dh * (int)sizeof(T)) +
                         2 * (size_t)(4 * D + 16) * sizeof(T) + 16 + HSIZE * 8 + 16;
