@@ -384,9 +384,20 @@ def main():
         e2e = {"value": tokens_per_step / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "steps": k2}
 
+    # verification (outside the timed region): per-rank checksums of the last
+    # step's outputs gathered over NCCL; no collective touches the data path
+    from deltagrid_b200.shard import checksum
+    outs = run_step(ext, w, d)
+    cs = checksum(outs[0])
+    verify = None
     if world > 1:
+        all_cs = [torch.zeros_like(cs) for _ in range(world)]
+        dist.all_gather(all_cs, cs)
+        verify = [[float(x) for x in c.tolist()] for c in all_cs]
         dist.barrier()
         dist.destroy_process_group()
+    else:
+        verify = [[float(x) for x in cs.tolist()]]
     if rank != 0:
         return
 
@@ -419,6 +430,7 @@ def main():
                    "l2": "inputs larger than L2 (no flush)"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
         "clocks": clk.summary(),
+        "verify": {"output_checksums_per_rank": verify},
     }
     print(json.dumps(line))
 
