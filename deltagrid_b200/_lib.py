@@ -34,6 +34,9 @@ _SIGS = {
     "dg_pkm_forward": [_I, _I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P],
     "dg_pkm_step": [_I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P],
     "dg_read_device_status": [_P, _I, _P, _P],
+    "dg_pkm_route": [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
+    "dg_fxp_dense_forward": [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P],
+    "dg_fxp_pkm_forward": [_I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
 }
 _RESTYPE = {"dg_status_string": ctypes.c_char_p}
 

@@ -217,6 +217,25 @@ def pkm_forward(v: torch.Tensor, beta: torch.Tensor, wk: torch.Tensor, wq: torch
     return [out, state_c, saved]
 
 
+def pkm_fused_forward(k: torch.Tensor, q: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
+                      router_k, router_q, q_scale: Optional[torch.Tensor], decay: torch.Tensor,
+                      state: torch.Tensor, top_k: int = 8, grid=None,
+                      save: bool = False) -> List[Optional[torch.Tensor]]:
+    """Routing plus recurrence: what DeltaGridLayer.forward does in Sparse Delta-PKM
+    mode between its projections and out_proj (memory.py:452-464 then :510).
+
+    k, q [B,H,T,Dh]; router_k / router_q two [G_a, Dh] weights each (the layer's
+    axes_proj_k / axes_proj_q); q_scale [H] or None.  Returns [out, state, idx,
+    saved_s_act]; state is updated in place as in pkm_forward.
+    """
+    from .route import pkm_route
+    if grid is not None and tuple(grid) != (router_k[0].shape[0], router_k[1].shape[0]):
+        raise RuntimeError(f"pkm_fused_forward: grid {tuple(grid)} does not match the router weights")
+    wk, wq, idx = pkm_route(k, q, router_k, router_q, top_k, q_scale)
+    out, state_c, saved = pkm_forward(v, beta, wk, wq, idx, decay, state, save)
+    return [out, state_c, idx, saved]
+
+
 def backward(grad_out, grad_s_final, v, beta, wk, wq, decay, s_final, err_saved,
              needs_grad_s_init: bool = False):
     """Dense analytic backward (binding.cpp:223-312)."""

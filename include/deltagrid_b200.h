@@ -139,6 +139,44 @@ int dg_pkm_step(int dtype, int B, int H, int active, int64_t total_slots, int dh
                 const int64_t* idx, const void* decay, int dynamic_decay,
                 void* state, void* out, int32_t* dev_status, void* stream);
 
+/*
+ * Q16.16 fixed-point recurrence core, bit-exact with the reference engine's
+ * integer mode.  Replaces the dense loops of dg_memory_layer_step_fxp
+ * (src/cpp/engine/src/deltagrid_fxp.cpp:380-405) applied once per step.
+ * Lanes-first int32 layouts (one lane = one (context, head) of the engine):
+ *   wk, wq [lanes,T,slots] (wq already multiplied by q_scale, :376-378)
+ *   v, y [lanes,T,dh]; beta, alpha [lanes,T]; state [lanes,slots,dh] (in place)
+ */
+int dg_fxp_dense_forward(int lanes, int T, int slots, int dh, const int32_t* wk, const int32_t* wq,
+                         const int32_t* v, const int32_t* beta, const int32_t* alpha, int32_t* state,
+                         int32_t* y, void* stream);
+
+/*
+ * Q16.16 sparse PKM recurrence core, bit-exact with deltagrid_fxp.cpp:298-326.
+ *   wk, wq, idx [lanes,T,active] int32 (active <= 64); state [lanes,total_slots,dh]
+ *   in place (dh a multiple of 4, 16-byte aligned).  Out-of-range indices are
+ *   skipped and flagged in dev_status (DG_DEVCHK_INDEX_RANGE).
+ */
+int dg_fxp_pkm_forward(int lanes, int T, int active, int64_t total_slots, int dh, const int32_t* wk,
+                       const int32_t* wq, const int32_t* idx, const int32_t* v, const int32_t* beta,
+                       const int32_t* alpha, int32_t* state, int32_t* y, int32_t* dev_status, void* stream);
+
+/*
+ * Two-axis product-key router for Sparse Delta-PKM, fused (one kernel).
+ * Replaces DeltaGridLayer._route_sparse_pkm (src/modules/memory.py:240-289) for two
+ * axes without subspace slicing, and the q_scale multiply of memory.py:453-455.
+ *   k, q [B,H,T,dh] (storage dtype `dtype`, dh <= 128)
+ *   router_k0/router_q0 [g0,dh], router_k1/router_q1 [g1,dh] fp32 (nn.Linear weights)
+ *   q_scale [H] fp32 or NULL;  top_k <= 8
+ *   wk, wq [B,H,T,top_k^2] (storage dtype), idx [B,H,T,top_k^2] int64 = i0*g1 + i1
+ * Scores are fp32 dot products in increasing dh order; equal scores keep the
+ * lower index first (src/cpp/engine/src/deltagrid_math.cpp:155-167).
+ */
+int dg_pkm_route(int dtype, int B, int H, int T, int dh, int g0, int g1, int top_k, const void* k,
+                 const void* q, const float* router_k0, const float* router_k1, const float* router_q0,
+                 const float* router_q1, const float* q_scale, void* wk, void* wq, int64_t* idx,
+                 void* stream);
+
 /* Reads (and clears when `clear`) a device status word; synchronizes `stream`. */
 int dg_read_device_status(int32_t* dev_status, int clear, int32_t* host_value, void* stream);
 
