@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(HERE, "libdeltagrid_b200.so")
 
 DTYPE_F32, DTYPE_F64, DTYPE_F16, DTYPE_BF16 = 0, 1, 2, 3
 ALGO_AUTO, ALGO_SEQUENTIAL, ALGO_CHUNKED_TC = 0, 1, 2
+PKM_AUTO, PKM_ONE_STEP, PKM_PIPELINED, PKM_WARP_SPECIALIZED = 0, 1, 2, 3
 DEVCHK_INDEX_RANGE = 0x1
 
 _P = ctypes.c_void_p
@@ -32,6 +33,7 @@ _SIGS = {
     "dg_dense_step": [_I, _I, _I, _I, _I, _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
                       _P, _I, _I64, _I64, _P, _P, _P, _P],
     "dg_pkm_forward": [_I, _I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P],
+    "dg_pkm_forward_ex": [_I, _I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _P],
     "dg_pkm_step": [_I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P],
     "dg_read_device_status": [_P, _I, _P, _P],
     "dg_pkm_route": [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],

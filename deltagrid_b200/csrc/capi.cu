@@ -35,6 +35,12 @@ bool pkm_pipe_supports(int dtype, int B, int H, int T, int A, int64_t total, int
 int pkm_forward_pipe(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
                      const void* wk, const void* wq, const int64_t* idx, const void* decay, int dynamic_decay,
                      void* state, void* out, int32_t* status, cudaStream_t stream);
+bool pkm_ws_supports(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
+                     const void* wk, const void* wq, const void* idx, const void* decay, int dynamic_decay,
+                     const void* state, const void* saved);
+int pkm_forward_ws(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
+                   const void* wk, const void* wq, const int64_t* idx, const void* decay, int dynamic_decay,
+                   void* state, void* out, int32_t* status, cudaStream_t stream);
 
 }  // namespace dg_host
 
@@ -105,25 +111,47 @@ int dg_dense_step(int dtype, int B, int H, int slots, int dh, const void* v, int
                       static_cast<cudaStream_t>(stream));
 }
 
-int dg_pkm_forward(int dtype, int B, int H, int T, int active, int64_t total_slots, int dh,
-                   const void* v, const void* beta, const void* wk, const void* wq,
-                   const int64_t* idx, const void* decay, int dynamic_decay, void* state, void* out,
-                   void* saved_s_act, int32_t* dev_status, void* stream) {
+int dg_pkm_forward_ex(int dtype, int B, int H, int T, int active, int64_t total_slots, int dh,
+                      const void* v, const void* beta, const void* wk, const void* wq,
+                      const int64_t* idx, const void* decay, int dynamic_decay, void* state, void* out,
+                      void* saved_s_act, int32_t* dev_status, int algo, void* stream) {
     if (!valid_dtype(dtype) || B <= 0 || H <= 0 || T < 0 || active <= 0 || total_slots <= 0 || dh <= 0)
         return DG_ERR_INVALID_ARGUMENT;
+    if (algo < DG_PKM_AUTO || algo > DG_PKM_WARP_SPECIALIZED) return DG_ERR_INVALID_ARGUMENT;
     if (!state) return DG_ERR_INVALID_ARGUMENT;
     if (T == 0) return DG_OK;              // nothing to do; per-step tensors may be empty
     if (!v || !beta || !wk || !wq || !idx || !decay || !out) return DG_ERR_INVALID_ARGUMENT;
     if ((int64_t)B * H > 65535) return DG_ERR_UNSUPPORTED;
-    // pipelined kernel for long sequences it covers; the one-step-at-a-time
-    // kernel for short ones (decode steps), saved rows and other shapes
-    if (T >= 64 && pkm_pipe_supports(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
-                                     dynamic_decay, state, saved_s_act))
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool ws = pkm_ws_supports(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
+                                    dynamic_decay, state, saved_s_act);
+    const bool pipe = pkm_pipe_supports(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
+                                        dynamic_decay, state, saved_s_act);
+    if (algo == DG_PKM_AUTO) {
+        // long sequences: the warp-specialised kernel (16-bit state) or the
+        // pipelined one; decode steps, saved rows and other shapes: one step at a time
+        algo = T < 64 ? DG_PKM_ONE_STEP : ws ? DG_PKM_WARP_SPECIALIZED : pipe ? DG_PKM_PIPELINED : DG_PKM_ONE_STEP;
+    }
+    if (algo == DG_PKM_WARP_SPECIALIZED) {
+        if (!ws) return DG_ERR_UNSUPPORTED;
+        return pkm_forward_ws(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
+                              dynamic_decay, state, out, dev_status, s);
+    }
+    if (algo == DG_PKM_PIPELINED) {
+        if (!pipe) return DG_ERR_UNSUPPORTED;
         return pkm_forward_pipe(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
-                                dynamic_decay, state, out, dev_status, static_cast<cudaStream_t>(stream));
+                                dynamic_decay, state, out, dev_status, s);
+    }
     return pkm_forward_v1(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
-                          dynamic_decay, state, out, saved_s_act, dev_status,
-                          static_cast<cudaStream_t>(stream));
+                          dynamic_decay, state, out, saved_s_act, dev_status, s);
+}
+
+int dg_pkm_forward(int dtype, int B, int H, int T, int active, int64_t total_slots, int dh,
+                   const void* v, const void* beta, const void* wk, const void* wq,
+                   const int64_t* idx, const void* decay, int dynamic_decay, void* state, void* out,
+                   void* saved_s_act, int32_t* dev_status, void* stream) {
+    return dg_pkm_forward_ex(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
+                             dynamic_decay, state, out, saved_s_act, dev_status, DG_PKM_AUTO, stream);
 }
 
 int dg_pkm_step(int dtype, int B, int H, int active, int64_t total_slots, int dh, const void* v,

@@ -28,12 +28,6 @@ __device__ __forceinline__ int64_t shfl_xor64(int64_t v, int o) {
     const int hi = __shfl_xor_sync(DG_FULL_MASK, (int)(v >> 32), o);
     return (int64_t)(((uint64_t)(uint32_t)hi << 32) | (uint32_t)lo);
 }
-__device__ __forceinline__ int64_t shfl64(int64_t v, int src) {
-    const int lo = __shfl_sync(DG_FULL_MASK, (int)(v & 0xffffffff), src);
-    const int hi = __shfl_sync(DG_FULL_MASK, (int)(v >> 32), src);
-    return (int64_t)(((uint64_t)(uint32_t)hi << 32) | (uint32_t)lo);
-}
-
 struct FxpDenseParams {
     const int32_t* wk;
     const int32_t* wq;

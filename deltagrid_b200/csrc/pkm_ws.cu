@@ -1,0 +1,643 @@
+// pkm_ws.cu -- warp-specialised Sparse Delta-PKM recurrence for 16-bit state.
+//
+// Same math as pkm_seq.cu (src/cpp/delta_kernel.cu:885-920): per lane and step,
+// gather the `active` rows S[idx_t], y = wq.s and pred = wk.s over the rows,
+// r = beta (v - pred), scatter S[idx_t] = cast(alpha s + (r) wk), rows rounded to
+// the storage dtype every step.
+//
+// One CTA per (lane, part of the row); four roles run concurrently on a ring of
+// R = 2D row slots, synchronised by mbarriers:
+//   hash (2 warps)  loads the metadata (idx, wk, wq, v, beta, alpha) 16 steps at
+//       a time and, for every row of those steps, finds the last earlier step
+//       inside the window [t-D+1, t-1] that wrote the same slot.  The steps of a
+//       chunk are resolved step by step with a chained table: 4096 heads hold
+//       the latest writer per hash of the slot, links the writer each one
+//       displaced, and a lookup walks the chain newest first, checking each
+//       writer's slot index in the resident metadata, until it leaves the
+//       window.  The result is a per-row code: gather, forward from (step,
+//       position), or no row.  A walk longer than 16 hops sends the step to
+//       sync mode: all its rows are gathered after every earlier update
+//       (exact, slow).
+//   gather (2 warps)  per step t, D steps ahead of the update: row-coalesced
+//       cp.async (8 lanes per 128 bytes) of the rows coded "gather" into the
+//       step's ring slot.
+//   gemv (PB/32 warps, 16 columns each)  per step s: y and pred of its columns
+//       as a tensor-core GEMV, mma.sync m16n8k16 with A = the gathered rows
+//       transposed (ldmatrix.trans, one row address per lane, so forwarded rows
+//       need no copy; columns are the M dimension) and B = [wq, wk] (2 of 8 N
+//       columns used), four MMAs for 64 rows; writes r = beta (v - pred) to
+//       shared memory and stages y for coalesced stores.
+//   update (PB/16 warps)  per step s: loads its gathered rows before r is ready,
+//       then the new rows (fp32 math, packed f32x2, one rounding), written to
+//       the ring slot (for forwarding) and to global memory with coalesced
+//       16-byte stores.
+// The update of step s overlaps the GEMV of step s+1 unless s+1 reads a row
+// that s writes, in which case the GEMV waits for that update.
+//
+// Ordering argument: a row gathered from global memory for step t has its last
+// writer w <= t-D, and the gather is issued only after the update of step t-D
+// has completed (mbarrier release/acquire); a row whose last writer is in the
+// window is read from the writer's ring slot, which the slot's next gather (for
+// step w+R, issued after update w+R-D >= w+D) cannot overwrite before every
+// reader (steps <= w+D-1) is done.
+#include "dg_common.cuh"
+#include "tc_util.cuh"
+
+namespace {
+
+constexpr int MAXA = 64;
+constexpr int CHS = 16;                 // steps per metadata chunk
+constexpr int NC = 3;                   // metadata chunks resident
+constexpr int HBITS = 12;
+constexpr int HHEADS = 1 << HBITS;      // chain heads of the hazard table
+constexpr int CR = 16;                  // steps of chain links kept (>= window)
+constexpr int MAXHOP = 16;              // longest chain walk before a step falls back to sync mode
+constexpr int NHASH = 64;               // hash threads (two warps)
+constexpr int NGATH = 64;               // gather threads (two warps)
+constexpr int ROLE_WARPS = 4;           // hash 2, gather 2 (then PB/32 GEMV warps, PB/16 update warps)
+
+struct WsParams {
+    const void* v;
+    const void* beta;
+    const void* wk;
+    const void* wq;
+    const int64_t* idx;
+    const void* decay;
+    void* state;
+    void* out;
+    int32_t* status;
+    int H, T, A, Dh, parts;
+    int64_t total;
+    int dynamic_decay;
+};
+
+struct MetaLayout {
+    int idx, wk, wq, v, beta, alpha, code, sync, bytes;
+};
+
+__host__ __device__ inline MetaLayout meta_layout(int A, int Dh) {
+    MetaLayout L;
+    int o = 0;
+    L.idx = o;   o += CHS * A * 8;
+    L.wk = o;    o += CHS * A * 2;
+    L.wq = o;    o += CHS * A * 2;
+    L.v = o;     o += CHS * Dh * 2;
+    L.beta = o;  o += 32;
+    L.alpha = o; o += 32;
+    L.code = o;  o += CHS * 64 * 2;
+    L.sync = o;  o += CHS;
+    L.bytes = (o + 127) / 128 * 128;
+    return L;
+}
+
+// shared-memory carve-up (same arithmetic on host and device)
+struct SmemLayout {
+    int bars, misc, table, rows, zrow, rbuf, ystage, meta, total;
+};
+__host__ __device__ inline SmemLayout smem_layout(int PB, int D, int A, int Dh) {
+    SmemLayout L;
+    const int R = 2 * D, RS = PB + 16;
+    int o = 0;
+    L.bars = o;   o += 512;
+    L.misc = o;   o += 16;
+    L.table = o;  o += HHEADS * 4 + CR * 64 * 4;
+    L.rows = o;   o += R * 64 * RS;
+    L.zrow = o;   o += RS;
+    L.rbuf = o;   o += 2 * 64 * 4;
+    L.ystage = o; o += CHS * PB;
+    o = (o + 127) / 128 * 128;
+    L.meta = o;   o += NC * meta_layout(A, Dh).bytes;
+    L.total = o;
+    return L;
+}
+
+// chain head of a slot: a 32-bit integer mix (xor-shift / multiply) so that
+// the lattice-shaped slot sets of Kronecker routing spread over the heads
+__device__ __forceinline__ uint32_t slot_head(uint32_t x) {
+    x ^= x >> 16;
+    x *= 0x85ebca6bu;
+    x ^= x >> 13;
+    x *= 0xc2b2ae35u;
+    x ^= x >> 16;
+    return x >> (32 - HBITS);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void hash_bar() { asm volatile("bar.sync 1, 64;" ::: "memory"); }
+// barrier over the 64 hash threads that also ORs a predicate across them
+__device__ __forceinline__ bool hash_bar_or(bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n barrier.cta.red.or.pred q, 1, 64, p;\n"
+        " selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)pred)
+        : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// one poll that lets the hardware park the warp until the phase completes (or
+// ~1 ms passes), so waiting warps take no issue slots
+__device__ __forceinline__ bool mbar_try_wait_long(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(tc::smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "memory");
+    return ok != 0;
+}
+// Bounded mbarrier wait: gives up when another role aborted or after 2 s of
+// wall time, flagging DG_DEVCHK_TIMEOUT.
+__device__ __forceinline__ bool ws_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                        int32_t* status) {
+    if (mbar_try_wait_long(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait_long(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > 2000000000ull) break;
+    }
+    dg::flag_status(status, DG_DEVCHK_TIMEOUT);
+    *abort_flag = 1;
+    return false;
+}
+
+template <typename T> struct MmaOp;
+template <> struct MmaOp<__half> {
+    __device__ __forceinline__ static void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+};
+template <> struct MmaOp<__nv_bfloat16> {
+    __device__ __forceinline__ static void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+};
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// two storage values <-> two floats
+__device__ __forceinline__ float2 unpack2(uint32_t u, __half) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&u));
+}
+__device__ __forceinline__ float2 unpack2(uint32_t u, __nv_bfloat16) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b, __half) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// (x0, x1) * (y0, y1) and a * (x0, x1) + (c0, c1), each element rounded once (IEEE RN)
+__device__ __forceinline__ unsigned long long f2pack(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float2 f2unpack(unsigned long long r) {
+    float2 f;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(f.x), "=f"(f.y) : "l"(r));
+    return f;
+}
+__device__ __forceinline__ unsigned long long mul_f32x2(unsigned long long x, unsigned long long y) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(x), "l"(y));
+    return d;
+}
+__device__ __forceinline__ unsigned long long fma_f32x2(unsigned long long a, unsigned long long b,
+                                                        unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+template <typename T, int PB, int D>
+__global__ void __launch_bounds__(32 * (ROLE_WARPS + PB / 32 + PB / 16)) pkm_ws_kernel(WsParams p) {
+    constexpr int CH = PB / 16;          // 16-byte chunks per row part = N-tiles of 8 columns
+    constexpr int NU = CH;               // update warps: two (row, chunk) pairs per thread
+    constexpr int NM = PB / 32;          // GEMV warps: 16 columns each
+    constexpr int RS = PB + 16;          // padded row stride: conflict-free ldmatrix / 16-byte accesses
+    constexpr int R = 2 * D;
+    constexpr int SLOT = 64 * RS;
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    const SmemLayout SL = smem_layout(PB, D, p.A, p.Dh);
+    const MetaLayout ML = meta_layout(p.A, p.Dh);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + SL.bars);   // [R] rows of step landed
+    uint64_t* done = full + R;                                      // [R] update of step complete
+    uint64_t* rdy = done + R;                                       // [2] r of step ready
+    uint64_t* rfree = rdy + 2;                                      // [2] r buffer consumed
+    uint64_t* mfull = rfree + 2;                                    // [NC] metadata chunk landed
+    uint64_t* hready = mfull + NC;                                  // [NC] row codes of chunk ready
+    uint64_t* mfree = hready + NC;                                  // [NC] chunk's last update done
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SL.misc);
+    uint32_t* heads = reinterpret_cast<uint32_t*>(smem + SL.table);           // [HHEADS] latest writer per head
+    uint32_t* links = heads + HHEADS;                                         // [CR][64] next (older) writer
+    uint8_t* rows = smem + SL.rows;
+    uint8_t* zrow = smem + SL.zrow;
+    float* rbuf = reinterpret_cast<float*>(smem + SL.rbuf);
+    uint8_t* ystage = smem + SL.ystage;
+    uint8_t* meta = smem + SL.meta;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int lane_bh = blockIdx.y, part = blockIdx.x;
+    const int A = p.A, Dh = p.Dh, T_ = p.T;
+    const int64_t total = p.total;
+    const int64_t lt0 = (int64_t)lane_bh * T_;
+    const int64_t row_bytes = (int64_t)Dh * 2;
+    const int nchunks = (T_ + CHS - 1) / CHS;
+    uint8_t* gstate = reinterpret_cast<uint8_t*>(p.state) + (int64_t)lane_bh * total * row_bytes + (int64_t)part * PB;
+
+    for (int i = tid; i < RS / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(zrow)[i] = 0u;
+    for (int i = tid; i < HHEADS; i += blockDim.x) heads[i] = 0u;
+    if (tid == 0) {
+        for (int i = 0; i < R; ++i) {
+            tc::mbar_init(full + i, 2 * NGATH);
+            tc::mbar_init(done + i, NU * 32);
+        }
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(rdy + i, NM * 32);
+            tc::mbar_init(rfree + i, NU * 32);
+        }
+        for (int i = 0; i < NC; ++i) {
+            tc::mbar_init(mfull + i, NHASH);
+            tc::mbar_init(hready + i, NHASH);
+            tc::mbar_init(mfree + i, NU * 32);
+        }
+        *abort_flag = 0;
+    }
+    __syncthreads();
+
+    if (warp < 2) {
+        // ================================ hash ================================
+        const int ht = tid;                              // 0..63
+        const T* gwk = static_cast<const T*>(p.wk);
+        const T* gwq = static_cast<const T*>(p.wq);
+        const T* gv = static_cast<const T*>(p.v);
+        const T* gbeta = static_cast<const T*>(p.beta);
+        const T* gdecay = static_cast<const T*>(p.decay);
+        auto copy = [&](uint8_t* dst, const void* src, int nbytes) {
+            const uint32_t d0 = tc::smem_u32(dst);
+            const uint8_t* s0 = static_cast<const uint8_t*>(src);
+            for (int i = ht; i < nbytes / 16; i += NHASH) cp_async16(d0 + 16 * i, s0 + 16 * i);
+        };
+        auto load_chunk = [&](int c) {
+            const int t0 = c * CHS;
+            const int n = min(CHS, T_ - t0);              // a multiple of 8
+            uint8_t* mc = meta + (c % NC) * ML.bytes;
+            const int64_t bt = lt0 + t0;
+            copy(mc + ML.idx, p.idx + bt * A, n * A * 8);
+            copy(mc + ML.wk, gwk + bt * A, n * A * 2);
+            copy(mc + ML.wq, gwq + bt * A, n * A * 2);
+            copy(mc + ML.v, gv + bt * Dh, n * Dh * 2);
+            copy(mc + ML.beta, gbeta + bt, n * 2);
+            if (p.dynamic_decay) copy(mc + ML.alpha, gdecay + bt, n * 2);
+            cp_async_arrive_noinc(mfull + (c % NC));
+        };
+        load_chunk(0);
+        if (nchunks > 1) load_chunk(1);
+        for (int c = 0; c < nchunks; ++c) {
+            bool ok = ws_wait(mfull + (c % NC), (c / NC) & 1, abort_flag, p.status);
+            if (hash_bar_or(!ok)) break;
+            const int t0 = c * CHS;
+            const int n = min(CHS, T_ - t0);
+            uint8_t* mc = meta + (c % NC) * ML.bytes;
+            const int64_t* midx = reinterpret_cast<const int64_t*>(mc + ML.idx);
+            int16_t* code = reinterpret_cast<int16_t*>(mc + ML.code);
+            uint8_t* sync = mc + ML.sync;
+            // Steps in order; thread ht owns row ht.  A head holds the latest writer
+            // (step + 1) << 6 | position of any slot hashing there, a link the writer
+            // it displaced, so a chain lists writers newest first; a lookup walks it
+            // until it leaves the window and checks each writer's slot index.
+            bool stop = false;
+            for (int ts = 0; ts < n; ++ts) {
+                const int t = t0 + ts;
+                int cd = -2;
+                uint32_t hd = 0, ent = 0;
+                bool incomplete = false;
+                if (ht < A) {
+                    const int64_t x = midx[ts * A + ht];
+                    if (x >= 0 && x < total) {
+                        hd = slot_head((uint32_t)x);
+                        ent = ((uint32_t)(t + 1) << 6) | (uint32_t)ht;
+                        cd = -1;
+                        uint32_t e = heads[hd];
+                        int hop = 0;
+                        for (; hop < MAXHOP && e != 0u; ++hop) {
+                            const int w = (int)(e >> 6) - 1, pos = (int)(e & 63);
+                            if (w < t - (D - 1)) break;               // older than the window: done
+                            const uint8_t* mw = meta + ((w / CHS) % NC) * ML.bytes;
+                            if (reinterpret_cast<const int64_t*>(mw + ML.idx)[(w % CHS) * A + pos] == x) {
+                                cd = ((t - w) << 6) | pos;
+                                break;
+                            }
+                            e = links[(w % CR) * 64 + pos];
+                        }
+                        incomplete = hop == MAXHOP;
+                    } else {
+                        dg::flag_status(p.status, DG_DEVCHK_INDEX_RANGE);
+                    }
+                }
+                // every lookup of step t before its inserts; a step whose walk gave up
+                // gathers all rows after every earlier update
+                const bool lost = hash_bar_or(incomplete);
+                if (lost && cd >= 0) cd = -1;
+                code[ts * 64 + ht] = (int16_t)cd;
+                if (ht == 0) sync[ts] = lost ? 1 : 0;
+                if (ent != 0u) links[(t % CR) * 64 + ht] = atomicExch(heads + hd, ent);
+                if (hash_bar_or(*abort_flag != 0)) { stop = true; break; }   // inserts before the next lookups
+            }
+            if (stop) break;
+            mbar_arrive(hready + (c % NC));
+            // chunk c+1 was loaded ahead; chunk c+2 reuses the buffer of chunk c-1
+            if (c + 2 < nchunks) {
+                if (c >= 1) ok = ws_wait(mfree + ((c - 1) % NC), ((c - 1) / NC) & 1, abort_flag, p.status);
+                if (hash_bar_or(!ok)) break;
+                load_chunk(c + 2);
+            }
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp < 4) {
+        // =============================== gather ===============================
+        const int gt = tid - 64;                          // 0..63
+        for (int t = 0; t < T_; ++t) {
+            const int sl = t % R;
+            const int c = t / CHS, ts = t % CHS;
+            bool ok = true;
+            if (ts == 0) ok = ws_wait(hready + (c % NC), (c / NC) & 1, abort_flag, p.status);
+            if (ok && t >= D) ok = ws_wait(done + ((t - D) % R), ((t - D) / R) & 1, abort_flag, p.status);
+            if (!ok) break;
+            const uint8_t* mc = meta + (c % NC) * ML.bytes;
+            const int64_t* midx = reinterpret_cast<const int64_t*>(mc + ML.idx) + ts * A;
+            const int16_t* code = reinterpret_cast<const int16_t*>(mc + ML.code) + ts * 64;
+            if (mc[ML.sync + ts] && t >= 1) {            // hazard table lost entries: wait for every earlier update
+                if (!ws_wait(done + ((t - 1) % R), ((t - 1) / R) & 1, abort_flag, p.status)) break;
+            }
+            const uint32_t slot = tc::smem_u32(rows + sl * SLOT);
+            // all addresses first, then the copies
+            uint32_t dst[CH];
+            const uint8_t* src[CH];
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+                const int q = j * NGATH + gt;
+                const int m = q / CH, cc = q % CH;
+                dst[j] = 0u;
+                src[j] = nullptr;
+                if (code[m] == -1) {
+                    dst[j] = slot + m * RS + 16 * cc;
+                    src[j] = gstate + midx[m] * row_bytes + 16 * cc;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < CH; ++j)
+                if (src[j]) cp_async16(dst[j], src[j]);
+            cp_async_arrive_noinc(full + sl);
+            mbar_arrive(full + sl);
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp < ROLE_WARPS + NM) {
+        // ============================ tensor-core GEMV ============================
+        const int mw = warp - ROLE_WARPS;                      // columns mw*16 .. mw*16+15 of the part
+        const int g = lane >> 2, tig = lane & 3;
+        const int kk = ((lane >> 4) & 1) * 8 + (lane & 7);     // ldmatrix row of this lane in a K block
+        const uint32_t colb = (uint32_t)(mw * 32 + ((lane >> 3) & 1) * 16);
+        const uint32_t rows_u = tc::smem_u32(rows);
+        const uint32_t zrow_u = tc::smem_u32(zrow);
+        T* gout = static_cast<T*>(p.out);
+        for (int s = 0; s < T_; ++s) {
+            const int sl = s % R;
+            const int cn = s / CHS, ts = s % CHS;
+            const uint8_t* mc = meta + (cn % NC) * ML.bytes;
+            bool ok = ws_wait(full + sl, (s / R) & 1, abort_flag, p.status);
+            if (!__all_sync(DG_FULL_MASK, ok)) break;
+            const int16_t* fw = reinterpret_cast<const int16_t*>(mc + ML.code) + ts * 64;
+            const int c0 = fw[lane], c1 = fw[lane + 32];
+            int dmin = 64;
+            if (c0 >= 0) dmin = c0 >> 6;
+            if (c1 >= 0) dmin = min(dmin, c1 >> 6);
+            dmin = __reduce_min_sync(DG_FULL_MASK, dmin);
+            if (dmin < 64) {                          // a forwarded row: its writer's update must be complete
+                const int w = s - dmin;
+                ok = ws_wait(done + (w % R), (w / R) & 1, abort_flag, p.status);
+            }
+            if (ok && s >= 2) ok = ws_wait(rfree + (s & 1), ((s - 2) >> 1) & 1, abort_flag, p.status);
+            if (!__all_sync(DG_FULL_MASK, ok)) break;
+
+            // B = [wq, wk] as the first two of 8 N columns: lanes of group 0 hold wq, group 1 wk
+            const uint16_t* wsrc = reinterpret_cast<const uint16_t*>(mc + (g == 0 ? ML.wq : ML.wk)) + ts * A;
+            const int nkb = (A + 15) >> 4;
+            uint32_t b[4][2], base[4];
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int i0 = kb * 16 + h * 8 + tig * 2;
+                    const uint32_t lo = (g < 2 && i0 < A) ? wsrc[i0] : 0u;
+                    const uint32_t hi = (g < 2 && i0 + 1 < A) ? wsrc[i0 + 1] : 0u;
+                    b[kb][h] = lo | (hi << 16);
+                }
+                const int k = kb * 16 + kk;
+                const int cd = fw[k];
+                uint32_t bs;
+                if (cd == -1) {
+                    bs = rows_u + sl * SLOT + k * RS;
+                } else if (cd < 0) {
+                    bs = zrow_u;
+                } else {
+                    const int w = s - (cd >> 6);
+                    bs = rows_u + (w % R) * SLOT + (cd & 63) * RS;
+                }
+                base[kb] = bs + colb;
+            }
+            uint32_t a[4][4];
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb)
+                if (kb < nkb) ldsm_x4_trans(base[kb], a[kb][0], a[kb][1], a[kb][2], a[kb][3]);
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb)
+                if (kb < nkb) MmaOp<T>::run(acc, a[kb], b[kb][0], b[kb][1]);
+            // lanes with tig == 0: acc = {y, pred} of column g and {y, pred} of column g + 8
+            if (tig == 0) {
+                const int col0 = mw * 16 + g;
+                const float bta = dg::to_f(reinterpret_cast<const T*>(mc + ML.beta)[ts]);
+                const T* mv = reinterpret_cast<const T*>(mc + ML.v) + ts * Dh + part * (PB / 2);
+                T* yrow = reinterpret_cast<T*>(ystage + ts * PB);
+                float* rb = rbuf + (s & 1) * 64;
+                yrow[col0] = dg::from_f<T>(acc[0]);
+                yrow[col0 + 8] = dg::from_f<T>(acc[2]);
+                rb[col0] = bta * (dg::to_f(mv[col0]) - acc[1]);
+                rb[col0 + 8] = bta * (dg::to_f(mv[col0 + 8]) - acc[3]);
+            }
+            __syncwarp();
+            mbar_arrive(rdy + (s & 1));
+            if (ts == CHS - 1 || s == T_ - 1) {         // flush this warp's 32 bytes of y per step
+                const int n = ts + 1;
+                const int64_t bt0 = lt0 + (s - ts);
+                for (int i = lane; i < 2 * n; i += 32) {
+                    const int jj = i >> 1, hh = i & 1;
+                    const uint4 val = *reinterpret_cast<const uint4*>(ystage + jj * PB + mw * 32 + hh * 16);
+                    dg::st16(reinterpret_cast<uint8_t*>(gout + (bt0 + jj) * Dh) + part * PB + mw * 32 + hh * 16, val);
+                }
+                __syncwarp();
+            }
+        }
+    } else {
+        // ================================ update ================================
+        const int ut = tid - 32 * (ROLE_WARPS + NM);   // 0 .. NU*32-1
+        const int cc = ut % CH;                      // this thread's 16-byte chunk (8 columns)
+        const int m0 = ut / CH;                      // rows m0 and m0 + 32
+        const float alpha_static = p.dynamic_decay ? 1.f : dg::to_f(static_cast<const T*>(p.decay)[lane_bh % p.H]);
+        for (int s = 0; s < T_; ++s) {
+            const int sl = s % R;
+            bool ok = ws_wait(full + sl, (s / R) & 1, abort_flag, p.status);
+            if (!ok) break;
+            const int cn = s / CHS, ts = s % CHS;
+            const uint8_t* mc = meta + (cn % NC) * ML.bytes;
+            const int16_t* fw = reinterpret_cast<const int16_t*>(mc + ML.code) + ts * 64;
+            const int64_t* midx = reinterpret_cast<const int64_t*>(mc + ML.idx) + ts * A;
+            const T* mwk = reinterpret_cast<const T*>(mc + ML.wk) + ts * A;
+            uint8_t* slot = rows + sl * SLOT;
+            // everything that does not depend on r: codes, slots, keys, gathered rows
+            int cd[2];
+            int64_t x[2];
+            float wkv[2];
+            uint4 raw[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int m = m0 + 32 * j;
+                cd[j] = fw[m];
+                x[j] = 0; wkv[j] = 0.f; raw[j] = make_uint4(0, 0, 0, 0);
+                if (cd[j] != -2) {
+                    x[j] = midx[m];
+                    wkv[j] = dg::to_f(mwk[m]);
+                }
+                if (cd[j] == -1) raw[j] = *reinterpret_cast<const uint4*>(slot + m * RS + cc * 16);
+            }
+            const float al = p.dynamic_decay ? dg::to_f(reinterpret_cast<const T*>(mc + ML.alpha)[ts]) : alpha_static;
+            const unsigned long long al2 = f2pack(al, al);
+            ok = ws_wait(rdy + (s & 1), (s >> 1) & 1, abort_flag, p.status);
+            if (!ok) break;
+            const float4* rb4 = reinterpret_cast<const float4*>(rbuf + (s & 1) * 64 + cc * 8);
+            const float4 ra = rb4[0], rbv = rb4[1];
+            mbar_arrive(rfree + (s & 1));
+            const float br[8] = {ra.x, ra.y, ra.z, ra.w, rbv.x, rbv.y, rbv.z, rbv.w};
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                if (cd[j] == -2) continue;               // no row (m >= A or index out of range)
+                const int m = m0 + 32 * j;
+                if (cd[j] >= 0) {                        // forwarded: the writer finished before r was ready
+                    const int w = s - (cd[j] >> 6);
+                    raw[j] = *reinterpret_cast<const uint4*>(rows + (w % R) * SLOT + (cd[j] & 63) * RS + cc * 16);
+                }
+                const uint32_t in[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+                uint32_t o[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 sv = unpack2(in[i], T());
+                    const unsigned long long u = mul_f32x2(f2pack(br[2 * i], br[2 * i + 1]), f2pack(wkv[j], wkv[j]));
+                    const float2 nv = f2unpack(fma_f32x2(al2, f2pack(sv.x, sv.y), u));
+                    o[i] = pack2(nv.x, nv.y, T());
+                }
+                const uint4 nv4 = make_uint4(o[0], o[1], o[2], o[3]);
+                *reinterpret_cast<uint4*>(slot + m * RS + cc * 16) = nv4;
+                dg::st16(gstate + x[j] * row_bytes + cc * 16, nv4);
+            }
+            mbar_arrive(done + sl);
+            if (ts == CHS - 1 || s == T_ - 1) mbar_arrive(mfree + (cn % NC));
+        }
+    }
+}
+
+template <typename T, int PB, int D>
+int launch_ws(const WsParams& p, int lanes, cudaStream_t stream) {
+    const SmemLayout SL = smem_layout(PB, D, p.A, p.Dh);
+    auto kern = pkm_ws_kernel<T, PB, D>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SL.total);
+    if (e != cudaSuccess) return dg_host::record_cuda_error(e);
+    dim3 grid(p.parts, lanes);
+    kern<<<grid, 32 * (ROLE_WARPS + PB / 32 + PB / 16), SL.total, stream>>>(p);
+    return dg_host::check_launch();
+}
+
+constexpr int kDepthFull = 7;     // window depth for 128-byte row parts (ring fits 227 KB)
+constexpr int kDepthHalf = 8;     // for 64-byte row parts
+
+// row part bytes for a call: 128 (full 64-column fp16 rows), or 64 (two CTAs per lane)
+int ws_part_bytes(int B, int H, int Dh) {
+    const int rb = Dh * 2;
+    const int lanes = B * H;
+    if (rb == 128) return lanes < 120 ? 64 : 128;
+    if (rb == 64) return 64;
+    if (rb == 256) return 128;
+    return 0;
+}
+
+}  // namespace
+
+namespace dg_host {
+
+bool pkm_ws_supports(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
+                     const void* wk, const void* wq, const void* idx, const void* decay, int dynamic_decay,
+                     const void* state, const void* saved) {
+    if (saved) return false;
+    if (dtype != DG_DTYPE_F16 && dtype != DG_DTYPE_BF16) return false;
+    if (A < 1 || A > MAXA || T < 1 || T % 8 != 0) return false;
+    if (total >= (int64_t)0x7fffffff - 1 || T >= (1 << 25)) return false;
+    const int PB = ws_part_bytes(B, H, Dh);
+    if (PB == 0) return false;
+    const int D = PB == 128 ? kDepthFull : kDepthHalf;
+    if (smem_layout(PB, D, A, Dh).total > 232448) return false;
+    const uintptr_t al = (uintptr_t)v | (uintptr_t)beta | (uintptr_t)wk | (uintptr_t)wq | (uintptr_t)idx |
+                         (uintptr_t)state | (dynamic_decay ? (uintptr_t)decay : 0);
+    return (al & 15) == 0;
+}
+
+int pkm_forward_ws(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
+                   const void* wk, const void* wq, const int64_t* idx, const void* decay, int dynamic_decay,
+                   void* state, void* out, int32_t* status, cudaStream_t stream) {
+    const int PB = ws_part_bytes(B, H, Dh);
+    const int parts = Dh * 2 / PB;
+    WsParams p{v, beta, wk, wq, idx, decay, state, out, status, H, T, A, Dh, parts, total, dynamic_decay};
+    const int lanes = B * H;
+    if (dtype == DG_DTYPE_F16)
+        return PB == 128 ? launch_ws<__half, 128, kDepthFull>(p, lanes, stream)
+                         : launch_ws<__half, 64, kDepthHalf>(p, lanes, stream);
+    if (dtype == DG_DTYPE_BF16)
+        return PB == 128 ? launch_ws<__nv_bfloat16, 128, kDepthFull>(p, lanes, stream)
+                         : launch_ws<__nv_bfloat16, 64, kDepthHalf>(p, lanes, stream);
+    return DG_ERR_UNSUPPORTED;
+}
+
+}  // namespace dg_host

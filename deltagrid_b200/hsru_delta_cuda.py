@@ -193,6 +193,13 @@ def pkm_forward(v: torch.Tensor, beta: torch.Tensor, wk: torch.Tensor, wq: torch
     Returns [out, state, saved_s_act]; saved_s_act [B,H,T,A,Dh] holds the rows
     gathered at each step when save_for_backward, else None.
     """
+    return pkm_forward_algo(v, beta, wk, wq, active_idx, decay, state, save_for_backward, _lib.PKM_AUTO)
+
+
+def pkm_forward_algo(v: torch.Tensor, beta: torch.Tensor, wk: torch.Tensor, wq: torch.Tensor,
+                     active_idx: torch.Tensor, decay: torch.Tensor, state: torch.Tensor,
+                     save_for_backward: bool = False, algo: int = 0) -> List[Optional[torch.Tensor]]:
+    """pkm_forward with an explicit kernel (dg_pkm_algo); raises if it does not cover the call."""
     for t, n in ((v, "v"), (beta, "beta"), (wk, "wk"), (wq, "wq"), (active_idx, "active_idx"),
                  (decay, "decay"), (state, "state")):
         _check_cuda(t, n)
@@ -210,10 +217,10 @@ def pkm_forward(v: torch.Tensor, beta: torch.Tensor, wk: torch.Tensor, wq: torch
              if save_for_backward else None)
     dynamic = 1 if decay_c.dim() > 1 else 0
     with torch.cuda.device(v_c.device):
-        _lib.call("dg_pkm_forward", code, B, H, T, A, total, Dh, v_c.data_ptr(), beta_c.data_ptr(),
+        _lib.call("dg_pkm_forward_ex", code, B, H, T, A, total, Dh, v_c.data_ptr(), beta_c.data_ptr(),
                   wk_c.data_ptr(), wq_c.data_ptr(), idx_c.data_ptr(), decay_c.data_ptr(), dynamic,
                   state_c.data_ptr(), out.data_ptr(), saved.data_ptr() if saved is not None else None,
-                  _status_word(v_c.device).data_ptr(), _stream(v_c))
+                  _status_word(v_c.device).data_ptr(), int(algo), _stream(v_c))
     return [out, state_c, saved]
 
 

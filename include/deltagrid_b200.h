@@ -51,6 +51,14 @@ typedef enum dg_dense_algo {
     DG_DENSE_CHUNKED_TC = 2  /* chunkwise WY/UT form on tcgen05 (f16/bf16, Dh = 64) */
 } dg_dense_algo;
 
+/* PKM sequence-forward kernel selector for dg_pkm_forward_ex */
+typedef enum dg_pkm_algo {
+    DG_PKM_AUTO = 0,             /* warp-specialised, else pipelined, else one step at a time */
+    DG_PKM_ONE_STEP = 1,         /* one CTA per lane and part, one step per iteration (any dtype) */
+    DG_PKM_PIPELINED = 2,        /* rows gathered D steps ahead by the column warps (f16/bf16/f32) */
+    DG_PKM_WARP_SPECIALIZED = 3  /* producer / tensor-core GEMV / update warps (f16/bf16) */
+} dg_pkm_algo;
+
 /* bits written into the optional device status word by kernel self-checks */
 #define DG_DEVCHK_INDEX_RANGE 0x1 /* a slot index was outside [0, total_slots) */
 #define DG_DEVCHK_DUPLICATE 0x2   /* reserved */
@@ -125,6 +133,14 @@ int dg_pkm_forward(int dtype, int B, int H, int T, int active, int64_t total_slo
                    const int64_t* idx, const void* decay, int dynamic_decay,
                    void* state, void* out, void* saved_s_act, int32_t* dev_status,
                    void* stream);
+
+/* dg_pkm_forward with an explicit kernel choice (dg_pkm_algo); DG_ERR_UNSUPPORTED
+ * when the chosen kernel does not cover the call. */
+int dg_pkm_forward_ex(int dtype, int B, int H, int T, int active, int64_t total_slots, int dh,
+                      const void* v, const void* beta, const void* wk, const void* wq,
+                      const int64_t* idx, const void* decay, int dynamic_decay,
+                      void* state, void* out, void* saved_s_act, int32_t* dev_status,
+                      int algo, void* stream);
 
 /*
  * Sparse Delta-PKM single decode step, state updated in place.
