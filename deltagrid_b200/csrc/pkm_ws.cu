@@ -21,7 +21,8 @@
 //   gather (2 warps)  per step t, D steps ahead of the update: row-coalesced
 //       cp.async (8 lanes per 128 bytes) of the rows coded "gather" into the
 //       step's ring slot.
-//   gemv (PB/32 warps, 16 columns each)  per step s: y and pred of its columns
+//   gemv (two groups of PB/32 warps, 16 columns each, alternate steps)
+//       per step s: y and pred of its columns
 //       as a tensor-core GEMV, mma.sync m16n8k16 with A = the gathered rows
 //       transposed (ldmatrix.trans, one row address per lane, so forwarded rows
 //       need no copy; columns are the M dimension) and B = [wq, wk] (2 of 8 N
@@ -124,6 +125,10 @@ __device__ __forceinline__ uint32_t slot_head(uint32_t x) {
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+// 16-byte copy of which only the first `src_bytes` (16 or 0) are read; the rest is zero-filled
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
 __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
@@ -243,10 +248,10 @@ __device__ __forceinline__ unsigned long long fma_f32x2(unsigned long long a, un
 }
 
 template <typename T, int PB, int D>
-__global__ void __launch_bounds__(32 * (ROLE_WARPS + PB / 32 + PB / 16)) pkm_ws_kernel(WsParams p) {
+__global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) pkm_ws_kernel(WsParams p) {
     constexpr int CH = PB / 16;          // 16-byte chunks per row part = N-tiles of 8 columns
     constexpr int NU = CH;               // update warps: two (row, chunk) pairs per thread
-    constexpr int NM = PB / 32;          // GEMV warps: 16 columns each
+    constexpr int NM = PB / 32;          // GEMV warps per group: 16 columns each; two groups take alternate steps
     constexpr int RS = PB + 16;          // padded row stride: conflict-free ldmatrix / 16-byte accesses
     constexpr int R = 2 * D;
     constexpr int SLOT = 64 * RS;
@@ -405,37 +410,39 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + PB / 32 + PB / 16)) pkm_ws_
                 if (!ws_wait(done + ((t - 1) % R), ((t - 1) / R) & 1, abort_flag, p.status)) break;
             }
             const uint32_t slot = tc::smem_u32(rows + sl * SLOT);
-            // all addresses first, then the copies
-            uint32_t dst[CH];
+            // every (row, chunk) gets a copy; rows not coded "gather" copy 0 bytes
+            // (their ring row is zero-filled and rewritten by the update before any read).
+            // Addresses first, in plain code, so their shared-memory loads overlap.
             const uint8_t* src[CH];
+            uint32_t nb[CH];
 #pragma unroll
             for (int j = 0; j < CH; ++j) {
-                const int q = j * NGATH + gt;
-                const int m = q / CH, cc = q % CH;
-                dst[j] = 0u;
-                src[j] = nullptr;
-                if (code[m] == -1) {
-                    dst[j] = slot + m * RS + 16 * cc;
-                    src[j] = gstate + midx[m] * row_bytes + 16 * cc;
-                }
+                const int m = (j * NGATH + gt) / CH, cc = (j * NGATH + gt) % CH;
+                const bool gath = code[m] == -1;
+                const int64_t xm = midx[min(m, A - 1)];
+                src[j] = gstate + (gath ? xm : 0) * row_bytes + 16 * cc;
+                nb[j] = gath ? 16u : 0u;
             }
 #pragma unroll
-            for (int j = 0; j < CH; ++j)
-                if (src[j]) cp_async16(dst[j], src[j]);
+            for (int j = 0; j < CH; ++j) {
+                const int m = (j * NGATH + gt) / CH, cc = (j * NGATH + gt) % CH;
+                cp_async16_zfill(slot + m * RS + 16 * cc, src[j], nb[j]);
+            }
             cp_async_arrive_noinc(full + sl);
             mbar_arrive(full + sl);
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
-    } else if (warp < ROLE_WARPS + NM) {
+    } else if (warp < ROLE_WARPS + 2 * NM) {
         // ============================ tensor-core GEMV ============================
-        const int mw = warp - ROLE_WARPS;                      // columns mw*16 .. mw*16+15 of the part
+        const int grp = (warp - ROLE_WARPS) / NM;              // steps s with s % 2 == grp
+        const int mw = (warp - ROLE_WARPS) % NM;               // columns mw*16 .. mw*16+15 of the part
         const int g = lane >> 2, tig = lane & 3;
         const int kk = ((lane >> 4) & 1) * 8 + (lane & 7);     // ldmatrix row of this lane in a K block
         const uint32_t colb = (uint32_t)(mw * 32 + ((lane >> 3) & 1) * 16);
         const uint32_t rows_u = tc::smem_u32(rows);
         const uint32_t zrow_u = tc::smem_u32(zrow);
         T* gout = static_cast<T*>(p.out);
-        for (int s = 0; s < T_; ++s) {
+        for (int s = grp; s < T_; s += 2) {
             const int sl = s % R;
             const int cn = s / CHS, ts = s % CHS;
             const uint8_t* mc = meta + (cn % NC) * ML.bytes;
@@ -455,29 +462,25 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + PB / 32 + PB / 16)) pkm_ws_
             if (!__all_sync(DG_FULL_MASK, ok)) break;
 
             // B = [wq, wk] as the first two of 8 N columns: lanes of group 0 hold wq, group 1 wk
-            const uint16_t* wsrc = reinterpret_cast<const uint16_t*>(mc + (g == 0 ? ML.wq : ML.wk)) + ts * A;
-            const int nkb = (A + 15) >> 4;
+            const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(
+                reinterpret_cast<const uint16_t*>(mc + (g == 0 ? ML.wq : ML.wk)) + ts * A);
+            const bool bl = g < 2;
+            const int nkb = A >> 4;
+            const uint32_t own = rows_u + sl * SLOT;
             uint32_t b[4][2], base[4];
 #pragma unroll
             for (int kb = 0; kb < 4; ++kb) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int i0 = kb * 16 + h * 8 + tig * 2;
-                    const uint32_t lo = (g < 2 && i0 < A) ? wsrc[i0] : 0u;
-                    const uint32_t hi = (g < 2 && i0 + 1 < A) ? wsrc[i0 + 1] : 0u;
-                    b[kb][h] = lo | (hi << 16);
-                }
-                const int k = kb * 16 + kk;
+                const int kc = min(kb, nkb - 1);                  // in-bounds for every lane; unused blocks skipped below
+                const uint32_t w0 = wsrc[kc * 8 + tig];
+                const uint32_t w1 = wsrc[kc * 8 + 4 + tig];
+                b[kb][0] = bl ? w0 : 0u;
+                b[kb][1] = bl ? w1 : 0u;
+                const int k = kc * 16 + kk;
                 const int cd = fw[k];
-                uint32_t bs;
-                if (cd == -1) {
-                    bs = rows_u + sl * SLOT + k * RS;
-                } else if (cd < 0) {
-                    bs = zrow_u;
-                } else {
-                    const int w = s - (cd >> 6);
-                    bs = rows_u + (w % R) * SLOT + (cd & 63) * RS;
-                }
+                const int w = s - (cd >> 6);
+                const uint32_t fwd_row = rows_u + (uint32_t)((w % R) * SLOT + (cd & 63) * RS);
+                uint32_t bs = (cd == -1) ? own + (uint32_t)(k * RS) : zrow_u;
+                bs = (cd >= 0) ? fwd_row : bs;
                 base[kb] = bs + colb;
             }
             uint32_t a[4][4];
@@ -502,20 +505,21 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + PB / 32 + PB / 16)) pkm_ws_
             }
             __syncwarp();
             mbar_arrive(rdy + (s & 1));
-            if (ts == CHS - 1 || s == T_ - 1) {         // flush this warp's 32 bytes of y per step
-                const int n = ts + 1;
-                const int64_t bt0 = lt0 + (s - ts);
-                for (int i = lane; i < 2 * n; i += 32) {
-                    const int jj = i >> 1, hh = i & 1;
+            const int t0c = s - ts;
+            const int cend = min(t0c + CHS, T_);
+            if (s + 2 >= cend) {                        // this group's last step of the chunk: flush its rows of y
+                const int nj = (cend - t0c - grp + 1) >> 1;          // rows grp, grp + 2, ... of the chunk
+                for (int i = lane; i < 2 * nj; i += 32) {
+                    const int jj = grp + 2 * (i >> 1), hh = i & 1;
                     const uint4 val = *reinterpret_cast<const uint4*>(ystage + jj * PB + mw * 32 + hh * 16);
-                    dg::st16(reinterpret_cast<uint8_t*>(gout + (bt0 + jj) * Dh) + part * PB + mw * 32 + hh * 16, val);
+                    dg::st16(reinterpret_cast<uint8_t*>(gout + (lt0 + t0c + jj) * Dh) + part * PB + mw * 32 + hh * 16, val);
                 }
                 __syncwarp();
             }
         }
     } else {
         // ================================ update ================================
-        const int ut = tid - 32 * (ROLE_WARPS + NM);   // 0 .. NU*32-1
+        const int ut = tid - 32 * (ROLE_WARPS + 2 * NM);   // 0 .. NU*32-1
         const int cc = ut % CH;                      // this thread's 16-byte chunk (8 columns)
         const int m0 = ut / CH;                      // rows m0 and m0 + 32
         const float alpha_static = p.dynamic_decay ? 1.f : dg::to_f(static_cast<const T*>(p.decay)[lane_bh % p.H]);
@@ -536,14 +540,12 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + PB / 32 + PB / 16)) pkm_ws_
             uint4 raw[2];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                const int m = m0 + 32 * j;
+                const int m = m0 + 32 * j;                  // rows >= A carry code -2 and are skipped
+                const int mc_ = min(m, A - 1);
                 cd[j] = fw[m];
-                x[j] = 0; wkv[j] = 0.f; raw[j] = make_uint4(0, 0, 0, 0);
-                if (cd[j] != -2) {
-                    x[j] = midx[m];
-                    wkv[j] = dg::to_f(mwk[m]);
-                }
-                if (cd[j] == -1) raw[j] = *reinterpret_cast<const uint4*>(slot + m * RS + cc * 16);
+                x[j] = midx[mc_];
+                wkv[j] = dg::to_f(mwk[mc_]);
+                raw[j] = *reinterpret_cast<const uint4*>(slot + m * RS + cc * 16);   // gathered row (used when code -1)
             }
             const float al = p.dynamic_decay ? dg::to_f(reinterpret_cast<const T*>(mc + ML.alpha)[ts]) : alpha_static;
             const unsigned long long al2 = f2pack(al, al);
@@ -587,7 +589,7 @@ int launch_ws(const WsParams& p, int lanes, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SL.total);
     if (e != cudaSuccess) return dg_host::record_cuda_error(e);
     dim3 grid(p.parts, lanes);
-    kern<<<grid, 32 * (ROLE_WARPS + PB / 32 + PB / 16), SL.total, stream>>>(p);
+    kern<<<grid, 32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16), SL.total, stream>>>(p);
     return dg_host::check_launch();
 }
 
@@ -613,7 +615,7 @@ bool pkm_ws_supports(int dtype, int B, int H, int T, int A, int64_t total, int D
                      const void* state, const void* saved) {
     if (saved) return false;
     if (dtype != DG_DTYPE_F16 && dtype != DG_DTYPE_BF16) return false;
-    if (A < 1 || A > MAXA || T < 1 || T % 8 != 0) return false;
+    if (A < 16 || A > MAXA || A % 16 != 0 || T < 1 || T % 8 != 0) return false;   // whole 16-row MMA blocks
     if (total >= (int64_t)0x7fffffff - 1 || T >= (1 << 25)) return false;
     const int PB = ws_part_bytes(B, H, Dh);
     if (PB == 0) return false;
