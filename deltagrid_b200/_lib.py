@@ -33,14 +33,16 @@ _SIGS = {
     "dg_dense_step": [_I, _I, _I, _I, _I, _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
                       _P, _I, _I64, _I64, _P, _P, _P, _P],
     "dg_pkm_forward": [_I, _I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P],
-    "dg_pkm_forward_ex": [_I, _I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _P],
+    "dg_pkm_forward_ex": [_I, _I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _P, _SZ,
+                          _P],
+    "dg_pkm_forward_workspace_size": [_I, _I, _I, _I, _I, _I64, _I, _I],
     "dg_pkm_step": [_I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P],
     "dg_read_device_status": [_P, _I, _P, _P],
     "dg_pkm_route": [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     "dg_fxp_dense_forward": [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P],
     "dg_fxp_pkm_forward": [_I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
 }
-_RESTYPE = {"dg_status_string": ctypes.c_char_p}
+_RESTYPE = {"dg_status_string": ctypes.c_char_p, "dg_pkm_forward_workspace_size": ctypes.c_size_t}
 
 _lib = None
 _lock = threading.Lock()

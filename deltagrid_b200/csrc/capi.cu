@@ -40,7 +40,8 @@ bool pkm_ws_supports(int dtype, int B, int H, int T, int A, int64_t total, int D
                      const void* state, const void* saved);
 int pkm_forward_ws(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
                    const void* wk, const void* wq, const int64_t* idx, const void* decay, int dynamic_decay,
-                   void* state, void* out, int32_t* status, cudaStream_t stream);
+                   void* state, void* out, int32_t* status, void* workspace, cudaStream_t stream);
+size_t pkm_ws_workspace_bytes(int B, int H, int T);
 
 }  // namespace dg_host
 
@@ -111,10 +112,22 @@ int dg_dense_step(int dtype, int B, int H, int slots, int dh, const void* v, int
                       static_cast<cudaStream_t>(stream));
 }
 
+size_t dg_pkm_forward_workspace_size(int dtype, int B, int H, int T, int active, int64_t total_slots, int dh,
+                                     int algo) {
+    if (!valid_dtype(dtype) || B <= 0 || H <= 0 || T <= 0 || active <= 0 || total_slots <= 0 || dh <= 0) return 0;
+    if (algo != DG_PKM_AUTO && algo != DG_PKM_WARP_SPECIALIZED) return 0;
+    if (algo == DG_PKM_AUTO && T < 64) return 0;
+    // shape-level check only (alignment is not known here): 16-byte-aligned placeholder pointers
+    const void* a = reinterpret_cast<const void*>(uintptr_t(256));
+    if (!pkm_ws_supports(dtype, B, H, T, active, total_slots, dh, a, a, a, a, a, a, 0, a, nullptr)) return 0;
+    return pkm_ws_workspace_bytes(B, H, T);
+}
+
 int dg_pkm_forward_ex(int dtype, int B, int H, int T, int active, int64_t total_slots, int dh,
                       const void* v, const void* beta, const void* wk, const void* wq,
                       const int64_t* idx, const void* decay, int dynamic_decay, void* state, void* out,
-                      void* saved_s_act, int32_t* dev_status, int algo, void* stream) {
+                      void* saved_s_act, int32_t* dev_status, int algo, void* workspace,
+                      size_t workspace_bytes, void* stream) {
     if (!valid_dtype(dtype) || B <= 0 || H <= 0 || T < 0 || active <= 0 || total_slots <= 0 || dh <= 0)
         return DG_ERR_INVALID_ARGUMENT;
     if (algo < DG_PKM_AUTO || algo > DG_PKM_WARP_SPECIALIZED) return DG_ERR_INVALID_ARGUMENT;
@@ -134,8 +147,21 @@ int dg_pkm_forward_ex(int dtype, int B, int H, int T, int active, int64_t total_
     }
     if (algo == DG_PKM_WARP_SPECIALIZED) {
         if (!ws) return DG_ERR_UNSUPPORTED;
-        return pkm_forward_ws(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
-                              dynamic_decay, state, out, dev_status, s);
+        const size_t need = pkm_ws_workspace_bytes(B, H, T);
+        if (workspace) {
+            if (workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15)) return DG_ERR_WORKSPACE;
+            return pkm_forward_ws(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
+                                  dynamic_decay, state, out, dev_status, workspace, s);
+        }
+        // no caller workspace: stream-ordered allocation from the device's default pool
+        void* w = nullptr;
+        cudaError_t e = cudaMallocAsync(&w, need, s);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        const int rc = pkm_forward_ws(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
+                                      dynamic_decay, state, out, dev_status, w, s);
+        e = cudaFreeAsync(w, s);
+        if (rc != DG_OK) return rc;
+        return e == cudaSuccess ? DG_OK : record_cuda_error(e);
     }
     if (algo == DG_PKM_PIPELINED) {
         if (!pipe) return DG_ERR_UNSUPPORTED;
@@ -151,7 +177,7 @@ int dg_pkm_forward(int dtype, int B, int H, int T, int active, int64_t total_slo
                    const int64_t* idx, const void* decay, int dynamic_decay, void* state, void* out,
                    void* saved_s_act, int32_t* dev_status, void* stream) {
     return dg_pkm_forward_ex(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
-                             dynamic_decay, state, out, saved_s_act, dev_status, DG_PKM_AUTO, stream);
+                             dynamic_decay, state, out, saved_s_act, dev_status, DG_PKM_AUTO, nullptr, 0, stream);
 }
 
 int dg_pkm_step(int dtype, int B, int H, int active, int64_t total_slots, int dh, const void* v,

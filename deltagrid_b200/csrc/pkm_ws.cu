@@ -5,42 +5,47 @@
 // r = beta (v - pred), scatter S[idx_t] = cast(alpha s + (r) wk), rows rounded to
 // the storage dtype every step.
 //
-// One CTA per (lane, part of the row); four roles run concurrently on a ring of
-// R = 2D row slots, synchronised by mbarriers:
-//   hash (2 warps)  loads the metadata (idx, wk, wq, v, beta, alpha) 16 steps at
-//       a time and, for every row of those steps, finds the last earlier step
-//       inside the window [t-D+1, t-1] that wrote the same slot.  The steps of a
-//       chunk are resolved step by step with a chained table: 4096 heads hold
-//       the latest writer per hash of the slot, links the writer each one
-//       displaced, and a lookup walks the chain newest first, checking each
-//       writer's slot index in the resident metadata, until it leaves the
-//       window.  The result is a per-row code: gather, forward from (step,
-//       position), or no row.  A walk longer than 16 hops sends the step to
-//       sync mode: all its rows are gathered after every earlier update
-//       (exact, slow).
+// Two kernels, launched back to back on the caller's stream:
+//
+// pkm_hazard_kernel -- index-only pre-pass over all SMs.  For every row (t, m)
+//   of every lane it finds the last earlier step w in [t-D+1, t-1] that wrote
+//   the same slot and writes a 16-bit code to the workspace: -1 gather the row
+//   from global memory, -2 no row (m >= A, or an index out of range, which is
+//   flagged), else (t - w) << 6 | position of the slot in step w.  A CTA
+//   resolves 48 steps of one lane plus D-1 steps of lookback in parallel: all
+//   (slot, step, position) entries go into a shared-memory open-addressing
+//   table that is never more than half full, so every insert finds a cell and
+//   every code is exact; then every row of the 48 steps scans its probe run.
+//
+// pkm_ws_kernel -- the recurrence.  One CTA per (lane, part of the row); four
+//   roles run concurrently on a ring of R = 2D row slots, synchronised by
+//   mbarriers:
+//   loader (1 warp)  metadata (idx, wk, wq, v, beta, alpha, codes) 16 steps at a
+//       time into a 3-chunk ring, each chunk reloaded once its last update is done.
 //   gather (2 warps)  per step t, D steps ahead of the update: row-coalesced
 //       cp.async (8 lanes per 128 bytes) of the rows coded "gather" into the
-//       step's ring slot.
+//       step's ring slot; other rows copy 0 bytes (zero-fill), so the issue
+//       loop has no branches.
 //   gemv (two groups of PB/32 warps, 16 columns each, alternate steps)
-//       per step s: y and pred of its columns
-//       as a tensor-core GEMV, mma.sync m16n8k16 with A = the gathered rows
-//       transposed (ldmatrix.trans, one row address per lane, so forwarded rows
-//       need no copy; columns are the M dimension) and B = [wq, wk] (2 of 8 N
-//       columns used), four MMAs for 64 rows; writes r = beta (v - pred) to
-//       shared memory and stages y for coalesced stores.
+//       per step s: y and pred of its columns as a tensor-core GEMV, mma.sync
+//       m16n8k16 with A = the gathered rows transposed (ldmatrix.trans, one row
+//       address per lane, so forwarded rows need no copy; columns are the M
+//       dimension) and B = [wq, wk] (2 of 8 N columns used), four MMAs for 64
+//       rows; writes r = beta (v - pred) to shared memory and stages y for
+//       coalesced stores.
 //   update (PB/16 warps)  per step s: loads its gathered rows before r is ready,
 //       then the new rows (fp32 math, packed f32x2, one rounding), written to
 //       the ring slot (for forwarding) and to global memory with coalesced
 //       16-byte stores.
-// The update of step s overlaps the GEMV of step s+1 unless s+1 reads a row
-// that s writes, in which case the GEMV waits for that update.
+//   The update of step s overlaps the GEMV of steps s+1 and s+2 unless they
+//   read a row that s writes, in which case the GEMV waits for that update.
 //
 // Ordering argument: a row gathered from global memory for step t has its last
 // writer w <= t-D, and the gather is issued only after the update of step t-D
-// has completed (mbarrier release/acquire); a row whose last writer is in the
-// window is read from the writer's ring slot, which the slot's next gather (for
-// step w+R, issued after update w+R-D >= w+D) cannot overwrite before every
-// reader (steps <= w+D-1) is done.
+// has completed (mbarrier release/acquire; updates complete in step order); a
+// row whose last writer is in the window is read from the writer's ring slot,
+// which the slot's next gather (for step w+R, issued after update w+R-D >= w+D)
+// cannot overwrite before every reader (steps <= w+D-1) is done.
 #include "dg_common.cuh"
 #include "tc_util.cuh"
 
@@ -49,13 +54,16 @@ namespace {
 constexpr int MAXA = 64;
 constexpr int CHS = 16;                 // steps per metadata chunk
 constexpr int NC = 3;                   // metadata chunks resident
-constexpr int HBITS = 12;
-constexpr int HHEADS = 1 << HBITS;      // chain heads of the hazard table
-constexpr int CR = 16;                  // steps of chain links kept (>= window)
-constexpr int MAXHOP = 16;              // longest chain walk before a step falls back to sync mode
-constexpr int NHASH = 64;               // hash threads (two warps)
+constexpr int NLOAD = 32;               // loader threads (one warp)
 constexpr int NGATH = 64;               // gather threads (two warps)
-constexpr int ROLE_WARPS = 4;           // hash 2, gather 2 (then PB/32 GEMV warps, PB/16 update warps)
+constexpr int ROLE_WARPS = 3;           // loader 1, gather 2 (then 2 x PB/32 GEMV warps, PB/16 update warps)
+constexpr int HZ_STEPS = 48;            // steps resolved per pre-pass CTA
+constexpr int HZ_CELLS = 8192;          // pre-pass table cells: >= 2 x (48 + 15) x 64 entries
+constexpr int HZ_THREADS = 512;
+constexpr int HZ_MAXWIN = 16;           // largest window depth D the pre-pass covers
+constexpr int HZ_KMAX = ((HZ_STEPS + HZ_MAXWIN - 1) * MAXA + HZ_THREADS - 1) / HZ_THREADS;   // entries per thread
+static_assert(HZ_KMAX * HZ_THREADS >= (HZ_STEPS + HZ_MAXWIN - 1) * MAXA, "pre-pass entry slots");
+static_assert(2 * (HZ_STEPS + HZ_MAXWIN - 1) * MAXA <= HZ_CELLS, "pre-pass table at most half full");
 
 struct WsParams {
     const void* v;
@@ -70,10 +78,11 @@ struct WsParams {
     int H, T, A, Dh, parts;
     int64_t total;
     int dynamic_decay;
+    const int16_t* codes;       // [lanes, T, 64] from pkm_hazard_kernel
 };
 
 struct MetaLayout {
-    int idx, wk, wq, v, beta, alpha, code, sync, bytes;
+    int idx, wk, wq, v, beta, alpha, code, bytes;
 };
 
 __host__ __device__ inline MetaLayout meta_layout(int A, int Dh) {
@@ -86,14 +95,13 @@ __host__ __device__ inline MetaLayout meta_layout(int A, int Dh) {
     L.beta = o;  o += 32;
     L.alpha = o; o += 32;
     L.code = o;  o += CHS * 64 * 2;
-    L.sync = o;  o += CHS;
     L.bytes = (o + 127) / 128 * 128;
     return L;
 }
 
 // shared-memory carve-up (same arithmetic on host and device)
 struct SmemLayout {
-    int bars, misc, table, rows, zrow, rbuf, ystage, meta, total;
+    int bars, misc, rows, zrow, rbuf, ystage, meta, total;
 };
 __host__ __device__ inline SmemLayout smem_layout(int PB, int D, int A, int Dh) {
     SmemLayout L;
@@ -101,7 +109,6 @@ __host__ __device__ inline SmemLayout smem_layout(int PB, int D, int A, int Dh) 
     int o = 0;
     L.bars = o;   o += 512;
     L.misc = o;   o += 16;
-    L.table = o;  o += HHEADS * 4 + CR * 64 * 4;
     L.rows = o;   o += R * 64 * RS;
     L.zrow = o;   o += RS;
     L.rbuf = o;   o += 2 * 64 * 4;
@@ -112,15 +119,87 @@ __host__ __device__ inline SmemLayout smem_layout(int PB, int D, int A, int Dh) 
     return L;
 }
 
-// chain head of a slot: a 32-bit integer mix (xor-shift / multiply) so that
-// the lattice-shaped slot sets of Kronecker routing spread over the heads
-__device__ __forceinline__ uint32_t slot_head(uint32_t x) {
+// home cell of a slot in the pre-pass table: a 32-bit integer mix (xor-shift /
+// multiply) so that the lattice-shaped slot sets of Kronecker routing spread out
+__device__ __forceinline__ uint32_t slot_home(uint32_t x) {
     x ^= x >> 16;
     x *= 0x85ebca6bu;
     x ^= x >> 13;
     x *= 0xc2b2ae35u;
     x ^= x >> 16;
-    return x >> (32 - HBITS);
+    return x & (HZ_CELLS - 1);
+}
+
+// ---------------------------------------------------------------------------
+// pre-pass: row codes of steps [blockIdx.x * HZ_STEPS, +HZ_STEPS) of lane blockIdx.y
+__global__ void __launch_bounds__(HZ_THREADS) pkm_hazard_kernel(const int64_t* __restrict__ idx, int16_t* codes,
+                                                                int32_t* status, int T, int A, int64_t total, int D) {
+    extern __shared__ unsigned long long cells[];          // [HZ_CELLS]
+    const int tid = threadIdx.x;
+    const int lane = blockIdx.y;
+    const int t0 = blockIdx.x * HZ_STEPS;
+    const int tb = max(0, t0 - (D - 1));
+    const int te = min(T, t0 + HZ_STEPS);
+    const int nE = (te - tb) * A;
+    const int64_t* li = idx + ((int64_t)lane * T + tb) * A;
+    int16_t* lc = codes + (int64_t)lane * T * 64;
+    for (int i = tid; i < HZ_CELLS; i += HZ_THREADS) cells[i] = 0ull;
+    __syncthreads();
+    int64_t xs[HZ_KMAX];
+#pragma unroll
+    for (int k = 0; k < HZ_KMAX; ++k) {
+        const int e = tid + k * HZ_THREADS;
+        xs[k] = -1;
+        if (e < nE) {
+            const int64_t x = li[e];
+            xs[k] = x;
+            if (x >= 0 && x < total) {
+                const int tl = e / A, m = e - tl * A;          // step relative to tb, position
+                const unsigned long long ent =
+                    (unsigned long long)((uint32_t)x + 1u) | ((unsigned long long)(((uint32_t)tl << 6) | (uint32_t)m) << 32);
+                uint32_t h = slot_home((uint32_t)x);
+                for (int probe = 0; probe < HZ_CELLS; ++probe) {  // the table is at most half full
+                    if (atomicCAS(cells + h, 0ull, ent) == 0ull) break;
+                    h = (h + 1) & (HZ_CELLS - 1);
+                }
+            }
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < HZ_KMAX; ++k) {
+        const int e = tid + k * HZ_THREADS;
+        if (e >= nE) continue;
+        const int tl = e / A, m = e - tl * A;
+        const int t = tb + tl;
+        if (t < t0) continue;                                   // lookback rows only feed the table
+        const int64_t x = xs[k];
+        int cd = -2;
+        if (x >= 0 && x < total) {
+            const uint32_t key = (uint32_t)x + 1u;
+            uint32_t h = slot_home((uint32_t)x);
+            int best = -1, bpos = 0;
+            for (int probe = 0; probe < HZ_CELLS; ++probe) {
+                const unsigned long long c = cells[h];
+                if (c == 0ull) break;
+                if ((uint32_t)c == key) {
+                    const uint32_t st = (uint32_t)(c >> 32);
+                    const int wl = (int)(st >> 6);
+                    if (wl < tl && wl > best) { best = wl; bpos = (int)(st & 63); }
+                }
+                h = (h + 1) & (HZ_CELLS - 1);
+            }
+            cd = (best >= 0 && tl - best <= D - 1) ? (((tl - best) << 6) | bpos) : -1;
+        } else {
+            dg::flag_status(status, DG_DEVCHK_INDEX_RANGE);
+        }
+        lc[(int64_t)t * 64 + m] = (int16_t)cd;
+    }
+    if (A < 64) {                                               // positions without a row
+        const int na = 64 - A;
+        for (int i = tid; i < (te - t0) * na; i += HZ_THREADS)
+            lc[(int64_t)(t0 + i / na) * 64 + A + i % na] = (int16_t)-2;
+    }
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
@@ -135,18 +214,6 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void hash_bar() { asm volatile("bar.sync 1, 64;" ::: "memory"); }
-// barrier over the 64 hash threads that also ORs a predicate across them
-__device__ __forceinline__ bool hash_bar_or(bool pred) {
-    uint32_t r;
-    asm volatile(
-        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n barrier.cta.red.or.pred q, 1, 64, p;\n"
-        " selp.u32 %0, 1, 0, q;\n}\n"
-        : "=r"(r)
-        : "r"((uint32_t)pred)
-        : "memory");
-    return r != 0;
 }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -264,11 +331,8 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) p
     uint64_t* rdy = done + R;                                       // [2] r of step ready
     uint64_t* rfree = rdy + 2;                                      // [2] r buffer consumed
     uint64_t* mfull = rfree + 2;                                    // [NC] metadata chunk landed
-    uint64_t* hready = mfull + NC;                                  // [NC] row codes of chunk ready
-    uint64_t* mfree = hready + NC;                                  // [NC] chunk's last update done
+    uint64_t* mfree = mfull + NC;                                   // [NC] chunk's last update done
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SL.misc);
-    uint32_t* heads = reinterpret_cast<uint32_t*>(smem + SL.table);           // [HHEADS] latest writer per head
-    uint32_t* links = heads + HHEADS;                                         // [CR][64] next (older) writer
     uint8_t* rows = smem + SL.rows;
     uint8_t* zrow = smem + SL.zrow;
     float* rbuf = reinterpret_cast<float*>(smem + SL.rbuf);
@@ -285,7 +349,6 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) p
     uint8_t* gstate = reinterpret_cast<uint8_t*>(p.state) + (int64_t)lane_bh * total * row_bytes + (int64_t)part * PB;
 
     for (int i = tid; i < RS / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(zrow)[i] = 0u;
-    for (int i = tid; i < HHEADS; i += blockDim.x) heads[i] = 0u;
     if (tid == 0) {
         for (int i = 0; i < R; ++i) {
             tc::mbar_init(full + i, 2 * NGATH);
@@ -296,17 +359,15 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) p
             tc::mbar_init(rfree + i, NU * 32);
         }
         for (int i = 0; i < NC; ++i) {
-            tc::mbar_init(mfull + i, NHASH);
-            tc::mbar_init(hready + i, NHASH);
+            tc::mbar_init(mfull + i, NLOAD);
             tc::mbar_init(mfree + i, NU * 32);
         }
         *abort_flag = 0;
     }
     __syncthreads();
 
-    if (warp < 2) {
-        // ================================ hash ================================
-        const int ht = tid;                              // 0..63
+    if (warp == 0) {
+        // =============================== loader ===============================
         const T* gwk = static_cast<const T*>(p.wk);
         const T* gwq = static_cast<const T*>(p.wq);
         const T* gv = static_cast<const T*>(p.v);
@@ -315,7 +376,7 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) p
         auto copy = [&](uint8_t* dst, const void* src, int nbytes) {
             const uint32_t d0 = tc::smem_u32(dst);
             const uint8_t* s0 = static_cast<const uint8_t*>(src);
-            for (int i = ht; i < nbytes / 16; i += NHASH) cp_async16(d0 + 16 * i, s0 + 16 * i);
+            for (int i = lane; i < nbytes / 16; i += NLOAD) cp_async16(d0 + 16 * i, s0 + 16 * i);
         };
         auto load_chunk = [&](int c) {
             const int t0 = c * CHS;
@@ -328,87 +389,33 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) p
             copy(mc + ML.v, gv + bt * Dh, n * Dh * 2);
             copy(mc + ML.beta, gbeta + bt, n * 2);
             if (p.dynamic_decay) copy(mc + ML.alpha, gdecay + bt, n * 2);
+            copy(mc + ML.code, p.codes + bt * 64, n * 128);
             cp_async_arrive_noinc(mfull + (c % NC));
         };
         load_chunk(0);
         if (nchunks > 1) load_chunk(1);
-        for (int c = 0; c < nchunks; ++c) {
-            bool ok = ws_wait(mfull + (c % NC), (c / NC) & 1, abort_flag, p.status);
-            if (hash_bar_or(!ok)) break;
-            const int t0 = c * CHS;
-            const int n = min(CHS, T_ - t0);
-            uint8_t* mc = meta + (c % NC) * ML.bytes;
-            const int64_t* midx = reinterpret_cast<const int64_t*>(mc + ML.idx);
-            int16_t* code = reinterpret_cast<int16_t*>(mc + ML.code);
-            uint8_t* sync = mc + ML.sync;
-            // Steps in order; thread ht owns row ht.  A head holds the latest writer
-            // (step + 1) << 6 | position of any slot hashing there, a link the writer
-            // it displaced, so a chain lists writers newest first; a lookup walks it
-            // until it leaves the window and checks each writer's slot index.
-            bool stop = false;
-            for (int ts = 0; ts < n; ++ts) {
-                const int t = t0 + ts;
-                int cd = -2;
-                uint32_t hd = 0, ent = 0;
-                bool incomplete = false;
-                if (ht < A) {
-                    const int64_t x = midx[ts * A + ht];
-                    if (x >= 0 && x < total) {
-                        hd = slot_head((uint32_t)x);
-                        ent = ((uint32_t)(t + 1) << 6) | (uint32_t)ht;
-                        cd = -1;
-                        uint32_t e = heads[hd];
-                        int hop = 0;
-                        for (; hop < MAXHOP && e != 0u; ++hop) {
-                            const int w = (int)(e >> 6) - 1, pos = (int)(e & 63);
-                            if (w < t - (D - 1)) break;               // older than the window: done
-                            const uint8_t* mw = meta + ((w / CHS) % NC) * ML.bytes;
-                            if (reinterpret_cast<const int64_t*>(mw + ML.idx)[(w % CHS) * A + pos] == x) {
-                                cd = ((t - w) << 6) | pos;
-                                break;
-                            }
-                            e = links[(w % CR) * 64 + pos];
-                        }
-                        incomplete = hop == MAXHOP;
-                    } else {
-                        dg::flag_status(p.status, DG_DEVCHK_INDEX_RANGE);
-                    }
-                }
-                // every lookup of step t before its inserts; a step whose walk gave up
-                // gathers all rows after every earlier update
-                const bool lost = hash_bar_or(incomplete);
-                if (lost && cd >= 0) cd = -1;
-                code[ts * 64 + ht] = (int16_t)cd;
-                if (ht == 0) sync[ts] = lost ? 1 : 0;
-                if (ent != 0u) links[(t % CR) * 64 + ht] = atomicExch(heads + hd, ent);
-                if (hash_bar_or(*abort_flag != 0)) { stop = true; break; }   // inserts before the next lookups
+        for (int c = 0; c + 2 < nchunks; ++c) {
+            // chunk c+2 reuses the buffer of chunk c-1
+            if (c >= 1) {
+                const bool ok = ws_wait(mfree + ((c - 1) % NC), ((c - 1) / NC) & 1, abort_flag, p.status);
+                if (!__all_sync(DG_FULL_MASK, ok)) break;
             }
-            if (stop) break;
-            mbar_arrive(hready + (c % NC));
-            // chunk c+1 was loaded ahead; chunk c+2 reuses the buffer of chunk c-1
-            if (c + 2 < nchunks) {
-                if (c >= 1) ok = ws_wait(mfree + ((c - 1) % NC), ((c - 1) / NC) & 1, abort_flag, p.status);
-                if (hash_bar_or(!ok)) break;
-                load_chunk(c + 2);
-            }
+            load_chunk(c + 2);
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
-    } else if (warp < 4) {
+    } else if (warp < 3) {
         // =============================== gather ===============================
-        const int gt = tid - 64;                          // 0..63
+        const int gt = tid - 32;                          // 0..63
         for (int t = 0; t < T_; ++t) {
             const int sl = t % R;
             const int c = t / CHS, ts = t % CHS;
             bool ok = true;
-            if (ts == 0) ok = ws_wait(hready + (c % NC), (c / NC) & 1, abort_flag, p.status);
+            if (ts == 0) ok = ws_wait(mfull + (c % NC), (c / NC) & 1, abort_flag, p.status);
             if (ok && t >= D) ok = ws_wait(done + ((t - D) % R), ((t - D) / R) & 1, abort_flag, p.status);
             if (!ok) break;
             const uint8_t* mc = meta + (c % NC) * ML.bytes;
             const int64_t* midx = reinterpret_cast<const int64_t*>(mc + ML.idx) + ts * A;
             const int16_t* code = reinterpret_cast<const int16_t*>(mc + ML.code) + ts * 64;
-            if (mc[ML.sync + ts] && t >= 1) {            // hazard table lost entries: wait for every earlier update
-                if (!ws_wait(done + ((t - 1) % R), ((t - 1) / R) & 1, abort_flag, p.status)) break;
-            }
             const uint32_t slot = tc::smem_u32(rows + sl * SLOT);
             // every (row, chunk) gets a copy; rows not coded "gather" copy 0 bytes
             // (their ring row is zero-filled and rewritten by the update before any read).
@@ -582,19 +589,9 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) p
     }
 }
 
-template <typename T, int PB, int D>
-int launch_ws(const WsParams& p, int lanes, cudaStream_t stream) {
-    const SmemLayout SL = smem_layout(PB, D, p.A, p.Dh);
-    auto kern = pkm_ws_kernel<T, PB, D>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SL.total);
-    if (e != cudaSuccess) return dg_host::record_cuda_error(e);
-    dim3 grid(p.parts, lanes);
-    kern<<<grid, 32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16), SL.total, stream>>>(p);
-    return dg_host::check_launch();
-}
-
-constexpr int kDepthFull = 7;     // window depth for 128-byte row parts (ring fits 227 KB)
-constexpr int kDepthHalf = 8;     // for 64-byte row parts
+constexpr int kDepthFull = 8;     // window depth for 128-byte row parts (ring of 16 slots)
+constexpr int kDepthHalf = 12;    // for 64-byte row parts (ring of 24 slots)
+static_assert(kDepthFull <= HZ_MAXWIN && kDepthHalf <= HZ_MAXWIN, "window depth covered by the pre-pass");
 
 // row part bytes for a call: 128 (full 64-column fp16 rows), or 64 (two CTAs per lane)
 int ws_part_bytes(int B, int H, int Dh) {
@@ -606,9 +603,22 @@ int ws_part_bytes(int B, int H, int Dh) {
     return 0;
 }
 
+template <typename T, int PB, int D>
+int launch_ws(const WsParams& p, int lanes, cudaStream_t stream) {
+    const SmemLayout SL = smem_layout(PB, D, p.A, p.Dh);
+    auto kern = pkm_ws_kernel<T, PB, D>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SL.total);
+    if (e != cudaSuccess) return dg_host::record_cuda_error(e);
+    dim3 grid(p.parts, lanes);
+    kern<<<grid, 32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16), SL.total, stream>>>(p);
+    return dg_host::check_launch();
+}
+
 }  // namespace
 
 namespace dg_host {
+
+size_t pkm_ws_workspace_bytes(int B, int H, int T) { return (size_t)B * H * T * 64 * sizeof(int16_t); }
 
 bool pkm_ws_supports(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
                      const void* wk, const void* wq, const void* idx, const void* decay, int dynamic_decay,
@@ -626,13 +636,23 @@ bool pkm_ws_supports(int dtype, int B, int H, int T, int A, int64_t total, int D
     return (al & 15) == 0;
 }
 
+// workspace: pkm_ws_workspace_bytes(B, H, T) bytes, 16-byte aligned
 int pkm_forward_ws(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
                    const void* wk, const void* wq, const int64_t* idx, const void* decay, int dynamic_decay,
-                   void* state, void* out, int32_t* status, cudaStream_t stream) {
+                   void* state, void* out, int32_t* status, void* workspace, cudaStream_t stream) {
     const int PB = ws_part_bytes(B, H, Dh);
     const int parts = Dh * 2 / PB;
-    WsParams p{v, beta, wk, wq, idx, decay, state, out, status, H, T, A, Dh, parts, total, dynamic_decay};
+    const int D = PB == 128 ? kDepthFull : kDepthHalf;
     const int lanes = B * H;
+    int16_t* codes = static_cast<int16_t*>(workspace);
+    const int hz_smem = HZ_CELLS * 8;
+    cudaError_t e = cudaFuncSetAttribute(pkm_hazard_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, hz_smem);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    pkm_hazard_kernel<<<dim3((T + HZ_STEPS - 1) / HZ_STEPS, lanes), HZ_THREADS, hz_smem, stream>>>(idx, codes, status,
+                                                                                                  T, A, total, D);
+    int rc = check_launch();
+    if (rc != DG_OK) return rc;
+    WsParams p{v, beta, wk, wq, idx, decay, state, out, status, H, T, A, Dh, parts, total, dynamic_decay, codes};
     if (dtype == DG_DTYPE_F16)
         return PB == 128 ? launch_ws<__half, 128, kDepthFull>(p, lanes, stream)
                          : launch_ws<__half, 64, kDepthHalf>(p, lanes, stream);

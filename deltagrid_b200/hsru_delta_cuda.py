@@ -217,10 +217,15 @@ def pkm_forward_algo(v: torch.Tensor, beta: torch.Tensor, wk: torch.Tensor, wq: 
              if save_for_backward else None)
     dynamic = 1 if decay_c.dim() > 1 else 0
     with torch.cuda.device(v_c.device):
+        # scratch for kernels that need it (per-row hazard codes), from torch's caching allocator
+        nws = _lib.lib().dg_pkm_forward_workspace_size(code, B, H, T, A, total, Dh, int(algo)) \
+            if saved is None else 0
+        ws = torch.empty(nws, dtype=torch.uint8, device=v_c.device) if nws else None
         _lib.call("dg_pkm_forward_ex", code, B, H, T, A, total, Dh, v_c.data_ptr(), beta_c.data_ptr(),
                   wk_c.data_ptr(), wq_c.data_ptr(), idx_c.data_ptr(), decay_c.data_ptr(), dynamic,
                   state_c.data_ptr(), out.data_ptr(), saved.data_ptr() if saved is not None else None,
-                  _status_word(v_c.device).data_ptr(), int(algo), _stream(v_c))
+                  _status_word(v_c.device).data_ptr(), int(algo), ws.data_ptr() if ws is not None else None,
+                  nws, _stream(v_c))
     return [out, state_c, saved]
 
 

@@ -134,13 +134,24 @@ int dg_pkm_forward(int dtype, int B, int H, int T, int active, int64_t total_slo
                    void* state, void* out, void* saved_s_act, int32_t* dev_status,
                    void* stream);
 
-/* dg_pkm_forward with an explicit kernel choice (dg_pkm_algo); DG_ERR_UNSUPPORTED
- * when the chosen kernel does not cover the call. */
+/* Bytes of device workspace dg_pkm_forward_ex needs for this shape and kernel
+ * choice (0: none).  The warp-specialised kernel stores a 16-bit hazard code per
+ * row in it: B*H*T*64*2 bytes.  Call-independent; no GPU work. */
+size_t dg_pkm_forward_workspace_size(int dtype, int B, int H, int T, int active, int64_t total_slots, int dh,
+                                     int algo);
+
+/* dg_pkm_forward with an explicit kernel choice (dg_pkm_algo) and an optional
+ * caller-owned workspace (16-byte aligned, at least
+ * dg_pkm_forward_workspace_size bytes; DG_ERR_WORKSPACE otherwise).  With
+ * workspace == NULL a kernel that needs one takes it from the device's default
+ * memory pool, stream-ordered (cudaMallocAsync / cudaFreeAsync on `stream`).
+ * DG_ERR_UNSUPPORTED when the chosen kernel does not cover the call.
+ * dg_pkm_forward is this call with DG_PKM_AUTO and no workspace. */
 int dg_pkm_forward_ex(int dtype, int B, int H, int T, int active, int64_t total_slots, int dh,
                       const void* v, const void* beta, const void* wk, const void* wq,
                       const int64_t* idx, const void* decay, int dynamic_decay,
                       void* state, void* out, void* saved_s_act, int32_t* dev_status,
-                      int algo, void* stream);
+                      int algo, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Sparse Delta-PKM single decode step, state updated in place.

@@ -1,7 +1,9 @@
 """Pipelined PKM kernel (rows fetched D steps ahead, hazards forwarded from shared
-memory) against the CPU oracle.  dg_pkm_forward takes it for T >= 64 with
-16-byte-aligned inputs; saving gathered rows forces the one-step kernel, which
-gives a second GPU reference on identical inputs."""
+memory) against the CPU oracle.  dg_pkm_forward takes it for fp32 state (and
+16-bit shapes the warp-specialised kernel does not cover) at T >= 64 with
+16-byte-aligned inputs; here it is selected explicitly.  Saving gathered rows
+runs the one-step kernel, which gives a second GPU reference on identical
+inputs."""
 import numpy as np
 import pytest
 import torch
@@ -23,8 +25,11 @@ def _oracle(d, dtype):
 
 
 def _gpu(d, save=False):
+    # the pipelined kernel explicitly (the default choice for 16-bit state is the
+    # warp-specialised kernel); saving rows always runs the one-step kernel
     g = {n: t.cuda() for n, t in d.items()}
-    return ext.pkm_forward(g["v"], g["beta"], g["wk"], g["wq"], g["idx"], g["decay"], g["state"], save)
+    return ext.pkm_forward_algo(g["v"], g["beta"], g["wk"], g["wq"], g["idx"], g["decay"], g["state"], save,
+                                1 if save else 2)
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
