@@ -36,6 +36,7 @@ _SIGS = {
     "dg_pkm_forward_ex": [_I, _I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _P, _SZ,
                           _P],
     "dg_pkm_forward_workspace_size": [_I, _I, _I, _I, _I, _I64, _I, _I],
+    "dg_pkm_forward_noalloc": [_I, _I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P],
     "dg_pkm_step": [_I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P],
     "dg_read_device_status": [_P, _I, _P, _P],
     "dg_pkm_route": [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],

@@ -153,6 +153,18 @@ int dg_pkm_forward_ex(int dtype, int B, int H, int T, int active, int64_t total_
                       void* state, void* out, void* saved_s_act, int32_t* dev_status,
                       int algo, void* workspace, size_t workspace_bytes, void* stream);
 
+/* dg_pkm_forward that allocates nothing (no reference counterpart).  Scratch comes
+ * from a fixed 16 MiB device array in this library (its address looked up once
+ * per device); calls needing more (dg_pkm_forward_workspace_size > 16 MiB, i.e.
+ * B*H*T > 131072 for the warp-specialised kernel) return DG_ERR_WORKSPACE without
+ * launching.  Calls that overlap in time on one device share that array and race:
+ * serialize them. */
+int dg_pkm_forward_noalloc(int dtype, int B, int H, int T, int active, int64_t total_slots, int dh,
+                           const void* v, const void* beta, const void* wk, const void* wq,
+                           const int64_t* idx, const void* decay, int dynamic_decay,
+                           void* state, void* out, void* saved_s_act, int32_t* dev_status,
+                           void* stream);
+
 /*
  * Sparse Delta-PKM single decode step, state updated in place.
  * Replaces launch_delta_grid_pkm_step (src/cpp/delta_kernel.cu:829-847) and

@@ -1,0 +1,56 @@
+"""dg_pkm_forward_noalloc (scratch from a fixed device array) against dg_pkm_forward
+(scratch from a stream-ordered pool allocation) on identical inputs, two calls in a
+row so the second call reuses the array the first one filled; plus the size check."""
+import ctypes
+
+import pytest
+import torch
+
+from inputs import pkm_inputs
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    from deltagrid_b200 import _lib
+
+F16 = 2
+
+
+def _args(g, B, H, T, A, total, status):
+    return (F16, B, H, T, A, ctypes.c_int64(total), 64, g["v"].data_ptr(), g["beta"].data_ptr(),
+            g["wk"].data_ptr(), g["wq"].data_ptr(), g["idx"].data_ptr(), g["decay"].data_ptr(), 0,
+            g["state"].data_ptr(), g["out"].data_ptr(), None, status.data_ptr(),
+            torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("B,H,G", [(16, 8, 32), (2, 3, 16)])     # full rows and row halves
+def test_noalloc_matches_dg_pkm_forward_twice(B, H, G):
+    T, K = 256, 8
+    d = pkm_inputs(B, H, T, G, K, 64, torch.float16, seed=B + G, s_init_scale=0.2)
+    runs = {}
+    for name in ("dg_pkm_forward", "dg_pkm_forward_noalloc"):
+        g = {n: t.cuda() for n, t in d.items()}
+        g["out"] = torch.empty_like(g["v"])
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        outs = []
+        for _ in range(2):                       # second call continues from the first call's state
+            _lib.call(name, *_args(g, B, H, T, K * K, G * G, status))
+            torch.cuda.synchronize()
+            outs.append(g["out"].clone())
+        assert int(status.item()) == 0
+        runs[name] = (outs, g["state"].clone())
+    (o1, s1), (o2, s2) = runs["dg_pkm_forward"], runs["dg_pkm_forward_noalloc"]
+    for a, b in zip(o1, o2):
+        assert torch.equal(a, b)
+    assert torch.equal(s1, s2)
+
+
+def test_noalloc_rejects_oversize_without_launching():
+    # 131080 steps of one lane need 131080 * 128 bytes > 16 MiB of scratch
+    T = 131080
+    g = {n: torch.zeros(16, dtype=torch.float16, device="cuda") for n in ("v", "beta", "wk", "wq", "decay", "state",
+                                                                            "out")}
+    g["idx"] = torch.zeros(16, dtype=torch.int64, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc = _lib.lib().dg_pkm_forward_noalloc(*_args(g, 1, 1, T, 64, 1 << 14, status))
+    assert rc == -4                                   # DG_ERR_WORKSPACE
