@@ -26,7 +26,7 @@
 //       cp.async (8 lanes per 128 bytes) of the rows coded "gather" into the
 //       step's ring slot; other rows copy 0 bytes (zero-fill), so the issue
 //       loop has no branches.
-//   gemv (two groups of PB/32 warps, 16 columns each, alternate steps)
+//   slices (KPAR warps per 16-column slice, taking turns by step)
 //       per step s: y and pred of its columns as a tensor-core GEMV, mma.sync
 //       m16n8k16 with A = the gathered rows transposed (ldmatrix.trans, one row
 //       address per lane, so forwarded rows need no copy; columns are the M
@@ -55,8 +55,9 @@ constexpr int MAXA = 64;
 constexpr int CHS = 16;                 // steps per metadata chunk
 constexpr int NC = 3;                   // metadata chunks resident
 constexpr int NLOAD = 32;               // loader threads (one warp)
-constexpr int NGATH = 64;               // gather threads (two warps)
-constexpr int ROLE_WARPS = 3;           // loader 1, gather 2 (then 2 x PB/32 GEMV warps, PB/16 update warps)
+constexpr int NGATH = 128;              // gather threads (four warps)
+constexpr int ROLE_WARPS = 5;           // loader 1, gather 4 (then KPAR warps per 16-column slice)
+constexpr int KPAR = 4;                 // warps per column slice; warp k takes the steps s with s % KPAR == k
 constexpr int HZ_STEPS = 48;            // steps resolved per pre-pass CTA
 constexpr int HZ_CELLS = 8192;          // pre-pass table cells: >= 2 x (48 + 15) x 64 entries
 constexpr int HZ_THREADS = 512;
@@ -107,11 +108,11 @@ __host__ __device__ inline SmemLayout smem_layout(int PB, int D, int A, int Dh) 
     SmemLayout L;
     const int R = 2 * D, RS = PB + 16;
     int o = 0;
-    L.bars = o;   o += 512;
+    L.bars = o;   o += 1024;
     L.misc = o;   o += 16;
     L.rows = o;   o += R * 64 * RS;
     L.zrow = o;   o += RS;
-    L.rbuf = o;   o += 2 * 64 * 4;
+    L.rbuf = o;   o += 16 * 64 * 4;
     L.ystage = o; o += CHS * PB;
     o = (o + 127) / 128 * 128;
     L.meta = o;   o += NC * meta_layout(A, Dh).bytes;
@@ -315,10 +316,9 @@ __device__ __forceinline__ unsigned long long fma_f32x2(unsigned long long a, un
 }
 
 template <typename T, int PB, int D>
-__global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) pkm_ws_kernel(WsParams p) {
-    constexpr int CH = PB / 16;          // 16-byte chunks per row part = N-tiles of 8 columns
-    constexpr int NU = CH;               // update warps: two (row, chunk) pairs per thread
-    constexpr int NM = PB / 32;          // GEMV warps per group: 16 columns each; two groups take alternate steps
+__global__ void __launch_bounds__(32 * (ROLE_WARPS + KPAR * (PB / 32))) pkm_ws_kernel(WsParams p) {
+    constexpr int CH = PB / 16;          // 16-byte chunks per row part
+    constexpr int NSL = PB / 32;         // column slices of 16 columns; KPAR warps per slice take turns by step
     constexpr int RS = PB + 16;          // padded row stride: conflict-free ldmatrix / 16-byte accesses
     constexpr int R = 2 * D;
     constexpr int SLOT = 64 * RS;
@@ -327,40 +327,35 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) p
     const SmemLayout SL = smem_layout(PB, D, p.A, p.Dh);
     const MetaLayout ML = meta_layout(p.A, p.Dh);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + SL.bars);   // [R] rows of step landed
-    uint64_t* done = full + R;                                      // [R] update of step complete
-    uint64_t* rdy = done + R;                                       // [2] r of step ready
-    uint64_t* rfree = rdy + 2;                                      // [2] r buffer consumed
-    uint64_t* mfull = rfree + 2;                                    // [NC] metadata chunk landed
-    uint64_t* mfree = mfull + NC;                                   // [NC] chunk's last update done
+    uint64_t* done = full + R;                                      // [R] every slice finished the step
+    uint64_t* dsl = done + R;                                       // [R][NSL] one slice finished the step
+    uint64_t* mfull = dsl + R * NSL;                                // [NC] metadata chunk landed
+    uint64_t* mfree = mfull + NC;                                   // [NC] chunk's last step done by every warp
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SL.misc);
     uint8_t* rows = smem + SL.rows;
     uint8_t* zrow = smem + SL.zrow;
-    float* rbuf = reinterpret_cast<float*>(smem + SL.rbuf);
+    float* rbuf = reinterpret_cast<float*>(smem + SL.rbuf);        // [KPAR * NSL warps][16] r of the warp's columns
     uint8_t* ystage = smem + SL.ystage;
     uint8_t* meta = smem + SL.meta;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int lane_bh = blockIdx.y, part = blockIdx.x;
     const int A = p.A, Dh = p.Dh, T_ = p.T;
-    const int64_t total = p.total;
     const int64_t lt0 = (int64_t)lane_bh * T_;
     const int64_t row_bytes = (int64_t)Dh * 2;
     const int nchunks = (T_ + CHS - 1) / CHS;
-    uint8_t* gstate = reinterpret_cast<uint8_t*>(p.state) + (int64_t)lane_bh * total * row_bytes + (int64_t)part * PB;
+    uint8_t* gstate = reinterpret_cast<uint8_t*>(p.state) + (int64_t)lane_bh * p.total * row_bytes + (int64_t)part * PB;
 
     for (int i = tid; i < RS / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(zrow)[i] = 0u;
     if (tid == 0) {
         for (int i = 0; i < R; ++i) {
             tc::mbar_init(full + i, 2 * NGATH);
-            tc::mbar_init(done + i, NU * 32);
-        }
-        for (int i = 0; i < 2; ++i) {
-            tc::mbar_init(rdy + i, NM * 32);
-            tc::mbar_init(rfree + i, NU * 32);
+            tc::mbar_init(done + i, NSL * 32);
+            for (int k = 0; k < NSL; ++k) tc::mbar_init(dsl + i * NSL + k, 32);
         }
         for (int i = 0; i < NC; ++i) {
             tc::mbar_init(mfull + i, NLOAD);
-            tc::mbar_init(mfree + i, NU * 32);
+            tc::mbar_init(mfree + i, KPAR * NSL * 32);
         }
         *abort_flag = 0;
     }
@@ -403,9 +398,9 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) p
             load_chunk(c + 2);
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
-    } else if (warp < 3) {
+    } else if (warp < ROLE_WARPS) {
         // =============================== gather ===============================
-        const int gt = tid - 32;                          // 0..63
+        const int gt = tid - 32;                          // 0 .. NGATH-1
         for (int t = 0; t < T_; ++t) {
             const int sl = t % R;
             const int c = t / CHS, ts = t % CHS;
@@ -420,10 +415,11 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) p
             // every (row, chunk) gets a copy; rows not coded "gather" copy 0 bytes
             // (their ring row is zero-filled and rewritten by the update before any read).
             // Addresses first, in plain code, so their shared-memory loads overlap.
-            const uint8_t* src[CH];
-            uint32_t nb[CH];
+            constexpr int GPT = CH * 64 / NGATH;             // copies per gather thread per step
+            const uint8_t* src[GPT];
+            uint32_t nb[GPT];
 #pragma unroll
-            for (int j = 0; j < CH; ++j) {
+            for (int j = 0; j < GPT; ++j) {
                 const int m = (j * NGATH + gt) / CH, cc = (j * NGATH + gt) % CH;
                 const bool gath = code[m] == -1;
                 const int64_t xm = midx[min(m, A - 1)];
@@ -431,7 +427,7 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) p
                 nb[j] = gath ? 16u : 0u;
             }
 #pragma unroll
-            for (int j = 0; j < CH; ++j) {
+            for (int j = 0; j < GPT; ++j) {
                 const int m = (j * NGATH + gt) / CH, cc = (j * NGATH + gt) % CH;
                 cp_async16_zfill(slot + m * RS + 16 * cc, src[j], nb[j]);
             }
@@ -439,41 +435,71 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) p
             mbar_arrive(full + sl);
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
-    } else if (warp < ROLE_WARPS + 2 * NM) {
-        // ============================ tensor-core GEMV ============================
-        const int grp = (warp - ROLE_WARPS) / NM;              // steps s with s % 2 == grp
-        const int mw = (warp - ROLE_WARPS) % NM;               // columns mw*16 .. mw*16+15 of the part
+    } else {
+        // ========================= column-slice warps =========================
+        const int sw = warp - ROLE_WARPS;                      // 0 .. KPAR*NSL-1
+        const int sli = sw % NSL;                              // columns sli*16 .. sli*16+15 of the part
+        const int par = sw / NSL;                              // steps s with s % KPAR == par
         const int g = lane >> 2, tig = lane & 3;
         const int kk = ((lane >> 4) & 1) * 8 + (lane & 7);     // ldmatrix row of this lane in a K block
-        const uint32_t colb = (uint32_t)(mw * 32 + ((lane >> 3) & 1) * 16);
+        const uint32_t colb = (uint32_t)(sli * 32 + ((lane >> 3) & 1) * 16);
+        const int mr = lane & 15, cc = lane >> 4;              // update: rows mr + 16 j, 16-byte chunk cc of the slice
         const uint32_t rows_u = tc::smem_u32(rows);
         const uint32_t zrow_u = tc::smem_u32(zrow);
+        float* rw = rbuf + sw * 16;
         T* gout = static_cast<T*>(p.out);
-        for (int s = grp; s < T_; s += 2) {
+        const float alpha_static = p.dynamic_decay ? 1.f : dg::to_f(static_cast<const T*>(p.decay)[lane_bh % p.H]);
+        for (int s = par; s < T_; s += KPAR) {
             const int sl = s % R;
             const int cn = s / CHS, ts = s % CHS;
             const uint8_t* mc = meta + (cn % NC) * ML.bytes;
             bool ok = ws_wait(full + sl, (s / R) & 1, abort_flag, p.status);
             if (!__all_sync(DG_FULL_MASK, ok)) break;
             const int16_t* fw = reinterpret_cast<const int16_t*>(mc + ML.code) + ts * 64;
-            const int c0 = fw[lane], c1 = fw[lane + 32];
-            int dmin = 64;
-            if (c0 >= 0) dmin = c0 >> 6;
-            if (c1 >= 0) dmin = min(dmin, c1 >> 6);
-            dmin = __reduce_min_sync(DG_FULL_MASK, dmin);
-            if (dmin < 64) {                          // a forwarded row: its writer's update must be complete
-                const int w = s - dmin;
-                ok = ws_wait(done + (w % R), (w / R) & 1, abort_flag, p.status);
+            // rows forwarded from a step another warp of this slice took: that warp must
+            // have finished it (this warp's own earlier steps precede this one in program order)
+            {
+                const int c0 = fw[lane], c1 = fw[lane + 32];
+                uint32_t dm = 0;
+                if (c0 >= 0) dm |= 1u << (c0 >> 6);
+                if (c1 >= 0) dm |= 1u << (c1 >> 6);
+                constexpr uint32_t kOwn = KPAR == 4 ? 0x11111111u : 0x55555555u;   // distances that are multiples of KPAR
+                dm = __reduce_or_sync(DG_FULL_MASK, dm) & ~kOwn;
+                while (dm != 0u && ok) {
+                    const int d = __ffs(dm) - 1;
+                    dm &= dm - 1;
+                    const int w = s - d;
+                    ok = ws_wait(dsl + (w % R) * NSL + sli, (w / R) & 1, abort_flag, p.status);
+                    ok = __all_sync(DG_FULL_MASK, ok);
+                }
+                if (!ok) break;
             }
-            if (ok && s >= 2) ok = ws_wait(rfree + (s & 1), ((s - 2) >> 1) & 1, abort_flag, p.status);
-            if (!__all_sync(DG_FULL_MASK, ok)) break;
-
-            // B = [wq, wk] as the first two of 8 N columns: lanes of group 0 hold wq, group 1 wk
+            const uint32_t own = rows_u + sl * SLOT;
+            // ---- update inputs that do not depend on r ----
+            const int64_t* midx = reinterpret_cast<const int64_t*>(mc + ML.idx) + ts * A;
+            const T* mwk = reinterpret_cast<const T*>(mc + ML.wk) + ts * A;
+            int ucd[4];
+            int64_t ux[4];
+            float uwk[4];
+            uint4 uraw[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int m = mr + 16 * j;                     // rows >= A carry code -2 and are skipped
+                const int mcl = min(m, A - 1);
+                const int cd = fw[m];
+                const int w = s - (cd >> 6);
+                const uint32_t fwd_row = rows_u + (uint32_t)((w % R) * SLOT + (cd & 63) * RS);
+                const uint32_t src = (cd >= 0) ? fwd_row : own + (uint32_t)(m * RS);
+                ucd[j] = cd;
+                ux[j] = midx[mcl];
+                uwk[j] = dg::to_f(mwk[mcl]);
+                uraw[j] = *reinterpret_cast<const uint4*>(rows + (src - rows_u) + sli * 32 + cc * 16);
+            }
+            // ---- GEMV: y and pred of the slice's 16 columns ----
             const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(
                 reinterpret_cast<const uint16_t*>(mc + (g == 0 ? ML.wq : ML.wk)) + ts * A);
             const bool bl = g < 2;
             const int nkb = A >> 4;
-            const uint32_t own = rows_u + sl * SLOT;
             uint32_t b[4][2], base[4];
 #pragma unroll
             for (int kb = 0; kb < 4; ++kb) {
@@ -500,91 +526,56 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16)) p
                 if (kb < nkb) MmaOp<T>::run(acc, a[kb], b[kb][0], b[kb][1]);
             // lanes with tig == 0: acc = {y, pred} of column g and {y, pred} of column g + 8
             if (tig == 0) {
-                const int col0 = mw * 16 + g;
+                const int col0 = sli * 16 + g;                 // column within the part
                 const float bta = dg::to_f(reinterpret_cast<const T*>(mc + ML.beta)[ts]);
                 const T* mv = reinterpret_cast<const T*>(mc + ML.v) + ts * Dh + part * (PB / 2);
                 T* yrow = reinterpret_cast<T*>(ystage + ts * PB);
-                float* rb = rbuf + (s & 1) * 64;
                 yrow[col0] = dg::from_f<T>(acc[0]);
                 yrow[col0 + 8] = dg::from_f<T>(acc[2]);
-                rb[col0] = bta * (dg::to_f(mv[col0]) - acc[1]);
-                rb[col0 + 8] = bta * (dg::to_f(mv[col0 + 8]) - acc[3]);
+                rw[g] = bta * (dg::to_f(mv[col0]) - acc[1]);
+                rw[g + 8] = bta * (dg::to_f(mv[col0 + 8]) - acc[3]);
             }
             __syncwarp();
-            mbar_arrive(rdy + (s & 1));
-            const int t0c = s - ts;
-            const int cend = min(t0c + CHS, T_);
-            if (s + 2 >= cend) {                        // this group's last step of the chunk: flush its rows of y
-                const int nj = (cend - t0c - grp + 1) >> 1;          // rows grp, grp + 2, ... of the chunk
-                for (int i = lane; i < 2 * nj; i += 32) {
-                    const int jj = grp + 2 * (i >> 1), hh = i & 1;
-                    const uint4 val = *reinterpret_cast<const uint4*>(ystage + jj * PB + mw * 32 + hh * 16);
-                    dg::st16(reinterpret_cast<uint8_t*>(gout + (lt0 + t0c + jj) * Dh) + part * PB + mw * 32 + hh * 16, val);
-                }
-                __syncwarp();
-            }
-        }
-    } else {
-        // ================================ update ================================
-        const int ut = tid - 32 * (ROLE_WARPS + 2 * NM);   // 0 .. NU*32-1
-        const int cc = ut % CH;                      // this thread's 16-byte chunk (8 columns)
-        const int m0 = ut / CH;                      // rows m0 and m0 + 32
-        const float alpha_static = p.dynamic_decay ? 1.f : dg::to_f(static_cast<const T*>(p.decay)[lane_bh % p.H]);
-        for (int s = 0; s < T_; ++s) {
-            const int sl = s % R;
-            bool ok = ws_wait(full + sl, (s / R) & 1, abort_flag, p.status);
-            if (!ok) break;
-            const int cn = s / CHS, ts = s % CHS;
-            const uint8_t* mc = meta + (cn % NC) * ML.bytes;
-            const int16_t* fw = reinterpret_cast<const int16_t*>(mc + ML.code) + ts * 64;
-            const int64_t* midx = reinterpret_cast<const int64_t*>(mc + ML.idx) + ts * A;
-            const T* mwk = reinterpret_cast<const T*>(mc + ML.wk) + ts * A;
-            uint8_t* slot = rows + sl * SLOT;
-            // everything that does not depend on r: codes, slots, keys, gathered rows
-            int cd[2];
-            int64_t x[2];
-            float wkv[2];
-            uint4 raw[2];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int m = m0 + 32 * j;                  // rows >= A carry code -2 and are skipped
-                const int mc_ = min(m, A - 1);
-                cd[j] = fw[m];
-                x[j] = midx[mc_];
-                wkv[j] = dg::to_f(mwk[mc_]);
-                raw[j] = *reinterpret_cast<const uint4*>(slot + m * RS + cc * 16);   // gathered row (used when code -1)
-            }
+            const float4 ra = reinterpret_cast<const float4*>(rw + cc * 8)[0];
+            const float4 rb = reinterpret_cast<const float4*>(rw + cc * 8)[1];
+            const float br[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
             const float al = p.dynamic_decay ? dg::to_f(reinterpret_cast<const T*>(mc + ML.alpha)[ts]) : alpha_static;
             const unsigned long long al2 = f2pack(al, al);
-            ok = ws_wait(rdy + (s & 1), (s >> 1) & 1, abort_flag, p.status);
-            if (!ok) break;
-            const float4* rb4 = reinterpret_cast<const float4*>(rbuf + (s & 1) * 64 + cc * 8);
-            const float4 ra = rb4[0], rbv = rb4[1];
-            mbar_arrive(rfree + (s & 1));
-            const float br[8] = {ra.x, ra.y, ra.z, ra.w, rbv.x, rbv.y, rbv.z, rbv.w};
+            // ---- update: new rows (fp32, one rounding) to the ring slot and to global memory ----
+            uint8_t* slot = rows + sl * SLOT;
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                if (cd[j] == -2) continue;               // no row (m >= A or index out of range)
-                const int m = m0 + 32 * j;
-                if (cd[j] >= 0) {                        // forwarded: the writer finished before r was ready
-                    const int w = s - (cd[j] >> 6);
-                    raw[j] = *reinterpret_cast<const uint4*>(rows + (w % R) * SLOT + (cd[j] & 63) * RS + cc * 16);
-                }
-                const uint32_t in[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+            for (int j = 0; j < 4; ++j) {
+                if (ucd[j] == -2) continue;
+                const int m = mr + 16 * j;
+                const uint32_t in[4] = {uraw[j].x, uraw[j].y, uraw[j].z, uraw[j].w};
                 uint32_t o[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const float2 sv = unpack2(in[i], T());
-                    const unsigned long long u = mul_f32x2(f2pack(br[2 * i], br[2 * i + 1]), f2pack(wkv[j], wkv[j]));
+                    const unsigned long long u = mul_f32x2(f2pack(br[2 * i], br[2 * i + 1]), f2pack(uwk[j], uwk[j]));
                     const float2 nv = f2unpack(fma_f32x2(al2, f2pack(sv.x, sv.y), u));
                     o[i] = pack2(nv.x, nv.y, T());
                 }
                 const uint4 nv4 = make_uint4(o[0], o[1], o[2], o[3]);
-                *reinterpret_cast<uint4*>(slot + m * RS + cc * 16) = nv4;
-                dg::st16(gstate + x[j] * row_bytes + cc * 16, nv4);
+                *reinterpret_cast<uint4*>(slot + m * RS + sli * 32 + cc * 16) = nv4;
+                dg::st16(gstate + ux[j] * row_bytes + sli * 32 + cc * 16, nv4);
             }
+            __syncwarp();
+            mbar_arrive(dsl + sl * NSL + sli);
             mbar_arrive(done + sl);
-            if (ts == CHS - 1 || s == T_ - 1) mbar_arrive(mfree + (cn % NC));
+            const int t0c = s - ts;
+            const int cend = min(t0c + CHS, T_);
+            if (s + KPAR >= cend) {                           // this warp's last step of the chunk
+                mbar_arrive(mfree + (cn % NC));
+                const int nj = (cend - t0c - par + KPAR - 1) / KPAR;   // rows par, par + KPAR, ... of y for this slice
+                for (int i = lane; i < 2 * nj; i += 32) {
+                    const int jj = par + KPAR * (i >> 1), hh = i & 1;
+                    const uint4 val = *reinterpret_cast<const uint4*>(ystage + jj * PB + sli * 32 + hh * 16);
+                    dg::st16(reinterpret_cast<uint8_t*>(gout + (lt0 + t0c + jj) * Dh) + part * PB + sli * 32 + hh * 16,
+                             val);
+                }
+                __syncwarp();
+            }
         }
     }
 }
@@ -610,7 +601,7 @@ int launch_ws(const WsParams& p, int lanes, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SL.total);
     if (e != cudaSuccess) return dg_host::record_cuda_error(e);
     dim3 grid(p.parts, lanes);
-    kern<<<grid, 32 * (ROLE_WARPS + 2 * (PB / 32) + PB / 16), SL.total, stream>>>(p);
+    kern<<<grid, 32 * (ROLE_WARPS + KPAR * (PB / 32)), SL.total, stream>>>(p);
     return dg_host::check_launch();
 }
 
