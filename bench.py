@@ -37,9 +37,9 @@ WORKLOADS = {
     "cfg2": dict(kind="dense", B=32, H=16, T=4096, S=512, Dh=64, dtype="float16",
                  desc="dense fp16 B=32 H=16 T=4096 Dh=64 slots=512"),
     "cfg3": dict(kind="pkm", B=16, H=8, T=8192, G=128, K=8, Dh=64, dtype="float16",
-                 desc="PKM fp16 B=16 H=8 T=8192 Dh=64 grid 128x128 top-8"),
-    "cfg4": dict(kind="pkm", B=8, H=8, T=16384, G=1024, K=8, Dh=64, dtype="float16",
-                 desc="PKM fp16 B=8 H=8 T=16384 Dh=64 grid 1024x1024 top-8"),
+                 desc="PKM fp16 B=16 H=8 T=8192 Dh=64 grid 128x128 top-8, routed keys"),
+    "cfg4": dict(kind="pkm", B=8, H=8, T=16384, G=1024, K=8, Dh=64, dtype="float16", writes=True,
+                 desc="PKM fp16 B=8 H=8 T=16384 Dh=64 grid 1024x1024 top-8, write stream (beta=1)"),
 }
 METRIC = "recurrence tokens/sec"
 UNIT = "tokens/s"
@@ -140,25 +140,32 @@ def make_inputs(w, torch, device, seed=0):
         decay = torch.ones(H, device=device, dtype=dt)
         return dict(q=v, k=v, v=v, beta=beta, wk=wk, wq=wq, decay=decay)
     G, K = w["G"], w["K"]
-    A = K * K
     total = G * G
-    # routing indices: K distinct per axis from a random permutation window, idx = i0*G + i1
-    i0 = torch.randint(0, G, (B, H, T, 1), device=device, generator=g)
-    i1 = torch.randint(0, G, (B, H, T, 1), device=device, generator=g)
-    ar = torch.arange(K, device=device)
-    s0 = torch.randint(1, G, (B, H, T, 1), device=device, generator=g)   # stride coprime-ish -> distinct
-    a0 = (i0 + ar * 1) % G
-    a1 = (i1 + ar * (s0 | 1)) % G
-    idx = (a0.unsqueeze(-1) * G + a1.unsqueeze(-2)).flatten(-2).to(torch.int64)
-    u0 = F.normalize(torch.rand(B, H, T, K, device=device, generator=g) + 0.1, dim=-1)
-    u1 = F.normalize(torch.rand(B, H, T, K, device=device, generator=g) + 0.1, dim=-1)
-    wk = (u0.unsqueeze(-1) * u1.unsqueeze(-2)).flatten(-2).to(dt)
-    wq = (torch.randn(B, H, T, A, device=device, generator=g) / K).to(dt)
+    # routing as the layer does it (memory.py:240-289), on the GPU: two router axes of
+    # G rows ~ N(0, 1/Dh) shared by keys and queries (memory.py:156-159)
+    from deltagrid_b200.route import pkm_route
+    gr = torch.Generator().manual_seed(seed + 1)
+    routers = [(torch.randn(G, Dh, generator=gr) / Dh ** 0.5).to(device) for _ in range(2)]
+    k = F.normalize(torch.randn(B, H, T, Dh, device=device, generator=g), dim=-1)
+    if w.get("writes"):
+        # write stream: random unit keys and values, beta = 1, read-out with the same key
+        q = k
+        beta = torch.ones(B, H, T, device=device, dtype=dt)
+    else:
+        q = torch.randn(B, H, T, Dh, device=device, generator=g)
+        beta = torch.sigmoid(torch.randn(B, H, T, device=device, generator=g)).to(dt)
+    wk, wq, idx = pkm_route(k.to(dt), q.to(dt), routers, routers, K)
+    del k, q
     v = F.normalize(torch.randn(B, H, T, Dh, device=device, generator=g), dim=-1).to(dt)
-    beta = torch.sigmoid(torch.randn(B, H, T, device=device, generator=g)).to(dt)
     decay = torch.ones(H, device=device, dtype=dt)
     state = torch.zeros(B, H, total, Dh, device=device, dtype=dt)
     return dict(v=v, beta=beta, wk=wk, wq=wq, idx=idx, decay=decay, state=state)
+
+
+def launches_per_step(w):
+    """Kernels one step launches: the dense kernel; for 16-bit PKM the hazard pre-pass
+    and the recurrence (pkm_hazard_kernel, pkm_ws_kernel)."""
+    return 2 if w["kind"] == "pkm" and w["dtype"] != "float32" else 1
 
 
 def run_step(ext, w, d):
@@ -414,6 +421,7 @@ def main():
     roofline = {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s",
                 "frac": achieved_gbs / hbm, "traffic": traffic, "peak_source": peak_src,
                 "algorithmic_bytes_per_launch": bytes_alg, "launch_ms": launch_ms,
+                "kernels_timed": launches_per_step(w),
                 "tensor_tflops_achieved": flops_alg / (launch_ms / 1e3) / 1e12}
 
     cpu = None
@@ -428,7 +436,8 @@ def main():
         "config": {"workload": f"{args.workload}: {w['desc']}", "global_batch": w["B"] * world,
                    "per_gpu_batch": w["B"], "seq_len": w["T"], "parallelism": f"dp{world} (batch shards)",
                    "l2": "inputs larger than L2 (no flush)"},
-        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": args.steps * launches_per_step(w),
         "clocks": clk.summary(),
         "verify": {"output_checksums_per_rank": verify},
     }

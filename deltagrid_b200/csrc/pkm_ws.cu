@@ -13,9 +13,9 @@
 //   from global memory, -2 no row (m >= A, or an index out of range, which is
 //   flagged), else (t - w) << 6 | position of the slot in step w.  A CTA
 //   resolves 48 steps of one lane plus D-1 steps of lookback in parallel: all
-//   (slot, step, position) entries go into a shared-memory open-addressing
-//   table that is never more than half full, so every insert finds a cell and
-//   every code is exact; then every row of the 48 steps scans its probe run.
+//   (slot, step, position) entries are bucket-sorted in shared memory (counting
+//   sort: one 32-bit atomicAdd per entry, a block prefix sum), then every row of
+//   the 48 steps scans its bucket.  Exact, with no capacity to overflow.
 //
 // pkm_ws_kernel -- the recurrence.  One CTA per (lane, part of the row); four
 //   roles run concurrently on a ring of R = 2D row slots, synchronised by
@@ -59,12 +59,12 @@ constexpr int NGATH = 128;              // gather threads (four warps)
 constexpr int ROLE_WARPS = 5;           // loader 1, gather 4 (then KPAR warps per 16-column slice)
 constexpr int KPAR = 4;                 // warps per column slice; warp k takes the steps s with s % KPAR == k
 constexpr int HZ_STEPS = 48;            // steps resolved per pre-pass CTA
-constexpr int HZ_CELLS = 8192;          // pre-pass table cells: >= 2 x (48 + 15) x 64 entries
+constexpr int HZ_BUCKETS = 1024;        // pre-pass hash buckets (counting sort)
 constexpr int HZ_THREADS = 512;
 constexpr int HZ_MAXWIN = 16;           // largest window depth D the pre-pass covers
 constexpr int HZ_KMAX = ((HZ_STEPS + HZ_MAXWIN - 1) * MAXA + HZ_THREADS - 1) / HZ_THREADS;   // entries per thread
 static_assert(HZ_KMAX * HZ_THREADS >= (HZ_STEPS + HZ_MAXWIN - 1) * MAXA, "pre-pass entry slots");
-static_assert(2 * (HZ_STEPS + HZ_MAXWIN - 1) * MAXA <= HZ_CELLS, "pre-pass table at most half full");
+constexpr int HZ_ENTRIES = (HZ_STEPS + HZ_MAXWIN - 1) * MAXA;   // most (slot, step, position) entries per block
 
 struct WsParams {
     const void* v;
@@ -128,43 +128,81 @@ __device__ __forceinline__ uint32_t slot_home(uint32_t x) {
     x ^= x >> 13;
     x *= 0xc2b2ae35u;
     x ^= x >> 16;
-    return x & (HZ_CELLS - 1);
+    return x >> (32 - 10);                                     // HZ_BUCKETS = 1024
 }
 
 // ---------------------------------------------------------------------------
-// pre-pass: row codes of steps [blockIdx.x * HZ_STEPS, +HZ_STEPS) of lane blockIdx.y
+// pre-pass: row codes of steps [blockIdx.x * HZ_STEPS, +HZ_STEPS) of lane blockIdx.y.
+// The block's (slot, step, position) entries are bucket-sorted in shared memory
+// (one 32-bit atomicAdd per entry gives its rank in its bucket, a block prefix sum
+// the bucket starts), then every row scans its bucket for the latest earlier step
+// with the same slot.  Exact: there is no capacity limit to overflow.
+template <int A>
 __global__ void __launch_bounds__(HZ_THREADS) pkm_hazard_kernel(const int64_t* __restrict__ idx, int16_t* codes,
-                                                                int32_t* status, int T, int A, int64_t total, int D) {
-    extern __shared__ unsigned long long cells[];          // [HZ_CELLS]
-    const int tid = threadIdx.x;
-    const int lane = blockIdx.y;
+                                                                int32_t* status, int T, int64_t total, int D) {
+    extern __shared__ __align__(16) uint8_t hz_smem[];
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(hz_smem);                 // [HZ_BUCKETS] entries per bucket
+    uint32_t* start = cnt + HZ_BUCKETS;                                    // [HZ_BUCKETS] first entry of a bucket
+    uint32_t* wsum = start + HZ_BUCKETS;                                   // [HZ_THREADS / 32] scan partials
+    unsigned long long* ent = reinterpret_cast<unsigned long long*>(wsum + 32);   // [HZ_ENTRIES] sorted
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int lid = blockIdx.y;
     const int t0 = blockIdx.x * HZ_STEPS;
     const int tb = max(0, t0 - (D - 1));
     const int te = min(T, t0 + HZ_STEPS);
     const int nE = (te - tb) * A;
-    const int64_t* li = idx + ((int64_t)lane * T + tb) * A;
-    int16_t* lc = codes + (int64_t)lane * T * 64;
-    for (int i = tid; i < HZ_CELLS; i += HZ_THREADS) cells[i] = 0ull;
-    __syncthreads();
-    int64_t xs[HZ_KMAX];
+    const int64_t* li = idx + ((int64_t)lid * T + tb) * A;
+    int16_t* lc = codes + (int64_t)lid * T * 64;
+    for (int i = tid; i < HZ_BUCKETS; i += HZ_THREADS) cnt[i] = 0u;
+    uint32_t key[HZ_KMAX], bkt[HZ_KMAX];
 #pragma unroll
     for (int k = 0; k < HZ_KMAX; ++k) {
         const int e = tid + k * HZ_THREADS;
-        xs[k] = -1;
+        key[k] = 0u;
         if (e < nE) {
             const int64_t x = li[e];
-            xs[k] = x;
-            if (x >= 0 && x < total) {
-                const int tl = e / A, m = e - tl * A;          // step relative to tb, position
-                const unsigned long long ent =
-                    (unsigned long long)((uint32_t)x + 1u) | ((unsigned long long)(((uint32_t)tl << 6) | (uint32_t)m) << 32);
-                uint32_t h = slot_home((uint32_t)x);
-                for (int probe = 0; probe < HZ_CELLS; ++probe) {  // the table is at most half full
-                    if (atomicCAS(cells + h, 0ull, ent) == 0ull) break;
-                    h = (h + 1) & (HZ_CELLS - 1);
-                }
-            }
+            if (x >= 0 && x < total) key[k] = (uint32_t)x + 1u;
+            else if (tb + e / A >= t0) dg::flag_status(status, DG_DEVCHK_INDEX_RANGE);
         }
+        bkt[k] = slot_home(key[k] - 1u);
+    }
+    __syncthreads();
+    uint32_t rank[HZ_KMAX];
+#pragma unroll
+    for (int k = 0; k < HZ_KMAX; ++k) rank[k] = key[k] ? atomicAdd(cnt + bkt[k], 1u) : 0u;
+    __syncthreads();
+    // exclusive prefix sum of the bucket counts: two buckets per thread
+    {
+        const uint32_t c0 = cnt[2 * tid], c1 = cnt[2 * tid + 1];
+        uint32_t v = c0 + c1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t u = __shfl_up_sync(DG_FULL_MASK, v, o);
+            if (lane >= o) v += u;
+        }
+        if (lane == 31) wsum[warp] = v;
+        __syncthreads();
+        if (warp == 0) {
+            uint32_t wv = lane < HZ_THREADS / 32 ? wsum[lane] : 0u;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t u = __shfl_up_sync(DG_FULL_MASK, wv, o);
+                if (lane >= o) wv += u;
+            }
+            if (lane < HZ_THREADS / 32) wsum[lane] = wv;          // inclusive warp totals
+        }
+        __syncthreads();
+        const uint32_t base = (warp ? wsum[warp - 1] : 0u) + v - (c0 + c1);
+        start[2 * tid] = base;
+        start[2 * tid + 1] = base + c0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < HZ_KMAX; ++k) {
+        if (!key[k]) continue;
+        const int e = tid + k * HZ_THREADS;
+        const int tl = e / A, m = e - tl * A;
+        ent[start[bkt[k]] + rank[k]] = (unsigned long long)key[k] | ((unsigned long long)(((uint32_t)tl << 6) | (uint32_t)m) << 32);
     }
     __syncthreads();
 #pragma unroll
@@ -174,25 +212,19 @@ __global__ void __launch_bounds__(HZ_THREADS) pkm_hazard_kernel(const int64_t* _
         const int tl = e / A, m = e - tl * A;
         const int t = tb + tl;
         if (t < t0) continue;                                   // lookback rows only feed the table
-        const int64_t x = xs[k];
         int cd = -2;
-        if (x >= 0 && x < total) {
-            const uint32_t key = (uint32_t)x + 1u;
-            uint32_t h = slot_home((uint32_t)x);
+        if (key[k]) {
+            const uint32_t b0 = start[bkt[k]], n = cnt[bkt[k]];
             int best = -1, bpos = 0;
-            for (int probe = 0; probe < HZ_CELLS; ++probe) {
-                const unsigned long long c = cells[h];
-                if (c == 0ull) break;
-                if ((uint32_t)c == key) {
+            for (uint32_t q = 0; q < n; ++q) {
+                const unsigned long long c = ent[b0 + q];
+                if ((uint32_t)c == key[k]) {
                     const uint32_t st = (uint32_t)(c >> 32);
                     const int wl = (int)(st >> 6);
                     if (wl < tl && wl > best) { best = wl; bpos = (int)(st & 63); }
                 }
-                h = (h + 1) & (HZ_CELLS - 1);
             }
             cd = (best >= 0 && tl - best <= D - 1) ? (((tl - best) << 6) | bpos) : -1;
-        } else {
-            dg::flag_status(status, DG_DEVCHK_INDEX_RANGE);
         }
         lc[(int64_t)t * 64 + m] = (int16_t)cd;
     }
@@ -636,11 +668,13 @@ int pkm_forward_ws(int dtype, int B, int H, int T, int A, int64_t total, int Dh,
     const int D = PB == 128 ? kDepthFull : kDepthHalf;
     const int lanes = B * H;
     int16_t* codes = static_cast<int16_t*>(workspace);
-    const int hz_smem = HZ_CELLS * 8;
-    cudaError_t e = cudaFuncSetAttribute(pkm_hazard_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, hz_smem);
+    const int hz_smem = (2 * HZ_BUCKETS + 32) * 4 + HZ_ENTRIES * 8;
+    const dim3 hz_grid((T + HZ_STEPS - 1) / HZ_STEPS, lanes);
+    auto hz = A == 16 ? pkm_hazard_kernel<16> : A == 32 ? pkm_hazard_kernel<32> : A == 48 ? pkm_hazard_kernel<48>
+                                                                                         : pkm_hazard_kernel<64>;
+    cudaError_t e = cudaFuncSetAttribute(hz, cudaFuncAttributeMaxDynamicSharedMemorySize, hz_smem);
     if (e != cudaSuccess) return record_cuda_error(e);
-    pkm_hazard_kernel<<<dim3((T + HZ_STEPS - 1) / HZ_STEPS, lanes), HZ_THREADS, hz_smem, stream>>>(idx, codes, status,
-                                                                                                  T, A, total, D);
+    hz<<<hz_grid, HZ_THREADS, hz_smem, stream>>>(idx, codes, status, T, total, D);
     int rc = check_launch();
     if (rc != DG_OK) return rc;
     WsParams p{v, beta, wk, wq, idx, decay, state, out, status, H, T, A, Dh, parts, total, dynamic_decay, codes};
