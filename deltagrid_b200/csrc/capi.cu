@@ -40,7 +40,7 @@ bool pkm_ws_supports(int dtype, int B, int H, int T, int A, int64_t total, int D
                      const void* state, const void* saved);
 int pkm_forward_ws(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
                    const void* wk, const void* wq, const int64_t* idx, const void* decay, int dynamic_decay,
-                   void* state, void* out, int32_t* status, void* workspace, cudaStream_t stream);
+                   void* state, void* out, void* saved, int32_t* status, void* workspace, cudaStream_t stream);
 size_t pkm_ws_workspace_bytes(int B, int H, int T);
 
 }  // namespace dg_host
@@ -119,7 +119,7 @@ size_t dg_pkm_forward_workspace_size(int dtype, int B, int H, int T, int active,
     if (algo == DG_PKM_AUTO && T < 64) return 0;
     // shape-level check only (alignment is not known here): 16-byte-aligned placeholder pointers
     const void* a = reinterpret_cast<const void*>(uintptr_t(256));
-    if (!pkm_ws_supports(dtype, B, H, T, active, total_slots, dh, a, a, a, a, a, a, 0, a, nullptr)) return 0;
+    if (!pkm_ws_supports(dtype, B, H, T, active, total_slots, dh, a, a, a, a, a, a, 0, a, a)) return 0;
     return pkm_ws_workspace_bytes(B, H, T);
 }
 
@@ -151,14 +151,14 @@ int dg_pkm_forward_ex(int dtype, int B, int H, int T, int active, int64_t total_
         if (workspace) {
             if (workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15)) return DG_ERR_WORKSPACE;
             return pkm_forward_ws(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
-                                  dynamic_decay, state, out, dev_status, workspace, s);
+                                  dynamic_decay, state, out, saved_s_act, dev_status, workspace, s);
         }
         // no caller workspace: stream-ordered allocation from the device's default pool
         void* w = nullptr;
         cudaError_t e = cudaMallocAsync(&w, need, s);
         if (e != cudaSuccess) return record_cuda_error(e);
         const int rc = pkm_forward_ws(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay,
-                                      dynamic_decay, state, out, dev_status, w, s);
+                                      dynamic_decay, state, out, saved_s_act, dev_status, w, s);
         e = cudaFreeAsync(w, s);
         if (rc != DG_OK) return rc;
         return e == cudaSuccess ? DG_OK : record_cuda_error(e);

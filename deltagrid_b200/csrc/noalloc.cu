@@ -56,9 +56,7 @@ int dg_pkm_forward_noalloc(int dtype, int B, int H, int T, int active, int64_t t
                            const void* v, const void* beta, const void* wk, const void* wq, const int64_t* idx,
                            const void* decay, int dynamic_decay, void* state, void* out, void* saved_s_act,
                            int32_t* dev_status, void* stream) {
-    const size_t need = saved_s_act ? 0
-                                    : dg_pkm_forward_workspace_size(dtype, B, H, T, active, total_slots, dh,
-                                                                    DG_PKM_AUTO);
+    const size_t need = dg_pkm_forward_workspace_size(dtype, B, H, T, active, total_slots, dh, DG_PKM_AUTO);
     if (need > kNoAllocBytes) return DG_ERR_WORKSPACE;
     void* ws = nullptr;
     if (need) {

@@ -55,8 +55,12 @@ constexpr int MAXA = 64;
 constexpr int CHS = 16;                 // steps per metadata chunk
 constexpr int NC = 3;                   // metadata chunks resident
 constexpr int NLOAD = 32;               // loader threads (one warp)
-constexpr int NGATH = 128;              // gather threads (four warps)
-constexpr int ROLE_WARPS = 5;           // loader 1, gather 4 (then KPAR warps per 16-column slice)
+// gather threads: four warps for 64-byte row parts; two for 128-byte parts, whose
+// 16 slice warps leave no registers for more
+template <int PB> struct GatherCfg {
+    static constexpr int NGATH = PB == 128 ? 64 : 128;
+    static constexpr int ROLE_WARPS = 1 + NGATH / 32;       // loader, gather (then KPAR warps per 16-column slice)
+};
 constexpr int KPAR = 4;                 // warps per column slice; warp k takes the steps s with s % KPAR == k
 constexpr int HZ_STEPS = 48;            // steps resolved per pre-pass CTA
 constexpr int HZ_BUCKETS = 1024;        // pre-pass hash buckets (counting sort)
@@ -80,6 +84,7 @@ struct WsParams {
     int64_t total;
     int dynamic_decay;
     const int16_t* codes;       // [lanes, T, 64] from pkm_hazard_kernel
+    void* saved;                // [lanes, T, A, Dh] rows as gathered at each step, or null
 };
 
 struct MetaLayout {
@@ -348,7 +353,9 @@ __device__ __forceinline__ unsigned long long fma_f32x2(unsigned long long a, un
 }
 
 template <typename T, int PB, int D>
-__global__ void __launch_bounds__(32 * (ROLE_WARPS + KPAR * (PB / 32))) pkm_ws_kernel(WsParams p) {
+__global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + KPAR * (PB / 32))) pkm_ws_kernel(WsParams p) {
+    constexpr int NGATH = GatherCfg<PB>::NGATH;
+    constexpr int ROLE_WARPS = GatherCfg<PB>::ROLE_WARPS;
     constexpr int CH = PB / 16;          // 16-byte chunks per row part
     constexpr int NSL = PB / 32;         // column slices of 16 columns; KPAR warps per slice take turns by step
     constexpr int RS = PB + 16;          // padded row stride: conflict-free ldmatrix / 16-byte accesses
@@ -577,8 +584,13 @@ __global__ void __launch_bounds__(32 * (ROLE_WARPS + KPAR * (PB / 32))) pkm_ws_k
             uint8_t* slot = rows + sl * SLOT;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                if (ucd[j] == -2) continue;
                 const int m = mr + 16 * j;
+                // rows as gathered (zeros for an index out of range: its ring row was zero-filled)
+                if (p.saved != nullptr && m < A)
+                    dg::st16(static_cast<uint8_t*>(p.saved) + ((lt0 + s) * A + m) * row_bytes + part * PB + sli * 32 +
+                                 cc * 16,
+                             uraw[j]);
+                if (ucd[j] == -2) continue;
                 const uint32_t in[4] = {uraw[j].x, uraw[j].y, uraw[j].z, uraw[j].w};
                 uint32_t o[4];
 #pragma unroll
@@ -633,7 +645,7 @@ int launch_ws(const WsParams& p, int lanes, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SL.total);
     if (e != cudaSuccess) return dg_host::record_cuda_error(e);
     dim3 grid(p.parts, lanes);
-    kern<<<grid, 32 * (ROLE_WARPS + KPAR * (PB / 32)), SL.total, stream>>>(p);
+    kern<<<grid, 32 * (GatherCfg<PB>::ROLE_WARPS + KPAR * (PB / 32)), SL.total, stream>>>(p);
     return dg_host::check_launch();
 }
 
@@ -646,7 +658,6 @@ size_t pkm_ws_workspace_bytes(int B, int H, int T) { return (size_t)B * H * T * 
 bool pkm_ws_supports(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
                      const void* wk, const void* wq, const void* idx, const void* decay, int dynamic_decay,
                      const void* state, const void* saved) {
-    if (saved) return false;
     if (dtype != DG_DTYPE_F16 && dtype != DG_DTYPE_BF16) return false;
     if (A < 16 || A > MAXA || A % 16 != 0 || T < 1 || T % 8 != 0) return false;   // whole 16-row MMA blocks
     if (total >= (int64_t)0x7fffffff - 1 || T >= (1 << 25)) return false;
@@ -655,14 +666,14 @@ bool pkm_ws_supports(int dtype, int B, int H, int T, int A, int64_t total, int D
     const int D = PB == 128 ? kDepthFull : kDepthHalf;
     if (smem_layout(PB, D, A, Dh).total > 232448) return false;
     const uintptr_t al = (uintptr_t)v | (uintptr_t)beta | (uintptr_t)wk | (uintptr_t)wq | (uintptr_t)idx |
-                         (uintptr_t)state | (dynamic_decay ? (uintptr_t)decay : 0);
+                         (uintptr_t)state | (dynamic_decay ? (uintptr_t)decay : 0) | (uintptr_t)saved;
     return (al & 15) == 0;
 }
 
 // workspace: pkm_ws_workspace_bytes(B, H, T) bytes, 16-byte aligned
 int pkm_forward_ws(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
                    const void* wk, const void* wq, const int64_t* idx, const void* decay, int dynamic_decay,
-                   void* state, void* out, int32_t* status, void* workspace, cudaStream_t stream) {
+                   void* state, void* out, void* saved, int32_t* status, void* workspace, cudaStream_t stream) {
     const int PB = ws_part_bytes(B, H, Dh);
     const int parts = Dh * 2 / PB;
     const int D = PB == 128 ? kDepthFull : kDepthHalf;
@@ -677,7 +688,7 @@ int pkm_forward_ws(int dtype, int B, int H, int T, int A, int64_t total, int Dh,
     hz<<<hz_grid, HZ_THREADS, hz_smem, stream>>>(idx, codes, status, T, total, D);
     int rc = check_launch();
     if (rc != DG_OK) return rc;
-    WsParams p{v, beta, wk, wq, idx, decay, state, out, status, H, T, A, Dh, parts, total, dynamic_decay, codes};
+    WsParams p{v, beta, wk, wq, idx, decay, state, out, status, H, T, A, Dh, parts, total, dynamic_decay, codes, saved};
     if (dtype == DG_DTYPE_F16)
         return PB == 128 ? launch_ws<__half, 128, kDepthFull>(p, lanes, stream)
                          : launch_ws<__half, 64, kDepthHalf>(p, lanes, stream);

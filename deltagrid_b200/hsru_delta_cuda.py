@@ -218,8 +218,7 @@ def pkm_forward_algo(v: torch.Tensor, beta: torch.Tensor, wk: torch.Tensor, wq: 
     dynamic = 1 if decay_c.dim() > 1 else 0
     with torch.cuda.device(v_c.device):
         # scratch for kernels that need it (per-row hazard codes), from torch's caching allocator
-        nws = _lib.lib().dg_pkm_forward_workspace_size(code, B, H, T, A, total, Dh, int(algo)) \
-            if saved is None else 0
+        nws = _lib.lib().dg_pkm_forward_workspace_size(code, B, H, T, A, total, Dh, int(algo))
         ws = torch.empty(nws, dtype=torch.uint8, device=v_c.device) if nws else None
         _lib.call("dg_pkm_forward_ex", code, B, H, T, A, total, Dh, v_c.data_ptr(), beta_c.data_ptr(),
                   wk_c.data_ptr(), wq_c.data_ptr(), idx_c.data_ptr(), decay_c.data_ptr(), dynamic,

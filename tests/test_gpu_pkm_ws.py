@@ -157,3 +157,23 @@ def test_ws_rejects_uncovered_shapes():
     d = pkm_inputs(1, 1, 64, 8, 4, 64, torch.float32, seed=1)       # fp32 state
     with pytest.raises(_lib.DeltaGridError):
         _run(d, WS)
+
+
+def test_ws_saved_rows_match_one_step_kernel():
+    # the reference layer always calls pkm_forward with save_for_backward=True
+    # (src/ops/_autograd.py:132): the gathered rows of every step, [B,H,T,A,Dh]
+    d = pkm_inputs(2, 4, 128, 16, 8, 64, torch.float16, dynamic=True, seed=17, s_init_scale=0.3)
+    idx = d["idx"].clone()
+    idx[1, 2, 7, 5] = -1                                   # an out-of-range row saves zeros
+    d["idx"] = idx
+    res = {}
+    for algo in (WS, ONE):
+        g = {n: t.cuda() for n, t in d.items()}
+        out, st, saved = ext.pkm_forward_algo(g["v"], g["beta"], g["wk"], g["wq"], g["idx"], g["decay"],
+                                              g["state"], True, algo)
+        torch.cuda.synchronize()
+        ext.device_status(clear=True)
+        res[algo] = (out.float().cpu(), st.float().cpu(), saved.float().cpu())
+    for a, b in zip(res[WS], res[ONE]):
+        assert rel_err(a.numpy(), b.numpy()) < 1e-3
+    assert torch.count_nonzero(res[WS][2][1, 2, 7, 5]) == 0
