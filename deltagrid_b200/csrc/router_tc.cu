@@ -1,0 +1,465 @@
+// router_tc.cu -- two-axis product-key router with tensor-core scores (16-bit keys).
+//
+// Same result as router.cu (DeltaGridLayer._route_sparse_pkm, src/modules/memory.py:240-289,
+// and the q_scale multiply of memory.py:453-455), for Dh = 64, top-k in {4, 8}:
+//   1. scores for all router rows as a tcgen05 GEMM: 128 tokens (one per TMEM lane) x
+//      up to 256 router rows per MMA block, K = 64; the two axes run side by side in
+//      two warpgroups, each with its own TMEM columns and router buffer.  The fp32
+//      router is split into two 16-bit parts (hi + lo), so the product is fp32-accurate
+//      up to the tensor core's accumulation; blocks stream through shared memory by TMA;
+//   2. each thread keeps its token's 16 best approximate scores (value descending,
+//      index ascending);
+//   3. exactness: with |approx - exact| <= delta (delta = c * sum|k| * max|W|, c
+//      covering the split residual, the accumulation and the sequential-sum error),
+//      every exact top-k member scores >= approx_k - 2 delta.  Those candidates are
+//      rescored in the sequential fp32 order of the CPU oracle (each product and sum
+//      rounded separately) and the top-k taken with the lower-index-first tie order
+//      (src/cpp/engine/src/deltagrid_math.cpp:155-167), so indices are exact.  A
+//      token whose 16th approximate score is still inside the window rescans all
+//      rows exactly;
+//   4. u_k, u_q (queries scored at the selected rows), normalisation, Kronecker.
+#include <cuda.h>
+
+#include "dg_common.cuh"
+#include "tc_util.cuh"
+
+namespace {
+
+constexpr int RT_M = 128;        // tokens per CTA
+constexpr int RT_NMAX = 128;     // router rows per MMA block (256 TMEM columns per CTA: two CTAs per SM)
+constexpr int RT_E = 16;         // approximate candidates kept per token and axis
+constexpr int RT_DH = 64;
+
+constexpr uint32_t SM_KT = 0;                              // K tile: 128 rows x 128 B, 128B swizzle
+constexpr uint32_t SM_W = 16384;                           // per axis (hi, lo) x 256 rows x 128 B
+constexpr uint32_t SM_WPART = RT_NMAX * 128;
+constexpr uint32_t SM_AX0 = SM_W;                           // results [axis][3][8][128] (u_k, u_q, index), over the
+                                                            // router buffers once every block is scored
+constexpr uint32_t SM_STASH = SM_W + 4 * SM_WPART;          // [axis][16][128] scores of the chunk being merged
+constexpr uint32_t SM_BAR = SM_STASH + 2 * 16 * RT_M * 4;
+static_assert(2 * 3 * 8 * RT_M * 4 <= 4 * SM_WPART, "results fit over the router buffers");
+constexpr uint32_t SM_BYTES = SM_BAR + 8 * 8;
+
+struct RtParams {
+    const void* k;
+    const void* q;
+    const float* wk[2];
+    const float* wq[2];
+    const float* q_scale;        // [H] or null
+    const unsigned* wmax;        // [2] max |router_k| per axis (float bits)
+    void* out_wk;
+    void* out_wq;
+    int64_t* out_idx;
+    int64_t N;
+    int H, T, nrows;
+    int G[2];
+    float delta_scale;
+    int32_t* status;
+};
+
+__device__ __forceinline__ bool ranks_before(float a, int ia, float b, int ib) {
+    return (a > b) | ((a == b) & (ia < ib));
+}
+
+// NC independent sequential fp32 dots over 64 (each product and sum rounded, the
+// oracle's order), interleaved so their dependency chains overlap.  x: this token's
+// 64 values, 16-byte chunks at xoff(c); w[j]: router rows.
+template <int NC, typename LoadX>
+__device__ __forceinline__ void exact_dots(LoadX load_x, const float* const (&w)[NC], float (&out)[NC]) {
+#pragma unroll
+    for (int j = 0; j < NC; ++j) out[j] = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+        float xv[8];
+        load_x(c, xv);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float4 wv[NC];
+#pragma unroll
+            for (int j = 0; j < NC; ++j) wv[j] = __ldg(reinterpret_cast<const float4*>(w[j] + 8 * c + 4 * h));
+#pragma unroll
+            for (int j = 0; j < NC; ++j) {
+                out[j] = __fadd_rn(out[j], __fmul_rn(wv[j].x, xv[4 * h + 0]));
+                out[j] = __fadd_rn(out[j], __fmul_rn(wv[j].y, xv[4 * h + 1]));
+                out[j] = __fadd_rn(out[j], __fmul_rn(wv[j].z, xv[4 * h + 2]));
+                out[j] = __fadd_rn(out[j], __fmul_rn(wv[j].w, xv[4 * h + 3]));
+            }
+        }
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(uint4 v, float (&x)[8]) {
+    const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = dg::to_f(e[i]);
+}
+
+// 256 threads: warps 0-3 route axis 0, warps 4-7 axis 1, of the same 128 tokens
+// (thread t of a group owns token t and TMEM lane t; each axis owns 256 TMEM columns).
+template <typename T, int K>
+__global__ void __launch_bounds__(2 * RT_M, 2)
+    router_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmhi,
+                     const __grid_constant__ CUtensorMap tmlo, RtParams p) {
+    constexpr bool BF16 = !std::is_same<T, __half>::value;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* kt = sm + SM_KT;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + SM_BAR);
+    uint64_t* bar_kt = bars;           // K tile landed
+    uint64_t* bar_w = bars + 1;        // [axis] router block landed
+    uint64_t* bar_a = bars + 3;        // [axis] scores of a block in TMEM (router buffer read)
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 5);
+    float* res = reinterpret_cast<float*>(sm + SM_AX0);         // [axis][3][8][RT_M] u_k, u_q, index
+    uint32_t* stash = reinterpret_cast<uint32_t*>(sm + SM_STASH);   // [axis][16][RT_M]
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int ax = warp >> 2;                      // axis of this thread's group
+    const int t = tid & (RT_M - 1);                // token within the tile = TMEM lane
+    const int64_t n0 = (int64_t)blockIdx.x * RT_M;
+    const int64_t n = n0 + t;
+    const int nrows = p.nrows;
+    const int G = p.G[ax];
+    const int nb = G / nrows;
+    const uint32_t wpart = (uint32_t)nrows * 128u;
+    const uint32_t idesc = tc::make_idesc(128, nrows, BF16 ? 1 : 0, 0, 0);
+    const bool issuer = t == 0;
+    uint8_t* whi = sm + SM_W + (uint32_t)(2 * ax) * SM_WPART;
+    uint8_t* wlo = whi + SM_WPART;
+    const int wrow0 = ax ? p.G[0] : 0;
+
+    auto load_w = [&](int j) {
+        tc::mbar_expect_tx(bar_w + ax, 2 * wpart);
+        tc::tma_load_2d(whi, &tmhi, bar_w + ax, 0, wrow0 + j * nrows);
+        tc::tma_load_2d(wlo, &tmlo, bar_w + ax, 0, wrow0 + j * nrows);
+    };
+
+    if (warp == 0) tc::tmem_alloc(tmem_holder, 2 * RT_NMAX);
+    if (tid == 0) {
+        for (int i = 0; i < 5; ++i) tc::mbar_init(bars + i, 1);
+        tc::fence_barrier_init();
+        tc::prefetch_tmap(&tmk);
+        tc::prefetch_tmap(&tmhi);
+        tc::prefetch_tmap(&tmlo);
+        tc::mbar_expect_tx(bar_kt, RT_M * 128);
+        tc::tma_load_2d(kt, &tmk, bar_kt, 0, (int)n0);
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    if (issuer) load_w(0);
+    const uint32_t tmem = *tmem_holder;
+    const uint32_t tacc = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)ax * RT_NMAX;
+
+    auto issue = [&]() {
+        const uint32_t d = tmem + (uint32_t)ax * RT_NMAX;
+        const uint32_t a0 = tc::smem_u32(kt);
+#pragma unroll
+        for (int lo = 0; lo < 2; ++lo) {
+            const uint32_t b0 = tc::smem_u32(lo ? wlo : whi);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+                tc::mma_f16(d, tc::make_desc(a0 + 32 * kk, 16, 1024), tc::make_desc(b0 + 32 * kk, 16, 1024), idesc,
+                            (lo | kk) != 0);
+        }
+        tc::mma_commit(bar_a + ax);
+    };
+
+    bool bad = !tc::mbar_wait(bar_kt, 0);
+    // sum |k| of this token, for the error bound
+    float kabs = 0.f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        float x[8];
+        unpack8<T>(*reinterpret_cast<const uint4*>(kt + tc::sw128(t, c)), x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) kabs += fabsf(x[e]);
+    }
+
+    float lv[RT_E];
+    int li[RT_E];
+#pragma unroll
+    for (int i = 0; i < RT_E; ++i) { lv[i] = -INFINITY; li[i] = 0x7fffffff; }
+    uint32_t* st = stash + ax * 16 * RT_M;
+
+    for (int j = 0; j < nb; ++j) {
+        const uint32_t ph = (uint32_t)j & 1u;
+        if (issuer) {
+            if (!bad && tc::mbar_wait(bar_w + ax, ph)) {
+                tc::tc_fence_after();
+                issue();
+            } else {
+                bad = true;
+            }
+        }
+        bad = bad || !tc::mbar_wait(bar_a + ax, ph);
+        tc::tc_fence_after();
+        if (issuer && j + 1 < nb && !bad) load_w(j + 1);          // the MMAs have read the router buffer
+        // running approximate top-RT_E; scores that beat the current 16th are rare after
+        // the first few, so the compare is unrolled and the sorted insert runs per such score
+        const int gbase = j * nrows;
+        for (int c0 = 0; c0 < nrows && !bad; c0 += 16) {
+            uint32_t r[16];
+            tc::tmem_ld16(tacc + (uint32_t)c0, r);
+            tc::tmem_wait_ld();
+            uint32_t m = 0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                m |= (ranks_before(__uint_as_float(r[i]), gbase + c0 + i, lv[RT_E - 1], li[RT_E - 1]) ? 1u : 0u) << i;
+            if (m == 0u) continue;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) st[i * RT_M + t] = r[i];
+#pragma unroll 1
+            while (m != 0u) {
+                const int i = __ffs(m) - 1;
+                m &= m - 1;
+                float v = __uint_as_float(st[i * RT_M + t]);
+                int vi = gbase + c0 + i;
+#pragma unroll
+                for (int q = 0; q < RT_E; ++q) {
+                    const bool sw = ranks_before(v, vi, lv[q], li[q]);
+                    const float tv = lv[q];
+                    const int ti = li[q];
+                    lv[q] = sw ? v : tv;
+                    li[q] = sw ? vi : ti;
+                    v = sw ? tv : v;
+                    vi = sw ? ti : vi;
+                }
+            }
+        }
+        tc::tc_fence_before();
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + ax) : "memory");      // accumulator free for the next block
+        tc::tc_fence_after();
+    }
+
+    // both axes are scored: the router buffers become the result arrays below
+    __syncthreads();
+    // exact top-k: rescore every row within 2 delta of the approximate k-th, in the oracle's order
+    const float* W = ax ? p.wk[1] : p.wk[0];
+    const float delta = p.delta_scale * kabs * __uint_as_float(p.wmax[ax]);
+    const float theta = lv[K - 1] - 2.f * delta;
+    float tv[K];
+    int ti[K];
+#pragma unroll
+    for (int r = 0; r < K; ++r) { tv[r] = -INFINITY; ti[r] = 0x7fffffff; }
+    auto keep = [&](float sc, int g) {
+#pragma unroll
+        for (int q = 0; q < K; ++q) {
+            const bool sw = ranks_before(sc, g, tv[q], ti[q]);
+            const float a = tv[q];
+            const int b = ti[q];
+            tv[q] = sw ? sc : a;
+            ti[q] = sw ? g : b;
+            sc = sw ? a : sc;
+            g = sw ? b : g;
+        }
+    };
+    auto load_k = [&](int c, float (&x)[8]) { unpack8<T>(*reinterpret_cast<const uint4*>(kt + tc::sw128(t, c)), x); };
+    const bool full_scan = !(lv[RT_E - 1] < theta);       // candidates may lie beyond the list
+    const int ncand = full_scan ? G : RT_E;
+#pragma unroll 1
+    for (int i0 = 0; i0 < ncand; i0 += 8) {
+        int gi[8];
+        bool use[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (full_scan) {
+                gi[j] = i0 + j;
+                use[j] = gi[j] < G;
+            } else {
+                float vv = lv[0];
+                int gg = li[0];
+#pragma unroll
+                for (int q = 1; q < RT_E; ++q)
+                    if (q == i0 + j) { vv = lv[q]; gg = li[q]; }
+                gi[j] = gg;
+                use[j] = (vv >= theta) && gg < G;
+            }
+        }
+        if (!use[0]) {
+            if (!full_scan) break;                         // the list is sorted: no more candidates
+            continue;
+        }
+        const float* wr[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wr[j] = W + (int64_t)(use[j] ? gi[j] : 0) * RT_DH;
+        float sc[8];
+        exact_dots<8>(load_k, wr, sc);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (use[j]) keep(sc[j], gi[j]);
+    }
+    // u_k = normalize(top scores); u_q = normalize(W_q[top] q), the K query dots interleaved
+    float ssk = 0.f;
+#pragma unroll
+    for (int r = 0; r < K; ++r) ssk += tv[r] * tv[r];
+    const float nk = fmaxf(sqrtf(ssk), 1e-12f);
+    const T* qrow = static_cast<const T*>(p.q) + (n < p.N ? n : 0) * RT_DH;
+    const float* WQ = ax ? p.wq[1] : p.wq[0];
+    auto load_q = [&](int c, float (&x)[8]) { unpack8<T>(*reinterpret_cast<const uint4*>(qrow + 8 * c), x); };
+    float qv[K];
+    {
+        const float* wr[K];
+#pragma unroll
+        for (int r = 0; r < K; ++r) wr[r] = WQ + (int64_t)ti[r] * RT_DH;
+        exact_dots<K>(load_q, wr, qv);
+    }
+    float ssq = 0.f;
+#pragma unroll
+    for (int r = 0; r < K; ++r) ssq += qv[r] * qv[r];
+    const float nq = fmaxf(sqrtf(ssq), 1e-12f);
+    float* rs = res + ax * 3 * 8 * RT_M;
+#pragma unroll
+    for (int r = 0; r < K; ++r) {
+        rs[(0 * 8 + r) * RT_M + t] = tv[r] / nk;
+        rs[(1 * 8 + r) * RT_M + t] = qv[r] / nq;
+        rs[(2 * 8 + r) * RT_M + t] = __int_as_float(ti[r]);
+    }
+    bad = __syncthreads_or(bad) != 0;
+    if (!bad && n < p.N) {
+        // Kronecker: group ax writes rows i in [ax K/2, ax K/2 + K/2) of the K x K product
+        constexpr int A = K * K;
+        const int h = (int)((n / p.T) % p.H);
+        const float qsc = p.q_scale ? p.q_scale[h] : 1.f;
+        const float* r0 = res;
+        const float* r1 = res + 3 * 8 * RT_M;
+        T* owk = static_cast<T*>(p.out_wk) + n * A;
+        T* owq = static_cast<T*>(p.out_wq) + n * A;
+        int64_t* oix = p.out_idx + n * A;
+#pragma unroll
+        for (int ii = 0; ii < K / 2; ++ii) {
+            const int i = ax * (K / 2) + ii;
+            const float uki = r0[(0 * 8 + i) * RT_M + t];
+            const float uqi = r0[(1 * 8 + i) * RT_M + t];
+            const int64_t xi = (int64_t)__float_as_int(r0[(2 * 8 + i) * RT_M + t]) * p.G[1];
+#pragma unroll
+            for (int j = 0; j < K; ++j) {
+                owk[i * K + j] = dg::from_f<T>(uki * r1[(0 * 8 + j) * RT_M + t]);
+                owq[i * K + j] = dg::from_f<T>((uqi * r1[(1 * 8 + j) * RT_M + t]) * qsc);
+                oix[i * K + j] = xi + __float_as_int(r1[(2 * 8 + j) * RT_M + t]);
+            }
+        }
+    }
+    if (bad && tid == 0) dg::flag_status(p.status, DG_DEVCHK_TIMEOUT);
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 2 * RT_NMAX);
+    }
+}
+
+// router weights -> 16-bit hi and lo parts (stacked axes) and max |w| per axis
+template <typename T>
+__global__ void router_split_kernel(const float* w0, const float* w1, int g0, int g1, T* hi, T* lo, unsigned* wmax) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t n0 = (int64_t)g0 * RT_DH, nt = n0 + (int64_t)g1 * RT_DH;
+    if (i >= nt) return;
+    const float w = i < n0 ? w0[i] : w1[i - n0];
+    const T h = dg::from_f<T>(w);
+    hi[i] = h;
+    lo[i] = dg::from_f<T>(w - dg::to_f(h));
+    atomicMax(wmax + (i < n0 ? 0 : 1), __float_as_uint(fabsf(w)));
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+    return fn;
+}
+
+// 2-D map over [rows][64] 16-bit values, box 64 x box_rows, 128B swizzle
+bool make_map_2d(CUtensorMap* m, const void* base, int64_t rows, int box_rows, bool bf16) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)RT_DH, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)RT_DH * 2};
+    cuuint32_t box[2] = {(cuuint32_t)RT_DH, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
+              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T, int K>
+int launch_tc(const RtParams& p0, const CUtensorMap& mk, const CUtensorMap& mhi, const CUtensorMap& mlo,
+              cudaStream_t s) {
+    auto kern = router_tc_kernel<T, K>;
+    const int smem = (int)SM_BYTES + 1024;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return dg_host::record_cuda_error(e);
+    kern<<<(unsigned)((p0.N + RT_M - 1) / RT_M), 2 * RT_M, smem, s>>>(mk, mhi, mlo, p0);
+    return dg_host::check_launch();
+}
+
+}  // namespace
+
+namespace dg_host {
+
+// Whether the tensor-core router covers the call (else the CUDA-core router runs).
+bool route_tc_supports(int dtype, int dh, int g0, int g1, int top_k, const void* k, const void* q,
+                       const float* rk0, const float* rk1, const float* rq0, const float* rq1) {
+    if (dtype != DG_DTYPE_F16 && dtype != DG_DTYPE_BF16) return false;
+    if (dh != RT_DH || (top_k != 4 && top_k != 8)) return false;
+    auto rows = [](int g) { return g <= RT_NMAX ? g : RT_NMAX; };
+    if (rows(g0) != rows(g1)) return false;
+    const int nr = rows(g0);
+    if (nr % 16 != 0 || g0 % nr != 0 || g1 % nr != 0 || nr < 32) return false;
+    const uintptr_t al = (uintptr_t)k | (uintptr_t)q | (uintptr_t)rk0 | (uintptr_t)rk1 | (uintptr_t)rq0 | (uintptr_t)rq1;
+    return (al & 15) == 0;
+}
+
+int route_tc(int dtype, int64_t N, int H, int T, int g0, int g1, int top_k, const void* k, const void* q,
+             const float* rk0, const float* rk1, const float* rq0, const float* rq1, const float* q_scale, void* wk,
+             void* wq, int64_t* idx, cudaStream_t s) {
+    const bool bf16 = dtype == DG_DTYPE_BF16;
+    const int64_t wn = (int64_t)(g0 + g1) * RT_DH;
+    const size_t bytes = (size_t)wn * 2 * 2 + 64;
+    void* ws = nullptr;
+    cudaError_t e = cudaMallocAsync(&ws, bytes, s);          // stream-ordered, from the device's default pool
+    if (e != cudaSuccess) return record_cuda_error(e);
+    uint8_t* hi = static_cast<uint8_t*>(ws);
+    uint8_t* lo = hi + wn * 2;
+    unsigned* wmax = reinterpret_cast<unsigned*>(lo + wn * 2);
+    int rc = DG_OK;
+    e = cudaMemsetAsync(wmax, 0, 2 * sizeof(unsigned), s);
+    if (e != cudaSuccess) rc = record_cuda_error(e);
+    if (rc == DG_OK) {
+        const unsigned blocks = (unsigned)((wn + 255) / 256);
+        if (bf16)
+            router_split_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(rk0, rk1, g0, g1, reinterpret_cast<__nv_bfloat16*>(hi),
+                                                                     reinterpret_cast<__nv_bfloat16*>(lo), wmax);
+        else
+            router_split_kernel<__half><<<blocks, 256, 0, s>>>(rk0, rk1, g0, g1, reinterpret_cast<__half*>(hi),
+                                                              reinterpret_cast<__half*>(lo), wmax);
+        rc = check_launch();
+    }
+    const int nr = g0 <= RT_NMAX ? g0 : RT_NMAX;
+    CUtensorMap mk, mhi, mlo;
+    if (rc == DG_OK && (!make_map_2d(&mk, k, N, RT_M, bf16) || !make_map_2d(&mhi, hi, g0 + g1, nr, bf16) ||
+                        !make_map_2d(&mlo, lo, g0 + g1, nr, bf16)))
+        rc = DG_ERR_UNSUPPORTED;
+    if (rc == DG_OK) {
+        // |approx - exact| <= c * sum|k| * max|w|: split residual, accumulation and the
+        // sequential sum's own rounding, with a factor 2 margin (2^-15 f16, 2^-14 bf16)
+        RtParams p{k, q, {rk0, rk1}, {rq0, rq1}, q_scale, wmax, wk, wq, idx, N, H, T, nr, {g0, g1},
+                   bf16 ? 6.103515625e-05f : 3.0517578125e-05f, nullptr};
+        if (bf16) rc = top_k == 8 ? launch_tc<__nv_bfloat16, 8>(p, mk, mhi, mlo, s) : launch_tc<__nv_bfloat16, 4>(p, mk, mhi, mlo, s);
+        else rc = top_k == 8 ? launch_tc<__half, 8>(p, mk, mhi, mlo, s) : launch_tc<__half, 4>(p, mk, mhi, mlo, s);
+    }
+    e = cudaFreeAsync(ws, s);
+    if (rc != DG_OK) return rc;
+    return e == cudaSuccess ? DG_OK : record_cuda_error(e);
+}
+
+}  // namespace dg_host

@@ -83,3 +83,23 @@ def test_routed_forward_matches_two_step_reference():
     st2 = torch.zeros_like(st)
     y2, st2, _ = ext.pkm_forward(v, beta, wk, wq, idx2, decay, st2)
     assert torch.equal(idx, idx2) and torch.equal(y, y2) and torch.equal(st, st2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_tensor_core_router_ties_and_crowded_threshold(dtype):
+    # 16-bit keys take the tensor-core router.  Duplicated router rows give exactly equal
+    # scores (lower index first); a block of 40 identical rows puts far more than 16
+    # candidates inside the error window, so those tokens take the exact full rescan.
+    Dh, G, K = 64, 256, 8
+    g = torch.Generator().manual_seed(11)
+    w = torch.randn(G, Dh, generator=g) / Dh ** 0.5
+    w[9] = w[2]
+    w[130] = w[77]
+    w[200:240] = w[199]
+    k = torch.nn.functional.normalize(torch.randn(1, 2, 96, Dh, generator=g), dim=-1)
+    k[0, 1, :40] = torch.nn.functional.normalize(w[199], dim=0)          # these tokens prefer rows 199..239
+    k = k.to(dtype)
+    q = torch.randn(1, 2, 96, Dh, generator=g).to(dtype)
+    wk, wq, idx = pkm_route(k.cuda(), q.cuda(), [w.cuda(), w.cuda()], [w.cuda(), w.cuda()], K)
+    _, _, idxo, _ = O.pkm_route(k.float().numpy(), q.float().numpy(), w.numpy(), w.numpy(), w.numpy(), w.numpy(), K)
+    np.testing.assert_array_equal(idx.cpu().numpy(), idxo)
