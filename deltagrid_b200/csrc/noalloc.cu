@@ -1,13 +1,24 @@
 // noalloc.cu -- dg_pkm_forward_noalloc: the PKM sequence forward with its
 // scratch taken from a fixed device array, so the call allocates nothing.
 //
+// Who needs it: a caller that may not allocate device memory while it runs the
+// recurrence -- a serving loop whose memory is sized and reserved up front and
+// must not grow or fragment between requests, code that runs inside a host
+// callback or under a memory manager that forbids allocation, or a step that
+// has to take the same memory on every call.  dg_pkm_forward allocates its
+// scratch from the stream-ordered pool when the caller hands it none; this
+// entry point never does.
+//
 // The only scratch any PKM kernel here uses is the warp-specialised kernel's
 // per-row hazard codes (B*H*T*64 int16, written in full by its pre-pass before
 // they are read, so nothing in the array has to start at zero).  The array is a
-// file-scope __device__ object of kNoAllocBytes; its address on each device is
-// looked up once (cudaGetSymbolAddress) and cached.  Calls whose scratch need
+// file-scope __device__ object of kNoAllocBytes.  Set-up: the first call of this
+// entry point on a device, with that device current, looks up the array's
+// address there (cudaGetSymbolAddress, return code checked) and caches it; that
+// first call should come before any stream capture.  Calls whose scratch need
 // exceeds the array are rejected with DG_ERR_WORKSPACE before any launch.
-// Calls that overlap in time on one device share the array and race.
+// Calls that overlap in time on one device share the array and race: the
+// caller serializes them (one stream, or events between streams).
 #include <mutex>
 
 #include "dg_common.cuh"
@@ -58,11 +69,12 @@ int dg_pkm_forward_noalloc(int dtype, int B, int H, int T, int active, int64_t t
                            int32_t* dev_status, void* stream) {
     const size_t need = dg_pkm_forward_workspace_size(dtype, B, H, T, active, total_slots, dh, DG_PKM_AUTO);
     if (need > kNoAllocBytes) return DG_ERR_WORKSPACE;
-    void* ws = nullptr;
-    if (need) {
-        const int rc = scratch_address(&ws);
-        if (rc != DG_OK) return rc;
-    }
+    // the set-up runs on the first call on a device whether or not this call
+    // needs scratch, so a later call (possibly under capture) only reads the cache
+    void* addr = nullptr;
+    const int rc = scratch_address(&addr);
+    if (rc != DG_OK) return rc;
+    void* ws = need ? addr : nullptr;
     return dg_pkm_forward_ex(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay, dynamic_decay,
                              state, out, saved_s_act, dev_status, DG_PKM_AUTO, ws, ws ? kNoAllocBytes : 0, stream);
 }

@@ -153,12 +153,17 @@ int dg_pkm_forward_ex(int dtype, int B, int H, int T, int active, int64_t total_
                       void* state, void* out, void* saved_s_act, int32_t* dev_status,
                       int algo, void* workspace, size_t workspace_bytes, void* stream);
 
-/* dg_pkm_forward that allocates nothing (no reference counterpart).  Scratch comes
- * from a fixed 16 MiB device array in this library (its address looked up once
- * per device); calls needing more (dg_pkm_forward_workspace_size > 16 MiB, i.e.
- * B*H*T > 131072 for the warp-specialised kernel) return DG_ERR_WORKSPACE without
- * launching.  Calls that overlap in time on one device share that array and race:
- * serialize them. */
+/* dg_pkm_forward that allocates nothing (no reference counterpart).  For callers
+ * that may not allocate device memory while the recurrence runs: a serving loop
+ * whose memory is reserved up front and must not grow or fragment between
+ * requests, or code under a memory manager or in a context that forbids
+ * allocation.  Scratch comes from a fixed 16 MiB device array inside this
+ * library.  Set-up: the first call on a device (that device current) looks up
+ * the array's address there and caches it, so make that first call before any
+ * stream capture.  Calls needing more scratch than the array holds
+ * (dg_pkm_forward_workspace_size > 16 MiB, i.e. B*H*T > 131072 on the
+ * warp-specialised kernel) return DG_ERR_WORKSPACE without launching.  Calls that
+ * overlap in time on one device share the array and race: serialize them. */
 int dg_pkm_forward_noalloc(int dtype, int B, int H, int T, int active, int64_t total_slots, int dh,
                            const void* v, const void* beta, const void* wk, const void* wq,
                            const int64_t* idx, const void* decay, int dynamic_decay,

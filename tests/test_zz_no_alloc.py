@@ -1,6 +1,11 @@
-"""dg_pkm_forward_noalloc (scratch from a fixed device array) against dg_pkm_forward
-(scratch from a stream-ordered pool allocation) on identical inputs, two calls in a
-row so the second call reuses the array the first one filled; plus the size check."""
+"""dg_pkm_forward_noalloc, the entry point for callers that may not allocate device
+memory while the recurrence runs (a serving loop with its memory reserved up front,
+code under an allocator that forbids growth), checked against dg_pkm_forward, which
+takes its scratch from the stream-ordered pool.  Identical inputs, two calls in a
+row, so the second call reuses the fixed scratch array the first one filled and
+the first call also performs the per-device address look-up.  Plus the size check:
+a call needing more than the 16 MiB array is refused before any launch.  This file
+is collected last so it also runs after every other GPU test in one process."""
 import ctypes
 
 import pytest
