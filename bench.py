@@ -280,6 +280,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--algo", type=int, default=0, help="dense algorithm (0 auto, 1 sequential, 2 chunked tcgen05)")
     ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (small profiling cases)")
+    ap.add_argument("--seq", type=int, default=0, help="override the sequence length T (small profiling cases)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -288,6 +289,9 @@ def main():
     if args.batch > 0:
         w["B"] = args.batch
         w["desc"] += f" (batch overridden to {args.batch})"
+    if args.seq > 0:
+        w["T"] = args.seq
+        w["desc"] += f" (T overridden to {args.seq})"
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
