@@ -42,8 +42,14 @@ _SIGS = {
     "dg_pkm_route": [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     "dg_fxp_dense_forward": [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P],
     "dg_fxp_pkm_forward": [_I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
+    "dg_dense_backward_workspace_size": [_I, _I, _I, _I],
+    "dg_dense_backward": [_I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P,
+                          _P, _P],
+    "dg_pkm_backward": [_I, _I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P,
+                        _P, _P],
 }
-_RESTYPE = {"dg_status_string": ctypes.c_char_p, "dg_pkm_forward_workspace_size": ctypes.c_size_t}
+_RESTYPE = {"dg_status_string": ctypes.c_char_p, "dg_pkm_forward_workspace_size": ctypes.c_size_t,
+            "dg_dense_backward_workspace_size": ctypes.c_size_t}
 
 _lib = None
 _lock = threading.Lock()

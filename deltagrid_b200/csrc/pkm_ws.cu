@@ -63,7 +63,7 @@ template <int PB> struct GatherCfg {
 };
 constexpr int KPAR = 4;                 // warps per column slice; warp k takes the steps s with s % KPAR == k
 constexpr int HZ_STEPS = 48;            // steps resolved per pre-pass CTA
-constexpr int HZ_BUCKETS = 1024;        // pre-pass hash buckets (counting sort)
+constexpr int HZ_BUCKETS = 4096;        // pre-pass hash buckets (counting sort): ~0.9 entries per bucket
 constexpr int HZ_THREADS = 512;
 constexpr int HZ_MAXWIN = 16;           // largest window depth D the pre-pass covers
 constexpr int HZ_KMAX = ((HZ_STEPS + HZ_MAXWIN - 1) * MAXA + HZ_THREADS - 1) / HZ_THREADS;   // entries per thread
@@ -109,11 +109,14 @@ __host__ __device__ inline MetaLayout meta_layout(int A, int Dh) {
 struct SmemLayout {
     int bars, misc, rows, zrow, rbuf, ystage, meta, total;
 };
+// mbarriers of the recurrence kernel: full[R], done[R], dsl[R][NSL], mfull[NC], mfree[NC]
+__host__ __device__ constexpr int ws_barriers(int PB, int D) { return 2 * (2 * D) + (2 * D) * (PB / 32) + 2 * NC; }
+
 __host__ __device__ inline SmemLayout smem_layout(int PB, int D, int A, int Dh) {
     SmemLayout L;
     const int R = 2 * D, RS = PB + 16;
     int o = 0;
-    L.bars = o;   o += 1024;
+    L.bars = o;   o += (ws_barriers(PB, D) * 8 + 127) / 128 * 128;
     L.misc = o;   o += 16;
     L.rows = o;   o += R * 64 * RS;
     L.zrow = o;   o += RS;
@@ -133,7 +136,7 @@ __device__ __forceinline__ uint32_t slot_home(uint32_t x) {
     x ^= x >> 13;
     x *= 0xc2b2ae35u;
     x ^= x >> 16;
-    return x >> (32 - 10);                                     // HZ_BUCKETS = 1024
+    return x >> (32 - 12);                                     // HZ_BUCKETS = 4096
 }
 
 // ---------------------------------------------------------------------------
@@ -176,10 +179,14 @@ __global__ void __launch_bounds__(HZ_THREADS) pkm_hazard_kernel(const int64_t* _
 #pragma unroll
     for (int k = 0; k < HZ_KMAX; ++k) rank[k] = key[k] ? atomicAdd(cnt + bkt[k], 1u) : 0u;
     __syncthreads();
-    // exclusive prefix sum of the bucket counts: two buckets per thread
+    // exclusive prefix sum of the bucket counts: BPT consecutive buckets per thread
     {
-        const uint32_t c0 = cnt[2 * tid], c1 = cnt[2 * tid + 1];
-        uint32_t v = c0 + c1;
+        constexpr int BPT = HZ_BUCKETS / HZ_THREADS;
+        uint32_t cb[BPT];
+        uint32_t v = 0;
+#pragma unroll
+        for (int i = 0; i < BPT; ++i) { cb[i] = cnt[BPT * tid + i]; v += cb[i]; }
+        const uint32_t tot = v;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const uint32_t u = __shfl_up_sync(DG_FULL_MASK, v, o);
@@ -197,9 +204,9 @@ __global__ void __launch_bounds__(HZ_THREADS) pkm_hazard_kernel(const int64_t* _
             if (lane < HZ_THREADS / 32) wsum[lane] = wv;          // inclusive warp totals
         }
         __syncthreads();
-        const uint32_t base = (warp ? wsum[warp - 1] : 0u) + v - (c0 + c1);
-        start[2 * tid] = base;
-        start[2 * tid + 1] = base + c0;
+        uint32_t base = (warp ? wsum[warp - 1] : 0u) + v - tot;
+#pragma unroll
+        for (int i = 0; i < BPT; ++i) { start[BPT * tid + i] = base; base += cb[i]; }
     }
     __syncthreads();
 #pragma unroll

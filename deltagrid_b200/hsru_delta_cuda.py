@@ -247,13 +247,95 @@ def pkm_fused_forward(k: torch.Tensor, q: torch.Tensor, v: torch.Tensor, beta: t
     return [out, state_c, idx, saved]
 
 
-def backward(grad_out, grad_s_final, v, beta, wk, wq, decay, s_final, err_saved,
-             needs_grad_s_init: bool = False):
-    """Dense analytic backward (binding.cpp:223-312)."""
-    raise RuntimeError("hsru_delta_cuda.backward: the dense backward kernel is not part of this build")
+def backward(grad_out: torch.Tensor, grad_s_final: Optional[torch.Tensor], v: torch.Tensor,
+             beta: torch.Tensor, wk: torch.Tensor, wq: torch.Tensor, decay: torch.Tensor,
+             s_final: torch.Tensor, err_saved: torch.Tensor,
+             needs_grad_s_init: bool = False) -> List[Optional[torch.Tensor]]:
+    """Dense analytic backward (binding.cpp:223-312).
+
+    s_final and err_saved are the fp32 final state and residuals of forward(...,
+    save_for_backward=True) (its s_final_f / err_out).  Returns [grad_v, grad_beta,
+    grad_wk, grad_wq, grad_decay, grad_s_init]; grad_s_init is an undefined (None)
+    tensor unless needs_grad_s_init.  A static [H] decay gets the sum over the batch.
+    """
+    for t, n in ((grad_out, "grad_out"), (v, "v"), (beta, "beta"), (wk, "wk"), (wq, "wq"), (decay, "decay"),
+                 (s_final, "s_final"), (err_saved, "err_saved")):
+        _check_cuda(t, n)
+    go_c, v_c, beta_c, wk_c, wq_c, decay_c = map(_contig, (grad_out, v, beta, wk, wq, decay))
+    sf_c = s_final.to(torch.float32).contiguous()
+    err_c = err_saved.to(torch.float32).contiguous()
+    code = _dtype_code(v_c, "delta_grid_backward_cuda")
+    _same_dtype(v_c, "backward", grad_out=go_c, beta=beta_c, wk=wk_c, wq=wq_c, decay=decay_c)
+    B, H, T, Dh = v_c.shape
+    S = wk_c.size(3)
+    gsf = None
+    if grad_s_final is not None:
+        _check_cuda(grad_s_final, "grad_s_final")
+        gsf = _contig(grad_s_final)
+        _same_dtype(v_c, "backward", grad_s_final=gsf)
+    dynamic = 1 if decay_c.dim() > 1 else 0
+    grad_v = torch.empty_like(v_c)
+    grad_beta = torch.empty_like(beta_c)
+    grad_wk = torch.empty_like(wk_c)
+    grad_wq = torch.empty_like(wq_c)
+    grad_decay = torch.empty_like(decay_c) if dynamic else torch.zeros_like(decay_c)
+    grad_s_init = torch.empty((B, H, S, Dh), dtype=v_c.dtype, device=v_c.device) if needs_grad_s_init else None
+    with torch.cuda.device(v_c.device):
+        nws = _lib.lib().dg_dense_backward_workspace_size(B, H, S, Dh)
+        ws = torch.empty(nws // 4, dtype=torch.float32, device=v_c.device) if nws else None
+        _lib.call("dg_dense_backward", code, B, H, T, S, Dh, go_c.data_ptr(),
+                  gsf.data_ptr() if gsf is not None else None, v_c.data_ptr(), beta_c.data_ptr(),
+                  wk_c.data_ptr(), wq_c.data_ptr(), decay_c.data_ptr(), dynamic, sf_c.data_ptr(), err_c.data_ptr(),
+                  grad_v.data_ptr(), grad_beta.data_ptr(), grad_wk.data_ptr(), grad_wq.data_ptr(),
+                  grad_decay.data_ptr(), grad_s_init.data_ptr() if grad_s_init is not None else None,
+                  ws.data_ptr() if ws is not None else None, _stream(v_c))
+    return [grad_v, grad_beta, grad_wk, grad_wq, grad_decay, grad_s_init]
 
 
-def pkm_backward(grad_out, v, beta, wk, wq, active_idx, decay, saved_s_act, total_slots,
-                 grad_final_state=None, needs_grad_decay: bool = False):
-    """Sparse Delta-PKM analytic backward (binding.cpp:439-518)."""
-    raise RuntimeError("hsru_delta_cuda.pkm_backward: the PKM backward kernel is not part of this build")
+def pkm_backward(grad_out: torch.Tensor, v: torch.Tensor, beta: torch.Tensor, wk: torch.Tensor,
+                 wq: torch.Tensor, active_idx: torch.Tensor, decay: torch.Tensor, saved_s_act: torch.Tensor,
+                 total_slots: int, grad_final_state: Optional[torch.Tensor] = None,
+                 needs_grad_decay: bool = False) -> List[Optional[torch.Tensor]]:
+    """Sparse Delta-PKM analytic backward (binding.cpp:439-518).
+
+    saved_s_act is the [B,H,T,A,Dh] rows of pkm_forward(..., save_for_backward=True).
+    Returns [grad_v, grad_beta, grad_wk, grad_wq, grad_decay, grad_state]: grad_state
+    is the gradient of the initial state (grad_final_state carried back to step 0),
+    grad_decay is None unless needs_grad_decay ([B,H,T] for a dynamic decay, else [H]
+    summed over the batch -- an output the reference allocates but never writes).
+    """
+    for t, n in ((grad_out, "grad_out"), (v, "v"), (beta, "beta"), (wk, "wk"), (wq, "wq"),
+                 (active_idx, "active_idx"), (decay, "decay"), (saved_s_act, "saved_s_act")):
+        _check_cuda(t, n)
+    go_c, v_c, beta_c, wk_c, wq_c, idx_c, decay_c, sv_c = map(
+        _contig, (grad_out, v, beta, wk, wq, active_idx, decay, saved_s_act))
+    code = _dtype_code(v_c, "delta_pkm_backward_cuda")
+    _same_dtype(v_c, "pkm_backward", grad_out=go_c, beta=beta_c, wk=wk_c, wq=wq_c, decay=decay_c,
+                saved_s_act=sv_c)
+    if idx_c.dtype != torch.int64:
+        raise RuntimeError(f"pkm_backward: expected active_idx to have dtype torch.int64, got {idx_c.dtype}")
+    B, H, T, Dh = v_c.shape
+    A = wk_c.size(3)
+    total = int(total_slots)
+    dynamic = 1 if decay_c.dim() > 1 else 0
+    if grad_final_state is not None:
+        _check_cuda(grad_final_state, "grad_final_state")
+        grad_state = grad_final_state.clone().contiguous()
+        _same_dtype(v_c, "pkm_backward", grad_final_state=grad_state)
+    else:
+        grad_state = torch.zeros((B, H, total, Dh), dtype=v_c.dtype, device=v_c.device)
+    grad_v = torch.empty((B, H, T, Dh), dtype=v_c.dtype, device=v_c.device)
+    grad_beta = torch.empty((B, H, T), dtype=v_c.dtype, device=v_c.device)
+    grad_wk = torch.empty((B, H, T, A), dtype=v_c.dtype, device=v_c.device)
+    grad_wq = torch.empty((B, H, T, A), dtype=v_c.dtype, device=v_c.device)
+    grad_decay = None
+    if needs_grad_decay:
+        grad_decay = (torch.empty((B, H, T), dtype=v_c.dtype, device=v_c.device) if dynamic
+                      else torch.zeros((H,), dtype=v_c.dtype, device=v_c.device))
+    with torch.cuda.device(v_c.device):
+        _lib.call("dg_pkm_backward", code, B, H, T, A, total, Dh, go_c.data_ptr(), v_c.data_ptr(),
+                  beta_c.data_ptr(), wk_c.data_ptr(), wq_c.data_ptr(), idx_c.data_ptr(), decay_c.data_ptr(),
+                  dynamic, sv_c.data_ptr(), grad_state.data_ptr(), grad_v.data_ptr(), grad_beta.data_ptr(),
+                  grad_wk.data_ptr(), grad_wq.data_ptr(), grad_decay.data_ptr() if grad_decay is not None else None,
+                  _status_word(v_c.device).data_ptr(), _stream(v_c))
+    return [grad_v, grad_beta, grad_wk, grad_wq, grad_decay, grad_state]

@@ -153,6 +153,40 @@ int dg_pkm_forward_ex(int dtype, int B, int H, int T, int active, int64_t total_
                       void* state, void* out, void* saved_s_act, int32_t* dev_status,
                       int algo, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Dense analytic backward.  Replaces delta_grid_bwd_kernel / launch_delta_grid_backward
+ * (src/cpp/delta_kernel.cu:364-558, :698-731); same call as delta_grid_backward_binding
+ * (binding.cpp:223-312).  s_final and err_saved are the fp32 final state and residuals
+ * that dg_dense_forward writes when asked (s_final_f / err_out).  grad_s_final and
+ * grad_s_init may be NULL.  A static [H] decay gets grad_decay[h] += the head's sum, so
+ * the caller zeroes it first.  workspace: dg_dense_backward_workspace_size() bytes of
+ * fp32 (the state and its adjoint when they do not fit on chip), else NULL.
+ */
+size_t dg_dense_backward_workspace_size(int B, int H, int slots, int dh);
+int dg_dense_backward(int dtype, int B, int H, int T, int slots, int dh,
+                      const void* grad_out, const void* grad_s_final, const void* v,
+                      const void* beta, const void* wk, const void* wq, const void* decay,
+                      int dynamic_decay, const float* s_final, const float* err_saved,
+                      void* grad_v, void* grad_beta, void* grad_wk, void* grad_wq,
+                      void* grad_decay, void* grad_s_init, float* workspace, void* stream);
+
+/*
+ * Sparse Delta-PKM analytic backward.  Replaces delta_pkm_sequence_backward_kernel /
+ * launch_delta_grid_pkm_backward (src/cpp/delta_kernel.cu:971-1102); same call as
+ * delta_pkm_backward_binding (binding.cpp:439-518).  grad_state [B,H,total,Dh] holds
+ * grad_final_state (or zeros) on entry and the gradient of the initial state on return.
+ * saved_s_act is the [B,H,T,active,Dh] rows dg_pkm_forward saved.  grad_decay may be
+ * NULL (not requested); a static [H] decay gets grad_decay[h] += the head's sum (the
+ * reference leaves that output unwritten), so the caller zeroes it first.  active <= 64,
+ * dh <= 128.  Indices out of range are skipped and set DG_DEVCHK_INDEX_RANGE.
+ */
+int dg_pkm_backward(int dtype, int B, int H, int T, int active, int64_t total_slots, int dh,
+                    const void* grad_out, const void* v, const void* beta, const void* wk,
+                    const void* wq, const int64_t* idx, const void* decay, int dynamic_decay,
+                    const void* saved_s_act, void* grad_state, void* grad_v, void* grad_beta,
+                    void* grad_wk, void* grad_wq, void* grad_decay, int32_t* dev_status,
+                    void* stream);
+
 /* dg_pkm_forward that allocates nothing (no reference counterpart).  For callers
  * that may not allocate device memory while the recurrence runs: a serving loop
  * whose memory is reserved up front and must not grow or fragment between
