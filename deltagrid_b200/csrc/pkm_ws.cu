@@ -17,28 +17,25 @@
 //   sort: one 32-bit atomicAdd per entry, a block prefix sum), then every row of
 //   the 48 steps scans its bucket.  Exact, with no capacity to overflow.
 //
-// pkm_ws_kernel -- the recurrence.  One CTA per (lane, part of the row); four
+// pkm_ws_kernel -- the recurrence.  One CTA per (lane, part of the row); three
 //   roles run concurrently on a ring of R = 2D row slots, synchronised by
 //   mbarriers:
 //   loader (1 warp)  metadata (idx, wk, wq, v, beta, alpha, codes) 16 steps at a
 //       time into a 3-chunk ring, each chunk reloaded once its last update is done.
-//   gather (2 warps)  per step t, D steps ahead of the update: row-coalesced
+//   gather (2 warps for 128-byte row parts, 4 for 64-byte parts)  per step t,
+//       D steps ahead of the update: row-coalesced
 //       cp.async (8 lanes per 128 bytes) of the rows coded "gather" into the
 //       step's ring slot; other rows copy 0 bytes (zero-fill), so the issue
 //       loop has no branches.
 //   slices (KPAR warps per 16-column slice, taking turns by step)
-//       per step s: y and pred of its columns as a tensor-core GEMV, mma.sync
-//       m16n8k16 with A = the gathered rows transposed (ldmatrix.trans, one row
-//       address per lane, so forwarded rows need no copy; columns are the M
-//       dimension) and B = [wq, wk] (2 of 8 N columns used), four MMAs for 64
-//       rows; writes r = beta (v - pred) to shared memory and stages y for
-//       coalesced stores.
-//   update (PB/16 warps)  per step s: loads its gathered rows before r is ready,
-//       then the new rows (fp32 math, packed f32x2, one rounding), written to
-//       the ring slot (for forwarding) and to global memory with coalesced
-//       16-byte stores.
-//   The update of step s overlaps the GEMV of steps s+1 and s+2 unless they
-//   read a row that s writes, in which case the GEMV waits for that update.
+//       per step s, for the slice's 16 columns: y and pred as a tensor-core GEMV,
+//       mma.sync m16n8k16 with A = the gathered rows transposed (ldmatrix.trans,
+//       one row address per lane, so forwarded rows need no copy; columns are the
+//       M dimension) and B = [wq, wk] (2 of 8 N columns used), four MMAs for 64
+//       rows; r = beta (v - pred); then the new rows (fp32 math, packed f32x2, one
+//       rounding), written to the ring slot (for forwarding) and to global memory
+//       with 16-byte stores; y is staged for coalesced stores.  A warp waits only
+//       for the warps of its slice that wrote a row it forwards.
 //
 // Ordering argument: a row gathered from global memory for step t has its last
 // writer w <= t-D, and the gather is issued only after the update of step t-D
@@ -60,8 +57,11 @@ constexpr int NLOAD = 32;               // loader threads (one warp)
 template <int PB> struct GatherCfg {
     static constexpr int NGATH = PB == 128 ? 64 : 128;
     static constexpr int ROLE_WARPS = 1 + NGATH / 32;       // loader, gather (then KPAR warps per 16-column slice)
+    // warps per column slice; warp k takes the steps s with s % KPAR == k.  Three for
+    // 128-byte parts (four slices: 15 warps in all measured fastest), four for 64-byte
+    // parts, whose two slices need the extra steps in flight
+    static constexpr int KPAR = PB == 128 ? 3 : 4;
 };
-constexpr int KPAR = 4;                 // warps per column slice; warp k takes the steps s with s % KPAR == k
 constexpr int HZ_STEPS = 48;            // steps resolved per pre-pass CTA
 constexpr int HZ_BUCKETS = 4096;        // pre-pass hash buckets (counting sort): ~0.9 entries per bucket
 constexpr int HZ_THREADS = 512;
@@ -121,7 +121,7 @@ __host__ __device__ inline SmemLayout smem_layout(int PB, int D, int A, int Dh) 
     L.rows = o;   o += R * 64 * RS;
     L.zrow = o;   o += RS;
     L.rbuf = o;   o += 16 * 64 * 4;
-    L.ystage = o; o += CHS * PB;
+    L.ystage = o; o += 2 * CHS * PB;     // y rows of two chunks (by chunk parity)
     o = (o + 127) / 128 * 128;
     L.meta = o;   o += NC * meta_layout(A, Dh).bytes;
     L.total = o;
@@ -360,11 +360,12 @@ __device__ __forceinline__ unsigned long long fma_f32x2(unsigned long long a, un
 }
 
 template <typename T, int PB, int D>
-__global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + KPAR * (PB / 32))) pkm_ws_kernel(WsParams p) {
+__global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB>::KPAR * (PB / 32))) pkm_ws_kernel(WsParams p) {
     constexpr int NGATH = GatherCfg<PB>::NGATH;
     constexpr int ROLE_WARPS = GatherCfg<PB>::ROLE_WARPS;
     constexpr int CH = PB / 16;          // 16-byte chunks per row part
     constexpr int NSL = PB / 32;         // column slices of 16 columns; KPAR warps per slice take turns by step
+    constexpr int KPAR = GatherCfg<PB>::KPAR;
     constexpr int RS = PB + 16;          // padded row stride: conflict-free ldmatrix / 16-byte accesses
     constexpr int R = 2 * D;
     constexpr int SLOT = 64 * RS;
@@ -509,7 +510,7 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + KPAR * (PB /
                 uint32_t dm = 0;
                 if (c0 >= 0) dm |= 1u << (c0 >> 6);
                 if (c1 >= 0) dm |= 1u << (c1 >> 6);
-                constexpr uint32_t kOwn = KPAR == 4 ? 0x11111111u : 0x55555555u;   // distances that are multiples of KPAR
+                constexpr uint32_t kOwn = KPAR == 4 ? 0x11111111u : KPAR == 3 ? 0x49249249u : 0x55555555u;   // distances that are multiples of KPAR
                 dm = __reduce_or_sync(DG_FULL_MASK, dm) & ~kOwn;
                 while (dm != 0u && ok) {
                     const int d = __ffs(dm) - 1;
@@ -575,7 +576,10 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + KPAR * (PB /
                 const int col0 = sli * 16 + g;                 // column within the part
                 const float bta = dg::to_f(reinterpret_cast<const T*>(mc + ML.beta)[ts]);
                 const T* mv = reinterpret_cast<const T*>(mc + ML.v) + ts * Dh + part * (PB / 2);
-                T* yrow = reinterpret_cast<T*>(ystage + ts * PB);
+                // y rows are staged per chunk parity: the same row of the next chunk may
+                // belong to another warp of the slice (KPAR need not divide CHS), which can
+                // be up to D < CHS steps ahead of this warp's flush
+                T* yrow = reinterpret_cast<T*>(ystage + ((cn & 1) * CHS + ts) * PB);
                 yrow[col0] = dg::from_f<T>(acc[0]);
                 yrow[col0 + 8] = dg::from_f<T>(acc[2]);
                 rw[g] = bta * (dg::to_f(mv[col0]) - acc[1]);
@@ -618,10 +622,12 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + KPAR * (PB /
             const int cend = min(t0c + CHS, T_);
             if (s + KPAR >= cend) {                           // this warp's last step of the chunk
                 mbar_arrive(mfree + (cn % NC));
-                const int nj = (cend - t0c - par + KPAR - 1) / KPAR;   // rows par, par + KPAR, ... of y for this slice
+                // this warp's rows of the chunk: steps s = par (mod KPAR), i.e. rows j0, j0 + KPAR, ...
+                const int j0 = ((par - t0c) % KPAR + KPAR) % KPAR;
+                const int nj = (cend - t0c - j0 + KPAR - 1) / KPAR;
                 for (int i = lane; i < 2 * nj; i += 32) {
-                    const int jj = par + KPAR * (i >> 1), hh = i & 1;
-                    const uint4 val = *reinterpret_cast<const uint4*>(ystage + jj * PB + sli * 32 + hh * 16);
+                    const int jj = j0 + KPAR * (i >> 1), hh = i & 1;
+                    const uint4 val = *reinterpret_cast<const uint4*>(ystage + ((cn & 1) * CHS + jj) * PB + sli * 32 + hh * 16);
                     dg::st16(reinterpret_cast<uint8_t*>(gout + (lt0 + t0c + jj) * Dh) + part * PB + sli * 32 + hh * 16,
                              val);
                 }
@@ -634,6 +640,10 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + KPAR * (PB /
 constexpr int kDepthFull = 8;     // window depth for 128-byte row parts (ring of 16 slots)
 constexpr int kDepthHalf = 12;    // for 64-byte row parts (ring of 24 slots)
 static_assert(kDepthFull <= HZ_MAXWIN && kDepthHalf <= HZ_MAXWIN, "window depth covered by the pre-pass");
+// y staging by chunk parity: a row of chunk c+2 is written no earlier than D steps after
+// step t0(c)+32-D finished, which is after the owning warp flushed chunk c when D + KPAR <= CHS + 1
+static_assert(kDepthFull + GatherCfg<128>::KPAR <= CHS + 1 && kDepthHalf + GatherCfg<64>::KPAR <= CHS + 1,
+              "y staging depth");
 
 // row part bytes for a call: 128 (full 64-column fp16 rows), or 64 (two CTAs per lane)
 int ws_part_bytes(int B, int H, int Dh) {
@@ -652,7 +662,7 @@ int launch_ws(const WsParams& p, int lanes, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SL.total);
     if (e != cudaSuccess) return dg_host::record_cuda_error(e);
     dim3 grid(p.parts, lanes);
-    kern<<<grid, 32 * (GatherCfg<PB>::ROLE_WARPS + KPAR * (PB / 32)), SL.total, stream>>>(p);
+    kern<<<grid, 32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB>::KPAR * (PB / 32)), SL.total, stream>>>(p);
     return dg_host::check_launch();
 }
 
