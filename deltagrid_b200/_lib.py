@@ -92,5 +92,17 @@ def check(status: int, what: str) -> None:
         raise DeltaGridError(f"{what} failed: {msg} [status {status}]")
 
 
+_fns = {}
+
+
+def fn(name: str):
+    """The bound C function `name` (looked up once)."""
+    f = _fns.get(name)
+    if f is None:
+        f = getattr(lib(), name)
+        _fns[name] = f
+    return f
+
+
 def call(name: str, *args) -> None:
-    check(getattr(lib(), name)(*args), name)
+    check(fn(name)(*args), name)

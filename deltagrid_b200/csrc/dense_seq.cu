@@ -270,8 +270,121 @@ __global__ void __launch_bounds__(CW * NG) dense_step_kernel(DenseStepParams p) 
     }
 }
 
+// Decode step, vectorised: one CTA of 256 threads per lane, the lane's S x 64 state
+// held in registers as 16-byte vectors (NV per thread, read once with coalesced
+// 16-byte loads: 4 KB per pass of the CTA).  Thread t owns, in pass w, row
+// w * RPW + t / NG and the CPV columns (t % NG) * CPV ..; y and pred are summed over
+// its rows, then over the threads of its column group (shuffles, then across warps in
+// shared memory); the new rows go back as 16-byte stores.  The whole lane is read
+// before any of it is written, so s_next may alias s_prev.
+constexpr int STEPV_THREADS = 256;
+template <typename T, int NV>
+__global__ void __launch_bounds__(STEPV_THREADS) dense_step_vec_kernel(DenseStepParams p) {
+    constexpr int CPV = 16 / (int)sizeof(T);            // columns per 16-byte vector
+    constexpr int NG = 64 / CPV;                         // column groups (Dh = 64)
+    constexpr int RPW = STEPV_THREADS / NG;              // rows per pass
+    __shared__ float red[2][STEPV_THREADS / 32][64];
+    __shared__ float rr[64];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int cg = tid % NG, rsub = tid / NG;
+    const int ln = blockIdx.x, b = ln / p.H, h = ln % p.H;
+    const int S = p.S;
+    const T* wk = static_cast<const T*>(p.wk) + b * p.wk_sb + h * p.wk_sh;
+    const T* wq = static_cast<const T*>(p.wq) + b * p.wq_sb + h * p.wq_sh;
+    const uint8_t* sp = static_cast<const uint8_t*>(p.s_prev) + (int64_t)ln * S * 64 * sizeof(T);
+    uint8_t* sn = static_cast<uint8_t*>(p.s_next) + (int64_t)ln * S * 64 * sizeof(T);
+
+    uint4 sv[NV];
+    float wkv[NV];
+#pragma unroll
+    for (int w = 0; w < NV; ++w) {
+        const int m = w * RPW + rsub;
+        sv[w] = dg::ld16(sp + ((int64_t)m * 64 + cg * CPV) * sizeof(T));
+        wkv[w] = dg::to_f(wk[m]);
+    }
+    float ya[CPV], pa[CPV];
+#pragma unroll
+    for (int i = 0; i < CPV; ++i) { ya[i] = 0.f; pa[i] = 0.f; }
+#pragma unroll
+    for (int w = 0; w < NV; ++w) {
+        const float wqm = dg::to_f(wq[w * RPW + rsub]);
+        const T* e = reinterpret_cast<const T*>(&sv[w]);
+#pragma unroll
+        for (int i = 0; i < CPV; ++i) {
+            const float x = dg::to_f(e[i]);
+            ya[i] = fmaf(wqm, x, ya[i]);
+            pa[i] = fmaf(wkv[w], x, pa[i]);
+        }
+    }
+    // threads of a column group: lanes l with l % NG equal, then the warps
+#pragma unroll
+    for (int o = NG; o < 32; o <<= 1) {
+#pragma unroll
+        for (int i = 0; i < CPV; ++i) {
+            ya[i] += __shfl_xor_sync(DG_FULL_MASK, ya[i], o);
+            pa[i] += __shfl_xor_sync(DG_FULL_MASK, pa[i], o);
+        }
+    }
+    if (lane < NG) {
+#pragma unroll
+        for (int i = 0; i < CPV; ++i) {
+            red[0][warp][cg * CPV + i] = ya[i];
+            red[1][warp][cg * CPV + i] = pa[i];
+        }
+    }
+    __syncthreads();
+    if (tid < 64) {
+        float y = 0.f, pr = 0.f;
+#pragma unroll
+        for (int k = 0; k < STEPV_THREADS / 32; ++k) { y += red[0][k][tid]; pr += red[1][k][tid]; }
+        const T* v = static_cast<const T*>(p.v) + b * p.v_sb + h * p.v_sh;
+        static_cast<T*>(p.out)[(int64_t)ln * 64 + tid] = dg::from_f<T>(y);
+        rr[tid] = dg::to_f(v[tid]) - pr;
+    }
+    __syncthreads();
+    const T* decay = static_cast<const T*>(p.decay);
+    const float al = p.dynamic_decay ? dg::to_f(decay[b * p.decay_sb + h * p.decay_sh]) : dg::to_f(decay[h]);
+    const float bt = dg::to_f(static_cast<const T*>(p.beta)[b * p.beta_sb + h * p.beta_sh]);
+    float r[CPV];
+#pragma unroll
+    for (int i = 0; i < CPV; ++i) r[i] = rr[cg * CPV + i];
+#pragma unroll
+    for (int w = 0; w < NV; ++w) {
+        const int m = w * RPW + rsub;
+        const float c = bt * wkv[w];
+        const T* e = reinterpret_cast<const T*>(&sv[w]);
+        uint4 o;
+        T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int i = 0; i < CPV; ++i) oe[i] = dg::from_f<T>(fmaf(al, dg::to_f(e[i]), c * r[i]));
+        dg::st16(sn + ((int64_t)m * 64 + cg * CPV) * sizeof(T), o);
+    }
+}
+
+template <typename T, int NV>
+int launch_step_vec(const DenseStepParams& p, cudaStream_t s) {
+    dense_step_vec_kernel<T, NV><<<p.B * p.H, STEPV_THREADS, 0, s>>>(p);
+    return dg_host::check_launch();
+}
+
 template <typename T>
 int dispatch_step(const DenseStepParams& p, cudaStream_t s) {
+    // the vectorised kernel: Dh = 64, 16-byte aligned state, and a lane state of 1, 2,
+    // 4, 8 or 16 passes of 4 KB (e.g. 256 slots in bf16 = 8 passes)
+    if (p.Dh == 64 && sizeof(T) <= 4) {
+        const int64_t lane_bytes = (int64_t)p.S * 64 * sizeof(T);
+        const bool al = ((uintptr_t)p.s_prev & 15) == 0 && ((uintptr_t)p.s_next & 15) == 0;
+        if (al && lane_bytes % (STEPV_THREADS * 16) == 0) {
+            switch (lane_bytes / (STEPV_THREADS * 16)) {
+            case 1: return launch_step_vec<T, 1>(p, s);
+            case 2: return launch_step_vec<T, 2>(p, s);
+            case 4: return launch_step_vec<T, 4>(p, s);
+            case 8: return launch_step_vec<T, 8>(p, s);
+            case 16: return launch_step_vec<T, 16>(p, s);
+            default: break;
+            }
+        }
+    }
     constexpr int CW = 32, NG = 8;
     dim3 grid((p.Dh + CW - 1) / CW, p.B * p.H);
     if (p.S <= NG * 4) dense_step_kernel<T, CW, NG, 4><<<grid, CW * NG, 0, s>>>(p);

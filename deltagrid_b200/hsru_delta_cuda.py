@@ -50,8 +50,35 @@ def _contig(t: torch.Tensor) -> torch.Tensor:
     return t if t.is_contiguous() else t.contiguous()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(t: torch.Tensor) -> int:
+    # the caller's current stream on t's device (the raw handle: no Stream object)
+    if _raw_stream is not None:
+        return _raw_stream(t.device.index)
     return torch.cuda.current_stream(t.device).cuda_stream
+
+
+class _on_device:
+    """`with torch.cuda.device(d)` only when d is not already current: switching the
+    device costs more host time than a decode step's kernel takes."""
+    __slots__ = ("idx", "ctx")
+
+    def __init__(self, device: torch.device):
+        self.idx = device.index
+        self.ctx = None
+
+    def __enter__(self):
+        if self.idx is not None and self.idx != torch.cuda.current_device():
+            self.ctx = torch.cuda.device(self.idx)
+            self.ctx.__enter__()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ctx is not None:
+            self.ctx.__exit__(*exc)
+        return False
 
 
 def _status_word(device: torch.device) -> torch.Tensor:
@@ -110,7 +137,7 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.Tenso
     s_final_f = (torch.empty((B, H, slots, Dh), dtype=torch.float32, device=v_c.device)
                  if (save_for_backward and not is_fp32) else s_final)
     dynamic = 1 if decay_c.dim() > 1 else 0
-    with torch.cuda.device(v_c.device):
+    with _on_device(v_c.device):
         _lib.call("dg_dense_forward_ex", code, B, H, T, slots, Dh, v_c.data_ptr(), beta_c.data_ptr(),
                   wk_c.data_ptr(), wq_c.data_ptr(), decay_c.data_ptr(), dynamic,
                   s_init_c.data_ptr() if has_init else None, out.data_ptr(), s_final.data_ptr(),
@@ -145,14 +172,13 @@ def step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
     s_next = torch.empty((B, H, slots, Dh), dtype=q.dtype, device=q.device)
     _same_dtype(v_c, "step", out=out)
     d_sb, d_sh = (decay_c.stride(0), decay_c.stride(1)) if dynamic else (0, 1)
-    with torch.cuda.device(v_c.device):
-        _lib.call("dg_dense_step", code, B, H, slots, Dh,
-                  v_c.data_ptr(), v_c.stride(0), v_c.stride(1),
-                  beta.data_ptr(), beta.stride(0), beta.stride(1),
-                  wk_c.data_ptr(), wk_c.stride(0), wk_c.stride(1),
-                  wq_c.data_ptr(), wq_c.stride(0), wq_c.stride(1),
-                  decay_c.data_ptr(), int(dynamic), d_sb, d_sh,
-                  s_prev_c.data_ptr(), out.data_ptr(), s_next.data_ptr(), _stream(v_c))
+    vs, bs, ks, qs = v_c.stride(), beta.stride(), wk_c.stride(), wq_c.stride()
+    with _on_device(v_c.device):
+        _lib.check(_lib.fn("dg_dense_step")(code, B, H, slots, Dh, v_c.data_ptr(), vs[0], vs[1],
+                                            beta.data_ptr(), bs[0], bs[1], wk_c.data_ptr(), ks[0], ks[1],
+                                            wq_c.data_ptr(), qs[0], qs[1], decay_c.data_ptr(), int(dynamic),
+                                            d_sb, d_sh, s_prev_c.data_ptr(), out.data_ptr(), s_next.data_ptr(),
+                                            _stream(v_c)), "dg_dense_step")
     return [out, s_next]
 
 
@@ -177,7 +203,7 @@ def pkm_step(v: torch.Tensor, beta: torch.Tensor, wk: torch.Tensor, wq: torch.Te
     total = state_c.size(2)
     out = torch.empty((B, H, Dh), dtype=v_c.dtype, device=v_c.device)
     dynamic = 1 if decay_c.dim() > 1 else 0
-    with torch.cuda.device(v_c.device):
+    with _on_device(v_c.device):
         _lib.call("dg_pkm_step", code, B, H, A, total, Dh, v_c.data_ptr(), beta_c.data_ptr(),
                   wk_c.data_ptr(), wq_c.data_ptr(), idx_c.data_ptr(), decay_c.data_ptr(), dynamic,
                   state_c.data_ptr(), out.data_ptr(), _status_word(v_c.device).data_ptr(),
@@ -216,7 +242,7 @@ def pkm_forward_algo(v: torch.Tensor, beta: torch.Tensor, wk: torch.Tensor, wq: 
     saved = (torch.empty((B, H, T, A, Dh), dtype=v_c.dtype, device=v_c.device)
              if save_for_backward else None)
     dynamic = 1 if decay_c.dim() > 1 else 0
-    with torch.cuda.device(v_c.device):
+    with _on_device(v_c.device):
         # scratch for kernels that need it (per-row hazard codes), from torch's caching allocator
         nws = _lib.lib().dg_pkm_forward_workspace_size(code, B, H, T, A, total, Dh, int(algo))
         ws = torch.empty(nws, dtype=torch.uint8, device=v_c.device) if nws else None
@@ -280,7 +306,7 @@ def backward(grad_out: torch.Tensor, grad_s_final: Optional[torch.Tensor], v: to
     grad_wq = torch.empty_like(wq_c)
     grad_decay = torch.empty_like(decay_c) if dynamic else torch.zeros_like(decay_c)
     grad_s_init = torch.empty((B, H, S, Dh), dtype=v_c.dtype, device=v_c.device) if needs_grad_s_init else None
-    with torch.cuda.device(v_c.device):
+    with _on_device(v_c.device):
         nws = _lib.lib().dg_dense_backward_workspace_size(B, H, S, Dh)
         ws = torch.empty(nws // 4, dtype=torch.float32, device=v_c.device) if nws else None
         _lib.call("dg_dense_backward", code, B, H, T, S, Dh, go_c.data_ptr(),
@@ -332,7 +358,7 @@ def pkm_backward(grad_out: torch.Tensor, v: torch.Tensor, beta: torch.Tensor, wk
     if needs_grad_decay:
         grad_decay = (torch.empty((B, H, T), dtype=v_c.dtype, device=v_c.device) if dynamic
                       else torch.zeros((H,), dtype=v_c.dtype, device=v_c.device))
-    with torch.cuda.device(v_c.device):
+    with _on_device(v_c.device):
         _lib.call("dg_pkm_backward", code, B, H, T, A, total, Dh, go_c.data_ptr(), v_c.data_ptr(),
                   beta_c.data_ptr(), wk_c.data_ptr(), wq_c.data_ptr(), idx_c.data_ptr(), decay_c.data_ptr(),
                   dynamic, sv_c.data_ptr(), grad_state.data_ptr(), grad_v.data_ptr(), grad_beta.data_ptr(),
