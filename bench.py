@@ -40,6 +40,10 @@ WORKLOADS = {
                  desc="PKM fp16 B=16 H=8 T=8192 Dh=64 grid 128x128 top-8, routed keys"),
     "cfg4": dict(kind="pkm", B=8, H=8, T=16384, G=1024, K=8, Dh=64, dtype="float16", writes=True,
                  desc="PKM fp16 B=8 H=8 T=16384 Dh=64 grid 1024x1024 top-8, write stream (beta=1)"),
+    # BASELINE config 4 (the LM) at its decode shape: one step is one token of a 256-sequence
+    # batch through the recurrence of all 12 layers (12 dense decode steps), states resident
+    "cfg5": dict(kind="decode", B=256, H=12, T=1, S=256, Dh=64, L=12, dtype="bfloat16",
+                 desc="LM decode recurrence: 12 layers x dense step, B=256 H=12 slots=256 Dh=64 bf16"),
 }
 METRIC = "recurrence tokens/sec"
 UNIT = "tokens/s"
@@ -63,6 +67,10 @@ def _algorithmic(w):
         S = w["S"]
         per_ht = (2 * Dh + 2 * S) * e + e              # v, y, wk, wq, beta
         return ht * per_ht + B * H * S * Dh * e, ht * 6.0 * S * Dh
+    if w["kind"] == "decode":
+        S, L = w["S"], w["L"]
+        per_lane = 2 * S * Dh * e + 2 * S * e + 2 * Dh * e + 2 * e    # state in+out, wk, wq, v, y, beta, decay
+        return L * B * H * per_lane, L * B * H * 6.0 * S * Dh
     A = w["K"] ** 2
     per_ht = 2 * A * Dh * e + 2 * Dh * e + e + 2 * A * e + A * 8    # rows in+out, v, y, beta, wk, wq, idx
     return ht * per_ht, ht * 6.0 * A * Dh
@@ -121,6 +129,24 @@ def make_inputs(w, torch, device, seed=0):
     g = torch.Generator(device=device).manual_seed(seed)
     dt = getattr(torch, w["dtype"])
     B, H, T, Dh = w["B"], w["H"], w["T"], w["Dh"]
+    if w["kind"] == "decode":
+        # per layer: the step inputs the layer forms (memory.py:544-636) and its resident state
+        S, L = w["S"], w["L"]
+        gp = torch.Generator().manual_seed(1)
+        P = torch.empty(S, Dh)
+        torch.nn.init.orthogonal_(P, generator=gp)
+        P = P.to(device)
+        lay = []
+        for _ in range(L):
+            k = F.normalize(torch.randn(B, H, Dh, device=device, generator=g), dim=-1)
+            q = torch.randn(B, H, Dh, device=device, generator=g)
+            lay.append(dict(
+                q=q.to(dt), k=k.to(dt), v=torch.randn(B, H, Dh, device=device, generator=g).to(dt),
+                beta=torch.sigmoid(torch.randn(B, H, device=device, generator=g)).to(dt),
+                wk=F.normalize(k @ P.T, dim=-1).to(dt), wq=(q @ P.T).to(dt),
+                decay=(0.99 + 0.01 * torch.sigmoid(torch.randn(B, H, device=device, generator=g))).to(dt),
+                state=(0.1 * torch.randn(B, H, S, Dh, device=device, generator=g)).to(dt)))
+        return dict(layers=lay)
     if w["kind"] == "dense":
         S = w["S"]
         k = F.normalize(torch.randn(B, H, T, Dh, device=device, generator=g), dim=-1)
@@ -164,11 +190,22 @@ def make_inputs(w, torch, device, seed=0):
 
 def launches_per_step(w):
     """Kernels one step launches: the dense kernel; for 16-bit PKM the hazard pre-pass
-    and the recurrence (pkm_hazard_kernel, pkm_ws_kernel)."""
+    and the recurrence (pkm_hazard_kernel, pkm_ws_kernel); for decode one step kernel
+    per layer (dense_step_vec_kernel)."""
+    if w["kind"] == "decode":
+        return w["L"]
     return 2 if w["kind"] == "pkm" and w["dtype"] != "float32" else 1
 
 
 def run_step(ext, w, d):
+    if w["kind"] == "decode":
+        ys = []
+        for lay in d["layers"]:
+            y, s = ext.step(lay["q"], lay["k"], lay["v"], lay["beta"], lay["wk"], lay["wq"], lay["decay"],
+                            lay["state"])
+            lay["state"] = s
+            ys.append(y)
+        return [ys[-1]]
     if w["kind"] == "dense":
         return ext.forward(d["q"], d["k"], d["v"], d["beta"], d["wk"], d["wq"], d["decay"])
     return ext.pkm_forward(d["v"], d["beta"], d["wk"], d["wq"], d["idx"], d["decay"], d["state"])
@@ -181,7 +218,7 @@ def cpu_baseline_port(w, threads):
     O.set_threads(threads)
     rs = np.random.RandomState(0)
     H, Dh = w["H"], w["Dh"]
-    if w["kind"] == "dense":
+    if w["kind"] in ("dense", "decode"):
         S = w["S"]
         T = 64 if S >= 256 else 512
         Bs = 1
@@ -200,6 +237,10 @@ def cpu_baseline_port(w, threads):
                 break
         dt = time.perf_counter() - t0
         tok = reps * Bs * T
+        if w["kind"] == "decode":             # a token of the LM passes the recurrence of L layers
+            return dict(value=tok / dt / w["L"], unit=UNIT, cores=threads, kind="port",
+                        sample=f"oracle dense_forward, {Bs}x{H} lanes x T={T}, slots={S}, fp32, x{reps}, "
+                               f"divided by {w['L']} layers")
         return dict(value=tok / dt, unit=UNIT, cores=threads, kind="port",
                     sample=f"oracle dense_forward, {Bs}x{H} lanes x T={T}, slots={S}, fp32, x{reps}")
     G, K = w["G"], w["K"]
@@ -243,19 +284,20 @@ def reference_arm(args, w):
     if O.ref_available():
         os.environ.setdefault("OMP_NUM_THREADS", str(threads))
         H, Dh = w["H"], w["Dh"]
-        if w["kind"] == "dense":
+        if w["kind"] in ("dense", "decode"):
             mode = 0 if w["S"] == Dh else 1
             kw = dict(slots=w["S"]) if mode == 1 else {}
         else:
             mode = 2
             kw = dict(G0=w["G"], G1=w["G"], topk=w["K"])
         contexts = 1 if w["kind"] == "pkm" and w["G"] >= 1024 else min(w["B"], 4)
-        steps = 8 if w["kind"] == "dense" and w["S"] >= 256 else 64
+        steps = 8 if w["kind"] in ("dense", "decode") and w["S"] >= 256 else 64
+        per_token = w.get("L", 1)             # decode: a token passes the recurrence of every layer
         O.ref_f32_time(mode, H, Dh, 2, contexts, **kw)               # warm-up
         vals, projs = [], []
         for _ in range(max(1, args.steps)):
             t, p = O.ref_f32_time(mode, H, Dh, steps, contexts, **kw)
-            vals.append(contexts * steps / t)
+            vals.append(contexts * steps / t / per_token)
             projs.append(p / t)
         value = statistics.median(vals)
         sample = (f"reference C++ engine dg_memory_layer_step (deltagrid_math.cpp:174-417), "
@@ -353,7 +395,45 @@ def main():
 
     # end to end through the public API: pinned host inputs in, result out, every step
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and w["kind"] == "decode":
+        # every step: the layers' step inputs from pinned host memory, y of the last layer back
+        names = ("q", "k", "v", "beta", "wk", "wq", "decay")
+        host = [{n: lay[n].to("cpu").pin_memory() for n in names} for lay in d["layers"]]
+        h2d = sum(t.numel() * t.element_size() for hl in host for t in hl.values())
+        dev_in = [{n: torch.empty_like(lay[n]) for n in names} for lay in d["layers"]]
+        y_host = torch.empty(d["layers"][-1]["v"].shape, dtype=d["layers"][-1]["v"].dtype, pin_memory=True)
+        d2h = y_host.numel() * y_host.element_size()
+
+        def e2e_step():
+            for lay, hl, dl in zip(d["layers"], host, dev_in):
+                for n in names:
+                    dl[n].copy_(hl[n], non_blocking=True)
+            ys = None
+            for lay, dl in zip(d["layers"], dev_in):
+                ys, lay["state"] = ext.step(dl["q"], dl["k"], dl["v"], dl["beta"], dl["wk"], dl["wq"],
+                                            dl["decay"], lay["state"])
+            y_host.copy_(ys, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize(device)
+        k2 = max(2, min(args.steps, 5))
+        if world > 1:
+            dist.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(k2):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        e_ms = a.elapsed_time(b) / k2
+        if world > 1:
+            tt = torch.tensor([e_ms], device=device)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e_ms = float(tt.item())
+        e2e = {"value": tokens_per_step / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "steps": k2}
+    elif not args.no_e2e:
         names = [n for n in ("v", "beta", "wk", "wq", "idx") if n in d]
         host = {n: d[n].to("cpu").pin_memory() for n in names}
         h2d = sum(t.numel() * t.element_size() for t in host.values())
@@ -435,7 +515,7 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": {"float16": "f16", "float32": "f32"}[w["dtype"]],
+        "vs_baseline": None, "dtype": {"float16": "f16", "float32": "f32", "bfloat16": "bf16"}[w["dtype"]],
         "data": "synthetic (seeded, BASELINE distributions, resident in HBM; inputs > L2, no flush)",
         "config": {"workload": f"{args.workload}: {w['desc']}", "global_batch": w["B"] * world,
                    "per_gpu_batch": w["B"], "seq_len": w["T"], "parallelism": f"dp{world} (batch shards)",
