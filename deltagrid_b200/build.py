@@ -1,10 +1,15 @@
-"""Builds libdeltagrid_b200.so in-tree with nvcc for sm_100a.
+"""Builds the native parts in-tree.
 
     python -m deltagrid_b200.build          (or deltagrid_b200.build.build())
 
-Every .cu under csrc/ is compiled to an object in parallel, then linked into a
-shared library next to this file.  Rebuilds only what changed (by mtime,
-including the shared headers).
+1. libdeltagrid_b200.so: every .cu under csrc/ compiled with nvcc for sm_100a in
+   parallel, then linked into a shared library next to this file (the C ABI of
+   include/deltagrid_b200.h).
+2. _hsru<ext suffix>: csrc/binding.cpp, the compiled torch extension behind
+   deltagrid_b200.hsru_delta_cuda, built with the host C++ compiler against
+   torch's headers and linked to libdeltagrid_b200.so (found next to it at run time).
+
+Rebuilds only what changed (by mtime, including the shared headers).
 """
 from __future__ import annotations
 
@@ -14,11 +19,14 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libdeltagrid_b200.so")
+BINDING_SRC = os.path.join(CSRC, "binding.cpp")
+BINDING = os.path.join(HERE, "_hsru" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -51,6 +59,29 @@ def _compile(src: str, verbose: bool) -> str:
     return obj
 
 
+def _build_binding() -> str:
+    """The torch extension module `_hsru` (needs torch's headers and libraries, no GPU)."""
+    deps = [BINDING_SRC, LIB, os.path.join(INCLUDE, "deltagrid_b200.h")]
+    if os.path.exists(BINDING) and os.path.getmtime(BINDING) >= max(os.path.getmtime(d) for d in deps):
+        return BINDING
+    import torch
+    tdir = os.path.dirname(torch.__file__)
+    tinc = os.path.join(tdir, "include")
+    tlib = os.path.join(tdir, "lib")
+    cuda_home = os.path.dirname(os.path.dirname(os.path.realpath(nvcc())))
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "c++"
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", BINDING_SRC, "-o", BINDING,
+           f"-I{tinc}", f"-I{os.path.join(tinc, 'torch', 'csrc', 'api', 'include')}",
+           f"-I{os.path.join(cuda_home, 'include')}", f"-I{sysconfig.get_paths()['include']}", f"-I{INCLUDE}",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}", "-DTORCH_EXTENSION_NAME=_hsru",
+           "-DTORCH_API_INCLUDE_EXTENSION_H", f"-L{tlib}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+           "-ltorch_python", f"-L{HERE}", "-ldeltagrid_b200", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{tlib}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"binding build failed:\n{r.stdout}\n{r.stderr}")
+    return BINDING
+
+
 def build(verbose: bool = False) -> str:
     os.makedirs(OBJ, exist_ok=True)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
@@ -61,6 +92,7 @@ def build(verbose: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    _build_binding()
     return LIB
 
 
