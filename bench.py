@@ -197,7 +197,7 @@ def launches_per_step(w):
     return 2 if w["kind"] == "pkm" and w["dtype"] != "float32" else 1
 
 
-def run_step(ext, w, d):
+def run_step(ext, w, d, algo=0):
     if w["kind"] == "decode":
         ys = []
         for lay in d["layers"]:
@@ -207,7 +207,11 @@ def run_step(ext, w, d):
             ys.append(y)
         return [ys[-1]]
     if w["kind"] == "dense":
+        if algo:
+            return ext.forward(d["q"], d["k"], d["v"], d["beta"], d["wk"], d["wq"], d["decay"], algo=algo)
         return ext.forward(d["q"], d["k"], d["v"], d["beta"], d["wk"], d["wq"], d["decay"])
+    if algo:
+        return ext.pkm_forward_algo(d["v"], d["beta"], d["wk"], d["wq"], d["idx"], d["decay"], d["state"], False, algo)
     return ext.pkm_forward(d["v"], d["beta"], d["wk"], d["wq"], d["idx"], d["decay"], d["state"])
 
 
@@ -320,7 +324,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--algo", type=int, default=0, help="dense algorithm (0 auto, 1 sequential, 2 chunked tcgen05)")
+    ap.add_argument("--algo", type=int, default=0,
+                    help="kernel selector: dense 0 auto, 1 sequential, 2 chunked tcgen05; "
+                         "PKM 0 auto, 1 one step, 2 pipelined, 3 warp-specialised")
     ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (small profiling cases)")
     ap.add_argument("--seq", type=int, default=0, help="override the sequence length T (small profiling cases)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -359,7 +365,7 @@ def main():
 
     def step():
         nonlocal d
-        r = run_step(ext, w, d)
+        r = run_step(ext, w, d, args.algo)
         return r
 
     for _ in range(args.warmup):
@@ -451,7 +457,7 @@ def main():
             dd.update(dev_in)
             if w["kind"] == "dense":
                 dd["q"] = dd["k"] = dd["v"]
-            o = run_step(ext, w, dd)
+            o = run_step(ext, w, dd, args.algo)
             for src, dst in zip(o[:n_res], res_host):
                 dst.copy_(src, non_blocking=True)
 
@@ -478,7 +484,7 @@ def main():
     # verification (outside the timed region): per-rank checksums of the last
     # step's outputs gathered over NCCL; no collective touches the data path
     from deltagrid_b200.shard import checksum
-    outs = run_step(ext, w, d)
+    outs = run_step(ext, w, d, args.algo)
     cs = checksum(outs[0])
     verify = None
     if world > 1:
