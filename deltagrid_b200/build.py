@@ -3,8 +3,9 @@
     python -m deltagrid_b200.build          (or deltagrid_b200.build.build())
 
 1. libdeltagrid_b200.so: every .cu under csrc/ compiled with nvcc for sm_100a in
-   parallel, then linked into a shared library next to this file (the C ABI of
-   include/deltagrid_b200.h).
+   parallel, and the host-only .cpp sources (all but binding.cpp) through nvcc's
+   host compiler, then linked into a shared library next to this file (the C ABI
+   of include/deltagrid_b200.h).
 2. _hsru<ext suffix>: csrc/binding.cpp, the compiled torch extension behind
    deltagrid_b200.hsru_delta_cuda, built with the host C++ compiler against
    torch's headers and linked to libdeltagrid_b200.so (found next to it at run time).
@@ -45,7 +46,7 @@ def _headers_mtime() -> float:
 
 
 def _compile(src: str, verbose: bool) -> str:
-    obj = os.path.join(OBJ, os.path.basename(src).replace(".cu", ".o"))
+    obj = os.path.join(OBJ, os.path.splitext(os.path.basename(src))[0] + ".o")
     if os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(src), _headers_mtime()):
         return obj
     cmd = [nvcc()] + NVCC_FLAGS + ["-c", src, "-o", obj]
@@ -85,6 +86,7 @@ def _build_binding() -> str:
 def build(verbose: bool = False) -> str:
     os.makedirs(OBJ, exist_ok=True)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    srcs += sorted(p for p in glob.glob(os.path.join(CSRC, "*.cpp")) if p != BINDING_SRC)
     with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
     if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):

@@ -60,6 +60,7 @@ const char* dg_status_string(int status) {
     case DG_ERR_WORKSPACE: return "workspace missing or too small";
     case DG_ERR_CUDA: return "CUDA error";
     case DG_ERR_DEVICE_CHECK: return "device-side check failed";
+    case DG_ERR_FORMAT: return "engine file unreadable, truncated or inconsistent";
     default: return "unknown status";
     }
 }

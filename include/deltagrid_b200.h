@@ -41,7 +41,8 @@ typedef enum dg_status {
     DG_ERR_MISALIGNED = -3,       /* a pointer lacks the alignment the kernel needs */
     DG_ERR_WORKSPACE = -4,        /* workspace missing or smaller than *_workspace_size */
     DG_ERR_CUDA = -5,             /* CUDA launch/runtime error (dg_last_cuda_error) */
-    DG_ERR_DEVICE_CHECK = -6      /* a kernel's own check tripped (dg_read_device_status) */
+    DG_ERR_DEVICE_CHECK = -6,     /* a kernel's own check tripped (dg_read_device_status) */
+    DG_ERR_FORMAT = -7            /* an engine file unreadable, truncated or inconsistent */
 } dg_status;
 
 /* dense-forward algorithm selector for dg_dense_forward_ex */
@@ -254,6 +255,85 @@ int dg_pkm_route(int dtype, int B, int H, int T, int dh, int g0, int g1, int top
                  const void* q, const float* router_k0, const float* router_k1, const float* router_q0,
                  const float* router_q1, const float* q_scale, void* wk, void* wq, int64_t* idx,
                  void* stream);
+
+/* ---------------------------------------------------------------------------
+ * The reference C++ engine's files (src/cpp/engine), read and written on the
+ * host so that its weights and recurrent state can drive the GPU recurrence
+ * (dg_fxp_* for Q16.16 files, dg_dense_forward / dg_pkm_forward for fp32 ones).
+ * ------------------------------------------------------------------------- */
+
+/* DeltaGridBinHeader (src/cpp/engine/include/deltagrid_internal.h:65-82) */
+typedef struct dg_dlg1_header {
+    int32_t magic, version, model_type, precision_mode, num_layers, d_model, num_heads, kernel_size,
+        thinking_cycles, input_or_vocab, output_dim, forecast_horizon, num_axes, top_k, actual_slots, flags;
+} dg_dlg1_header;
+
+#define DG_DLG1_MAX_AXES 8
+
+typedef enum dg_dlg1_encoding {
+    DG_ENC_F32 = 0, /* fp32 */
+    DG_ENC_Q8 = 1,  /* int8, value = q * scale (the fp32 scale precedes the bytes) */
+    DG_ENC_Q16 = 2  /* int32 Q16.16 */
+} dg_dlg1_encoding;
+
+/* one array of a DLG1 file: names follow the engine's struct fields
+   ("input_weight", "memory.decay", "memory.axes_proj_k", "ffn_fc1_weight", ...) */
+typedef struct dg_dlg1_array {
+    char name[32];
+    int32_t layer;    /* block index, -1 outside the blocks */
+    int32_t axis;     /* axis of memory.axes_proj_k / _q, else -1 */
+    int32_t encoding; /* dg_dlg1_encoding */
+    float scale;      /* DG_ENC_Q8 dequantisation scale, else 1 */
+    int64_t offset;   /* byte offset of the first element */
+    int64_t count;    /* elements */
+} dg_dlg1_array;
+
+/*
+ * DLG1 weights layout.  Replaces the read order of dg_load_context_from_file
+ * (src/cpp/engine/src/deltagrid_math.cpp:558-761, fp32 / int8 files) and
+ * deltagrid_init_context_fxp (src/cpp/engine/src/deltagrid_fxp.cpp:503-660,
+ * Q16.16 files), as written by export_deltagrid_to_bin
+ * (src/cpp/engine/tools/export_deltagrid_binary.py:77-237).  Fills *hdr, grid_dim
+ * (up to max_axes) and up to max_arrays entries of `arrays` (NULL: count only);
+ * *n_arrays = the file's array count.  DG_ERR_FORMAT for a bad magic, precision
+ * or shape, a truncated file or trailing bytes; DG_ERR_WORKSPACE when `arrays`
+ * is too short.  Opens and closes the file; keeps nothing.
+ */
+int dg_dlg1_layout(const char* path, dg_dlg1_header* hdr, int32_t* grid_dim, int max_axes, dg_dlg1_array* arrays,
+                   int max_arrays, int* n_arrays);
+
+/* DLGS state snapshot header (the six words after the magic,
+   src/cpp/engine/src/deltagrid_math.cpp:779-811) */
+typedef struct dg_dlgs_header {
+    int32_t num_layers, d_model, num_heads, actual_slots, kernel_size, step_count;
+} dg_dlgs_header;
+
+/* per-layer element counts: conv window d_model * max(kernel_size - 1, 1), memory
+   state num_heads * actual_slots * (d_model / num_heads) */
+size_t dg_dlgs_conv_elems(const dg_dlgs_header* h);
+size_t dg_dlgs_mem_elems(const dg_dlgs_header* h);
+
+/* Reads and checks the header (magic, shape, file length). */
+int dg_dlgs_read_header(const char* path, dg_dlgs_header* h);
+
+/*
+ * One layer of a snapshot.  Replaces dg_load_runtime_state
+ * (src/cpp/engine/src/deltagrid_math.cpp:812-844) and deltagrid_load_state_fxp
+ * (deltagrid_fxp.cpp:762-795) for one layer: the file's shape must equal
+ * `expect` (the step count may differ).  conv_state / mem_state (either may be
+ * NULL) receive 4-byte elements: fp32 for the float engine, Q16.16 for the
+ * fixed-point engine; mem_state is [num_heads, actual_slots, d_model/num_heads],
+ * the lanes-first layout of the GPU kernels.
+ */
+int dg_dlgs_read_layer(const char* path, const dg_dlgs_header* expect, int layer, void* conv_state, void* mem_state);
+
+/*
+ * Writes a snapshot.  Replaces dg_save_runtime_state (deltagrid_math.cpp:779-810)
+ * and deltagrid_save_state_fxp (deltagrid_fxp.cpp:728-760); conv_layers[l] and
+ * mem_layers[l] point at layer l's states (host memory, 4-byte elements).
+ */
+int dg_dlgs_write(const char* path, const dg_dlgs_header* h, const void* const* conv_layers,
+                  const void* const* mem_layers);
 
 /* Reads (and clears when `clear`) a device status word; synchronizes `stream`. */
 int dg_read_device_status(int32_t* dev_status, int clear, int32_t* host_value, void* stream);

@@ -11,7 +11,9 @@
 // and exports, per step, the kernel-level inputs the engine computed (routed
 // wk/wq/idx, v, beta, alpha) and its read-out y_t, plus the final state.  The
 // oracle restatement (dg_oracle.c) must reproduce y and the state from those
-// inputs.  A second entry point times the engine for the CPU baseline.
+// inputs.  A second entry point times the engine for the CPU baseline.  The
+// file entry points (ref_*_file_run) drive the engine through its own public API
+// from a DLG1 weights file and DLGS snapshots, for the engine-file fixtures.
 //
 // Engine modes: 0 = dense (Slots == Dh), 1 = dense with slot projection,
 // 2 = sparse PKM (two axes, top_k).
@@ -20,6 +22,7 @@
 #include "deltagrid_math.cpp"
 #include "deltagrid_math_fxp.cpp"
 #include "deltagrid_fxp.cpp"
+#include "deltagrid_continuous.cpp"
 
 #include <chrono>
 #include <cstdint>
@@ -341,6 +344,72 @@ double ref_fxp_time(int mode, int H, int Dh, int slots, int G0, int G1, int topk
 // Top-k known-answer entry (deltagrid_math.cpp:142-168 as shipped).
 void ref_topk_desc(const float* scores, int n, int k, float* vals, int32_t* idx) {
     dg_topk_descending(scores, n, k, vals, idx);
+}
+
+// Engine files end to end (DLG1 weights, DLGS snapshots).  The engine loads a
+// continuous-model weights file through its own API (deltagrid_init_context_fxp,
+// deltagrid_fxp.cpp:503; deltagrid_init_context, deltagrid_continuous.cpp:17),
+// optionally a snapshot (deltagrid_load_state_fxp / deltagrid_load_state), runs T
+// steps of its full model step on seeded inputs, and writes its final snapshot
+// (deltagrid_save_state_fxp / deltagrid_save_state).  After each step the
+// context's shared memory-tier buffers hold the last block's kernel-level inputs
+// and read-out; they are exported per step ([T, H, A], [T, D], [T, H]) -- the
+// fixtures use one block, so that block is the one exported.  Returns 0, or -1
+// when a file is refused.
+int ref_fxp_file_run(const char* weights, const char* state_in, const char* state_out, int T,
+                     unsigned long long seed, int32_t* wk_out, int32_t* wq_out, int32_t* idx_out,
+                     int32_t* v_out, int32_t* beta_out, int32_t* alpha_out, int32_t* y_out) {
+    DGFxpContext* ctx = static_cast<DGFxpContext*>(deltagrid_init_context_fxp(weights));
+    if (!ctx) return -1;
+    if (state_in && deltagrid_load_state_fxp(ctx, state_in) != 0) {
+        deltagrid_release_context_fxp(ctx);
+        return -1;
+    }
+    const int H = ctx->header.num_heads, D = ctx->header.d_model, A = ctx->active_slots;
+    std::vector<int32_t> in(ctx->header.input_or_vocab), out(ctx->header.output_dim);
+    Rng r(seed);
+    for (int t = 0; t < T; ++t) {
+        for (auto& x : in) x = DG_FLOAT_TO_FXP(r.normal());
+        deltagrid_step_fxp(ctx, in.data(), out.data());
+        std::memcpy(wk_out + (size_t)t * H * A, ctx->wk_buf, sizeof(int32_t) * H * A);
+        std::memcpy(wq_out + (size_t)t * H * A, ctx->wq_buf, sizeof(int32_t) * H * A);
+        if (idx_out) std::memcpy(idx_out + (size_t)t * H * A, ctx->active_idx_buf, sizeof(int32_t) * H * A);
+        std::memcpy(v_out + (size_t)t * D, ctx->v_buf, sizeof(int32_t) * D);
+        std::memcpy(beta_out + (size_t)t * H, ctx->beta_buf, sizeof(int32_t) * H);
+        std::memcpy(alpha_out + (size_t)t * H, ctx->alpha_buf, sizeof(int32_t) * H);
+        std::memcpy(y_out + (size_t)t * D, ctx->yt_buf, sizeof(int32_t) * D);
+    }
+    const int rc = state_out ? deltagrid_save_state_fxp(ctx, state_out) : 0;
+    deltagrid_release_context_fxp(ctx);
+    return rc == 0 ? 0 : -1;
+}
+
+int ref_f32_file_run(const char* weights, const char* state_in, const char* state_out, int T,
+                     unsigned long long seed, float* wk_out, float* wq_out, int32_t* idx_out, float* v_out,
+                     float* beta_out, float* alpha_out, float* y_out) {
+    DGRuntimeContext* ctx = static_cast<DGRuntimeContext*>(deltagrid_init_context(weights));
+    if (!ctx) return -1;
+    if (state_in && deltagrid_load_state(ctx, state_in) != 0) {
+        dg_free_runtime_context(ctx);
+        return -1;
+    }
+    const int H = ctx->header.num_heads, D = ctx->header.d_model, A = ctx->active_slots;
+    std::vector<float> in(ctx->header.input_or_vocab), out(ctx->header.output_dim);
+    Rng r(seed);
+    for (int t = 0; t < T; ++t) {
+        for (auto& x : in) x = r.normal();
+        deltagrid_step(ctx, in.data(), out.data());
+        std::memcpy(wk_out + (size_t)t * H * A, ctx->wk_buf, sizeof(float) * H * A);
+        std::memcpy(wq_out + (size_t)t * H * A, ctx->wq_buf, sizeof(float) * H * A);
+        if (idx_out) std::memcpy(idx_out + (size_t)t * H * A, ctx->active_idx_buf, sizeof(int32_t) * H * A);
+        std::memcpy(v_out + (size_t)t * D, ctx->v_buf, sizeof(float) * D);
+        std::memcpy(beta_out + (size_t)t * H, ctx->beta_buf, sizeof(float) * H);
+        std::memcpy(alpha_out + (size_t)t * H, ctx->alpha_buf, sizeof(float) * H);
+        std::memcpy(y_out + (size_t)t * D, ctx->yt_buf, sizeof(float) * D);
+    }
+    const int rc = state_out ? deltagrid_save_state(ctx, state_out) : 0;
+    dg_free_runtime_context(ctx);
+    return rc == 0 ? 0 : -1;
 }
 
 }  // extern "C"
