@@ -361,6 +361,109 @@ __global__ void __launch_bounds__(STEPV_THREADS) dense_step_vec_kernel(DenseStep
     }
 }
 
+// Decode step, staged: the same thread mapping and arithmetic as dense_step_vec_kernel,
+// but the lane's state goes to shared memory through cp.async (16 bytes a copy) instead
+// of registers, so a thread keeps only its accumulators (wk and wq are re-read, from
+// L1): 5 CTAs (5 lanes, 160 KB of state for bf16 at 256 slots) are in flight per SM
+// instead of 2.  Each thread reads
+// back only the vectors it copied (cp.async.wait_all orders them for that thread).
+template <typename T, int NV>
+__global__ void __launch_bounds__(STEPV_THREADS, 5) dense_step_staged_kernel(DenseStepParams p) {
+    constexpr int CPV = 16 / (int)sizeof(T);
+    constexpr int NG = 64 / CPV;
+    constexpr int RPW = STEPV_THREADS / NG;
+    extern __shared__ __align__(16) uint8_t st_smem[];               // [S][64] state of the lane
+    __shared__ float red[2][STEPV_THREADS / 32][64];
+    __shared__ float rr[64];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int cg = tid % NG, rsub = tid / NG;
+    const int ln = blockIdx.x, b = ln / p.H, h = ln % p.H;
+    const int S = p.S;
+    const T* wk = static_cast<const T*>(p.wk) + b * p.wk_sb + h * p.wk_sh;
+    const T* wq = static_cast<const T*>(p.wq) + b * p.wq_sb + h * p.wq_sh;
+    const uint8_t* sp = static_cast<const uint8_t*>(p.s_prev) + (int64_t)ln * S * 64 * sizeof(T);
+    uint8_t* sn = static_cast<uint8_t*>(p.s_next) + (int64_t)ln * S * 64 * sizeof(T);
+    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(st_smem));
+#pragma unroll
+    for (int w = 0; w < NV; ++w) {
+        const int64_t off = ((int64_t)(w * RPW + rsub) * 64 + cg * CPV) * sizeof(T);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sbase + (uint32_t)off), "l"(sp + off)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    float ya[CPV], pa[CPV];
+#pragma unroll
+    for (int i = 0; i < CPV; ++i) { ya[i] = 0.f; pa[i] = 0.f; }
+#pragma unroll
+    for (int w = 0; w < NV; ++w) {
+        const uint4 sv = *reinterpret_cast<const uint4*>(st_smem + ((w * RPW + rsub) * 64 + cg * CPV) * sizeof(T));
+        const float wqm = dg::to_f(wq[w * RPW + rsub]), wkm = dg::to_f(wk[w * RPW + rsub]);
+        const T* e = reinterpret_cast<const T*>(&sv);
+#pragma unroll
+        for (int i = 0; i < CPV; ++i) {
+            const float x = dg::to_f(e[i]);
+            ya[i] = fmaf(wqm, x, ya[i]);
+            pa[i] = fmaf(wkm, x, pa[i]);
+        }
+    }
+#pragma unroll
+    for (int o = NG; o < 32; o <<= 1) {
+#pragma unroll
+        for (int i = 0; i < CPV; ++i) {
+            ya[i] += __shfl_xor_sync(DG_FULL_MASK, ya[i], o);
+            pa[i] += __shfl_xor_sync(DG_FULL_MASK, pa[i], o);
+        }
+    }
+    if (lane < NG) {
+#pragma unroll
+        for (int i = 0; i < CPV; ++i) {
+            red[0][warp][cg * CPV + i] = ya[i];
+            red[1][warp][cg * CPV + i] = pa[i];
+        }
+    }
+    __syncthreads();
+    if (tid < 64) {
+        float y = 0.f, pr = 0.f;
+#pragma unroll
+        for (int k = 0; k < STEPV_THREADS / 32; ++k) { y += red[0][k][tid]; pr += red[1][k][tid]; }
+        const T* v = static_cast<const T*>(p.v) + b * p.v_sb + h * p.v_sh;
+        static_cast<T*>(p.out)[(int64_t)ln * 64 + tid] = dg::from_f<T>(y);
+        rr[tid] = dg::to_f(v[tid]) - pr;
+    }
+    __syncthreads();
+    const T* decay = static_cast<const T*>(p.decay);
+    const float al = p.dynamic_decay ? dg::to_f(decay[b * p.decay_sb + h * p.decay_sh]) : dg::to_f(decay[h]);
+    const float bt = dg::to_f(static_cast<const T*>(p.beta)[b * p.beta_sb + h * p.beta_sh]);
+    float r[CPV];
+#pragma unroll
+    for (int i = 0; i < CPV; ++i) r[i] = rr[cg * CPV + i];
+#pragma unroll
+    for (int w = 0; w < NV; ++w) {
+        const int64_t off = ((int64_t)(w * RPW + rsub) * 64 + cg * CPV) * sizeof(T);
+        const uint4 sv = *reinterpret_cast<const uint4*>(st_smem + off);
+        const float c = bt * dg::to_f(wk[w * RPW + rsub]);
+        const T* e = reinterpret_cast<const T*>(&sv);
+        uint4 o;
+        T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int i = 0; i < CPV; ++i) oe[i] = dg::from_f<T>(fmaf(al, dg::to_f(e[i]), c * r[i]));
+        dg::st16(sn + off, o);
+    }
+}
+
+template <typename T, int NV>
+int launch_step_staged(const DenseStepParams& p, cudaStream_t s) {
+    const int smem = p.S * 64 * (int)sizeof(T);
+    auto kern = dense_step_staged_kernel<T, NV>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return dg_host::record_cuda_error(e);
+    }
+    kern<<<p.B * p.H, STEPV_THREADS, smem, s>>>(p);
+    return dg_host::check_launch();
+}
+
 template <typename T, int NV>
 int launch_step_vec(const DenseStepParams& p, cudaStream_t s) {
     dense_step_vec_kernel<T, NV><<<p.B * p.H, STEPV_THREADS, 0, s>>>(p);
@@ -375,6 +478,16 @@ int dispatch_step(const DenseStepParams& p, cudaStream_t s) {
         const int64_t lane_bytes = (int64_t)p.S * 64 * sizeof(T);
         const bool al = ((uintptr_t)p.s_prev & 15) == 0 && ((uintptr_t)p.s_next & 15) == 0;
         if (al && lane_bytes % (STEPV_THREADS * 16) == 0) {
+            // 16-bit state up to 32 KB a lane: staged through shared memory (5 lanes per SM)
+            if constexpr (sizeof(T) == 2) {
+                switch (lane_bytes / (STEPV_THREADS * 16)) {
+                case 1: return launch_step_staged<T, 1>(p, s);
+                case 2: return launch_step_staged<T, 2>(p, s);
+                case 4: return launch_step_staged<T, 4>(p, s);
+                case 8: return launch_step_staged<T, 8>(p, s);
+                default: break;
+                }
+            }
             switch (lane_bytes / (STEPV_THREADS * 16)) {
             case 1: return launch_step_vec<T, 1>(p, s);
             case 2: return launch_step_vec<T, 2>(p, s);
