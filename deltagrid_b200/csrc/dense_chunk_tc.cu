@@ -73,29 +73,45 @@ struct Layout {
     static constexpr uint32_t TMEM_COLS = 512;
 };
 
-constexpr uint32_t IDESC_KK = tc::make_idesc(128, 64, 0, 0, 0);
-constexpr uint32_t IDESC_KM = tc::make_idesc(128, 64, 0, 0, 1);
-constexpr uint32_t IDESC_MM = tc::make_idesc(128, 64, 0, 1, 1);
+// Operand types.  The products with an input operand (the Gram [K;Q] K^T, [K;Q] S0 and the
+// update K^T R') take the input type TI (fp16 or bf16: both operands of one kind::f16 MMA
+// share a type), so the S0 and R' copies are written in TI.  T X and Mqk (R beta) have
+// only operands formed here and stay fp16 for both input types.
+template <typename TI> struct Io;
+template <> struct Io<__half> {
+    static constexpr int kBf16 = 0;
+    __device__ static uint32_t pack2(float a, float b) {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+    __device__ static float2 unpack2(uint32_t u) { return __half22float2(*reinterpret_cast<__half2*>(&u)); }
+};
+template <> struct Io<__nv_bfloat16> {
+    static constexpr int kBf16 = 1;
+    __device__ static uint32_t pack2(float a, float b) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+    __device__ static float2 unpack2(uint32_t u) { return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u)); }
+};
+template <typename TI> constexpr uint32_t idesc_kk() { return tc::make_idesc(128, 64, Io<TI>::kBf16, 0, 0); }
+template <typename TI> constexpr uint32_t idesc_km() { return tc::make_idesc(128, 64, Io<TI>::kBf16, 0, 1); }
+template <typename TI> constexpr uint32_t idesc_mm() { return tc::make_idesc(128, 64, Io<TI>::kBf16, 1, 1); }
+constexpr uint32_t IDESC_KM16 = tc::make_idesc(128, 64, 0, 0, 1);     // T X and Mqk (R beta), fp16
 constexpr int LDT = 68;                 // fp32 row stride of the L/T scratch
 constexpr uint32_t BAR_WG0 = 1, BAR_WG1 = 2;   // named barrier ids (0 is __syncthreads)
 
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-    __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-}
-__device__ __forceinline__ float2 unpack_h2(uint32_t u) {
-    return __half22float2(*reinterpret_cast<__half2*>(&u));
-}
 
-// write 64 fp32 values as one 128-byte swizzled fp16 row
-__device__ __forceinline__ void st_row_f16(uint8_t* tile, int row, const float* x) {
+// write 64 fp32 values as one 128-byte swizzled row of 16-bit type TT
+template <typename TT = __half>
+__device__ __forceinline__ void st_row16(uint8_t* tile, int row, const float* x) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
         uint4 v;
-        v.x = pack_h2(x[8 * c + 0], x[8 * c + 1]);
-        v.y = pack_h2(x[8 * c + 2], x[8 * c + 3]);
-        v.z = pack_h2(x[8 * c + 4], x[8 * c + 5]);
-        v.w = pack_h2(x[8 * c + 6], x[8 * c + 7]);
+        v.x = Io<TT>::pack2(x[8 * c + 0], x[8 * c + 1]);
+        v.y = Io<TT>::pack2(x[8 * c + 2], x[8 * c + 3]);
+        v.z = Io<TT>::pack2(x[8 * c + 4], x[8 * c + 5]);
+        v.w = Io<TT>::pack2(x[8 * c + 6], x[8 * c + 7]);
         *reinterpret_cast<uint4*>(tile + tc::sw128(row, c)) = v;
     }
 }
@@ -122,16 +138,17 @@ struct ChunkScalars {
     float atot;         // a_{C-1}
 };
 
-__device__ __forceinline__ ChunkScalars chunk_scalars(const __half* beta, const __half* decay, int dyn,
+template <typename TI>
+__device__ __forceinline__ ChunkScalars chunk_scalars(const TI* beta, const TI* decay, int dyn,
                                                       float alpha_static, int64_t lane_base, int t0, int T_,
                                                       int lane) {
     ChunkScalars c;
     const int t = t0 + 2 * lane;
     const bool ok0 = t < T_, ok1 = t + 1 < T_;
-    const float al0 = ok0 ? (dyn ? __half2float(decay[lane_base + t]) : alpha_static) : 1.f;
-    const float al1 = ok1 ? (dyn ? __half2float(decay[lane_base + t + 1]) : alpha_static) : 1.f;
-    c.b0 = ok0 ? __half2float(beta[lane_base + t]) : 0.f;
-    c.b1 = ok1 ? __half2float(beta[lane_base + t + 1]) : 0.f;
+    const float al0 = ok0 ? (dyn ? dg::to_f(decay[lane_base + t]) : alpha_static) : 1.f;
+    const float al1 = ok1 ? (dyn ? dg::to_f(decay[lane_base + t + 1]) : alpha_static) : 1.f;
+    c.b0 = ok0 ? dg::to_f(beta[lane_base + t]) : 0.f;
+    c.b1 = ok1 ? dg::to_f(beta[lane_base + t + 1]) : 0.f;
     float incl = al0 * al1;              // inclusive scan of pair products over lanes
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -257,7 +274,7 @@ __device__ void invert_unit_lower(float* lt, int t) {
     }
 }
 
-template <int S>
+template <int S, typename TI>
 __global__ void __launch_bounds__(256, 1)
     dense_chunk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmq,
                        const __grid_constant__ CUtensorMap tmv, ChunkParams p) {
@@ -290,8 +307,8 @@ __global__ void __launch_bounds__(256, 1)
     const int h = lane_bh % p.H;
     const int T_ = p.T, NC = p.nchunks;
     const int64_t lane_base = (int64_t)lane_bh * T_;
-    const __half* beta = static_cast<const __half*>(p.beta);
-    const __half* decay = static_cast<const __half*>(p.decay);
+    const TI* beta = static_cast<const TI*>(p.beta);
+    const TI* decay = static_cast<const TI*>(p.decay);
 
     if (warp == 0) tc::tmem_alloc(tmem_holder, Ly::TMEM_COLS);
     if (tid == 0) {
@@ -308,13 +325,13 @@ __global__ void __launch_bounds__(256, 1)
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_holder;
     const uint32_t tq = tmem + ((uint32_t)(32 * q4) << 16);
-    const float alpha_static = p.dynamic_decay ? 1.f : __half2float(decay[h]);
+    const float alpha_static = p.dynamic_decay ? 1.f : dg::to_f(decay[h]);
 
     bool failed = false;
     if (warp < 4) {
         // ================= WG0: state path; thread 0 issues TMA and MMAs =================
         {   // initial state -> TMEM (thread = slot row 128 b + 32 warp + lane)
-            const __half* s_init = static_cast<const __half*>(p.s_init);
+            const TI* s_init = static_cast<const TI*>(p.s_init);
             for (int b = 0; b < NB; ++b) {
                 const int slot = 128 * b + 32 * warp + lane;
                 uint32_t r0[32], r1[32];
@@ -326,7 +343,7 @@ __global__ void __launch_bounds__(256, 1)
                         const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            const float2 f = unpack_h2(w4[e]);
+                            const float2 f = Io<TI>::unpack2(w4[e]);
                             const int col = 8 * c + 2 * e;
                             uint32_t* dst = col < 32 ? r0 : r1;
                             dst[col & 31] = __float_as_uint(f.x);
@@ -370,7 +387,7 @@ __global__ void __launch_bounds__(256, 1)
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint32_t base = tc::smem_u32(kq + s * SLICE) + 32 * kk;
                         tc::mma_f16(tmem + Ly::ACC1, tc::make_desc(base, 16, 1024), tc::make_desc(base, 16, 1024),
-                                    IDESC_KK, (s | kk) != 0);
+                                    idesc_kk<TI>(), (s | kk) != 0);
                     }
                 tc::mma_commit(bar_acc1);
                 if (c + 1 < NC) {          // warm L2 with the next chunk's K and V
@@ -378,7 +395,7 @@ __global__ void __launch_bounds__(256, 1)
                     tc::tma_prefetch_3d(&tmv, 0, t0 + CH, lane_bh);
                 }
             }
-            // [K;Q] S0 over 128-slot blocks; S0 streamed TMEM -> fp16 smem (and scaled by atot in TMEM)
+            // [K;Q] S0 over 128-slot blocks; S0 streamed TMEM -> smem in the input type (and scaled by atot in TMEM)
             for (int b = 0; b < NB; ++b) {
                 const int buf = b & 1;
                 bad = false;
@@ -386,7 +403,7 @@ __global__ void __launch_bounds__(256, 1)
                 tc::tc_fence_after();
                 float x[64];
                 ld_row64(tq + 64 * b, x);
-                st_row_f16(s0b + buf * 16384, 32 * warp + lane, x);
+                st_row16<TI>(s0b + buf * 16384, 32 * warp + lane, x);
                 if (cs.atot != 1.f) {
                     uint32_t r0[32], r1[32];
 #pragma unroll
@@ -410,7 +427,7 @@ __global__ void __launch_bounds__(256, 1)
                             const uint32_t a = tc::smem_u32(kq + (2 * b + sl) * SLICE) + 32 * kk;
                             const uint32_t bb = tc::smem_u32(s0b + buf * 16384) + (sl * 4 + kk) * 2048;
                             tc::mma_f16(tmem + Ly::ACC2, tc::make_desc(a, 16, 1024), tc::make_desc(bb, 16384, 1024),
-                                        IDESC_KM, (b | sl | kk) != 0);
+                                        idesc_km<TI>(), (b | sl | kk) != 0);
                         }
                     tc::mma_commit(bar_s0 + buf);
                     if (b == NB - 1) tc::mma_commit(bar_acc2);
@@ -435,12 +452,12 @@ __global__ void __launch_bounds__(256, 1)
                     const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const float2 f = unpack_h2(w4[e]);
+                        const float2 f = Io<TI>::unpack2(w4[e]);
                         d1[8 * cc + 2 * e] = f.x - ap_row * d1[8 * cc + 2 * e];
                         d1[8 * cc + 2 * e + 1] = f.y - ap_row * d1[8 * cc + 2 * e + 1];
                     }
                 }
-                st_row_f16(xr, row, d1);
+                st_row16(xr, row, d1);
             }
             tc::fence_proxy_async();
             bad = bad || !tc::mbar_wait(bar_t, par);      // T and Mqk of this chunk ready
@@ -450,7 +467,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
                     tc::mma_f16(tmem + Ly::ACC3, tc::make_desc(tc::smem_u32(tzm) + 32 * kk, 16, 1024),
-                                tc::make_desc(tc::smem_u32(xr) + kk * 2048, 16384, 1024), IDESC_KM, kk != 0);
+                                tc::make_desc(tc::smem_u32(xr) + kk * 2048, 16384, 1024), IDESC_KM16, kk != 0);
                 tc::mma_commit(bar_acc3);
             }
             bad = !tc::mbar_wait(bar_acc3, par);
@@ -470,8 +487,8 @@ __global__ void __launch_bounds__(256, 1)
                     rb[j] = b_row * r[j];
                     r[j] = ae_row * rb[j];
                 }
-                st_row_f16(vr, row, rb);     // R * beta (V is dead)
-                st_row_f16(xr, row, r);      // R' = a_end * beta * R (X is dead)
+                st_row16(vr, row, rb);       // R * beta (V is dead), fp16
+                st_row16<TI>(xr, row, r);    // R' = a_end * beta * R (X is dead), input type
             }
             tc::fence_proxy_async();
             tc::tc_fence_before();
@@ -481,14 +498,14 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
                     tc::mma_f16(tmem + Ly::ACC4, tc::make_desc(tc::smem_u32(tzm + 8192) + 32 * kk, 16, 1024),
-                                tc::make_desc(tc::smem_u32(vr) + kk * 2048, 16384, 1024), IDESC_KM, kk != 0);
+                                tc::make_desc(tc::smem_u32(vr) + kk * 2048, 16384, 1024), IDESC_KM16, kk != 0);
                 tc::mma_commit(bar_acc4);
                 for (int b = 0; b < NB; ++b)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         tc::mma_f16(tmem + 64 * b,
                                     tc::make_desc(tc::smem_u32(kq + 2 * b * SLICE) + kk * 2048, SLICE, 1024),
-                                    tc::make_desc(tc::smem_u32(xr) + kk * 2048, 16384, 1024), IDESC_MM, 1u);
+                                    tc::make_desc(tc::smem_u32(xr) + kk * 2048, 16384, 1024), idesc_mm<TI>(), 1u);
                 tc::mma_commit(bar_upd);
             }
             // Y = aprev o (Q S0) + Mqk R  (warps 2-3)
@@ -500,14 +517,14 @@ __global__ void __launch_bounds__(256, 1)
                 ld_row64(tq + Ly::ACC4, m);
                 const int t = t0 + row;
                 if (t < T_) {
-                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + (lane_base + t) * DH);
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<TI*>(p.out) + (lane_base + t) * DH);
 #pragma unroll
                     for (int cc = 0; cc < 8; ++cc) {
                         float o[8];
 #pragma unroll
                         for (int e = 0; e < 8; ++e) o[e] = fmaf(ap_row, y[8 * cc + e], m[8 * cc + e]);
-                        dst[cc] = make_uint4(pack_h2(o[0], o[1]), pack_h2(o[2], o[3]), pack_h2(o[4], o[5]),
-                                             pack_h2(o[6], o[7]));
+                        dst[cc] = make_uint4(Io<TI>::pack2(o[0], o[1]), Io<TI>::pack2(o[2], o[3]),
+                                             Io<TI>::pack2(o[4], o[5]), Io<TI>::pack2(o[6], o[7]));
                     }
                 }
             }
@@ -522,7 +539,7 @@ __global__ void __launch_bounds__(256, 1)
             if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
         }
         if (!failed) {
-            __half* s_fin = static_cast<__half*>(p.s_final);
+            TI* s_fin = static_cast<TI*>(p.s_final);
             for (int b = 0; b < NB; ++b) {
                 const int slot = 128 * b + 32 * warp + lane;
                 float x[64];
@@ -531,8 +548,9 @@ __global__ void __launch_bounds__(256, 1)
                 uint4* dst = reinterpret_cast<uint4*>(s_fin + o);
 #pragma unroll
                 for (int cc = 0; cc < 8; ++cc)
-                    dst[cc] = make_uint4(pack_h2(x[8 * cc], x[8 * cc + 1]), pack_h2(x[8 * cc + 2], x[8 * cc + 3]),
-                                         pack_h2(x[8 * cc + 4], x[8 * cc + 5]), pack_h2(x[8 * cc + 6], x[8 * cc + 7]));
+                    dst[cc] = make_uint4(Io<TI>::pack2(x[8 * cc], x[8 * cc + 1]), Io<TI>::pack2(x[8 * cc + 2], x[8 * cc + 3]),
+                                         Io<TI>::pack2(x[8 * cc + 4], x[8 * cc + 5]),
+                                         Io<TI>::pack2(x[8 * cc + 6], x[8 * cc + 7]));
                 if (p.s_final_f) {
                     float4* df = reinterpret_cast<float4*>(p.s_final_f + o);
 #pragma unroll
@@ -576,7 +594,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
                 for (int q = 0; q < 16; ++q) dst[q] = make_float4(g[4 * q], g[4 * q + 1], g[4 * q + 2], g[4 * q + 3]);
             } else {                // Mqk_ij = aprev_i / a_j (q_i . k_j), j < i
-                st_row_f16(tzm + 16384, row, g);
+                st_row16(tzm + 16384, row, g);
             }
             tc::group_sync(BAR_WG1);
             invert_unit_lower(lt, t1);
@@ -588,7 +606,7 @@ __global__ void __launch_bounds__(256, 1)
                     const float4 v = src[q];
                     tr[4 * q] = v.x; tr[4 * q + 1] = v.y; tr[4 * q + 2] = v.z; tr[4 * q + 3] = v.w;
                 }
-                st_row_f16(tzm, t1, tr);
+                st_row16(tzm, t1, tr);
             }
             tc::fence_proxy_async();
             tc::group_sync(BAR_WG1);
@@ -626,35 +644,51 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 3-D map over [lanes][T][cols] fp16 with a 64 x 64 box and 128B swizzle
-bool make_map(CUtensorMap* m, const void* base, int cols, int T, int lanes) {
+// 3-D map over [lanes][T][cols] 16-bit elements with a 64 x 64 box and 128B swizzle
+bool make_map(CUtensorMap* m, const void* base, int cols, int T, int lanes, bool bf16) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)T, (cuuint64_t)lanes};
     cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)cols * 2 * (cuuint64_t)T};
     cuuint32_t box[3] = {64, 64, 1};
     cuuint32_t estr[3] = {1, 1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+    return fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+              const_cast<void*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int S>
+template <int S, typename TI>
 int launch_chunk(const void* v, const void* beta, const void* wk, const void* wq, const void* decay,
                  int dynamic_decay, const void* s_init, void* out, void* s_final, float* err_out,
                  float* s_final_f, int B, int H, int T, int32_t* status, cudaStream_t stream) {
     const int lanes = B * H;
     CUtensorMap mk, mq, mv;
-    if (!make_map(&mk, wk, S, T, lanes) || !make_map(&mq, wq, S, T, lanes) || !make_map(&mv, v, DH, T, lanes))
+    const bool bf = Io<TI>::kBf16 != 0;
+    if (!make_map(&mk, wk, S, T, lanes, bf) || !make_map(&mq, wq, S, T, lanes, bf) ||
+        !make_map(&mv, v, DH, T, lanes, bf))
         return DG_ERR_UNSUPPORTED;
     ChunkParams p{beta, decay, s_init, out, s_final, err_out, s_final_f, status,
                   H, T, (T + CH - 1) / CH, dynamic_decay};
     const size_t smem = Layout<S>::BYTES + 1024;
-    auto kern = dense_chunk_kernel<S>;
+    auto kern = dense_chunk_kernel<S, TI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return dg_host::record_cuda_error(e);
     kern<<<lanes, 256, smem, stream>>>(mk, mq, mv, p);
     return dg_host::check_launch();
+}
+
+template <typename TI>
+int launch_by_slots(int S, const void* v, const void* beta, const void* wk, const void* wq, const void* decay,
+                    int dynamic_decay, const void* s_init, void* out, void* s_final, float* err_out, float* s_final_f,
+                    int B, int H, int T, int32_t* status, cudaStream_t stream) {
+    switch (S) {
+    case 128: return launch_chunk<128, TI>(v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f, B, H, T, status, stream);
+    case 256: return launch_chunk<256, TI>(v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f, B, H, T, status, stream);
+    case 384: return launch_chunk<384, TI>(v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f, B, H, T, status, stream);
+    case 512: return launch_chunk<512, TI>(v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f, B, H, T, status, stream);
+    default: return DG_ERR_UNSUPPORTED;
+    }
 }
 
 }  // namespace
@@ -663,7 +697,8 @@ namespace dg_host {
 
 bool dense_chunked_tc_supports(int dtype, int B, int H, int T, int S, int Dh) {
     (void)B; (void)H;
-    return dtype == DG_DTYPE_F16 && Dh == DH && T > 0 && (S == 128 || S == 256 || S == 384 || S == 512);
+    return (dtype == DG_DTYPE_F16 || dtype == DG_DTYPE_BF16) && Dh == DH && T > 0 &&
+           (S == 128 || S == 256 || S == 384 || S == 512);
 }
 
 int dense_forward_chunked_tc(int dtype, int B, int H, int T, int S, int Dh, const void* v, const void* beta,
@@ -676,13 +711,11 @@ int dense_forward_chunked_tc(int dtype, int B, int H, int T, int S, int Dh, cons
                           (uintptr_t)(s_final_f ? (void*)s_final_f : s_final);
     if (mis & 15) return DG_ERR_MISALIGNED;
     int32_t* status = nullptr;
-    switch (S) {
-    case 128: return launch_chunk<128>(v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f, B, H, T, status, stream);
-    case 256: return launch_chunk<256>(v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f, B, H, T, status, stream);
-    case 384: return launch_chunk<384>(v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f, B, H, T, status, stream);
-    case 512: return launch_chunk<512>(v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f, B, H, T, status, stream);
-    default: return DG_ERR_UNSUPPORTED;
-    }
+    if (dtype == DG_DTYPE_BF16) return launch_by_slots<__nv_bfloat16>(S, v, beta, wk, wq, decay, dynamic_decay, s_init,
+                                                                     out, s_final, err_out, s_final_f, B, H, T, status,
+                                                                     stream);
+    return launch_by_slots<__half>(S, v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f,
+                                   B, H, T, status, stream);
 }
 
 }  // namespace dg_host

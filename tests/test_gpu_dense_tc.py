@@ -1,9 +1,11 @@
 """Chunkwise tensor-core dense forward (tcgen05, algo 2) against the CPU oracle.
 
-The oracle runs the per-step recurrence with an fp32 state on the fp16-quantised
+The oracle runs the per-step recurrence with an fp32 state on the storage-quantised
 inputs (delta_kernel.cu:64-121 semantics).  The chunked kernel evaluates the
-same recurrence 64 steps at a time with fp16 MMA operands and fp32
-accumulation; bar: max|a-b|/max|b| <= 1e-3 for y and for the final state.
+same recurrence 64 steps at a time with 16-bit MMA operands and fp32
+accumulation; bar: max|a-b|/max|b| <= 1e-3 for y and for the final state with
+fp16 storage, 8e-3 with bf16 storage (one bf16 ulp is 2^-8 relative; the products
+with an input operand then take bf16 copies of the state and of R').
 """
 import pytest
 import torch
@@ -21,13 +23,13 @@ if torch.cuda.is_available():
 TC = 2
 
 
-def _both(d, save=False):
+def _both(d, save=False, storage=O.F16):
     g = {n: (t.cuda() if t is not None else None) for n, t in d.items()}
     r = ext.forward(g["q"], g["k"], g["v"], g["beta"], g["wk"], g["wq"], g["decay"], g["s_init"], save, algo=TC)
     s0 = to_np32(d["s_init"]) if d["s_init"] is not None else None
     yo, so, eo = O.dense_forward(to_np32(d["v"]), to_np32(d["beta"]), to_np32(d["wk"]), to_np32(d["wq"]),
                                  to_np32(d["decay"]), s0, want_err=True)
-    return r, (O.round_to(yo, O.F16), so, eo)
+    return r, (O.round_to(yo, storage), so, eo)
 
 
 @pytest.mark.parametrize("S", [128, 256, 384, 512])
@@ -85,3 +87,35 @@ def test_auto_selects_tc_for_fp16_dh64():
     assert torch.equal(o_auto, o_tc)
     with pytest.raises(RuntimeError, match="unsupported"):
         ext.forward(*(t.float() for t in a), algo=TC)
+
+
+BF16_TOL = 8e-3
+
+
+@pytest.mark.parametrize("S,T,dyn,s_init", [(128, 200, False, False), (256, 1000, True, True),
+                                            (512, 333, True, False), (384, 64, False, True)])
+def test_tc_bf16_against_oracle(S, T, dyn, s_init):
+    d = dense_inputs(2, 3, T, S, 64, torch.bfloat16, dynamic=dyn, seed=S + T, s_init=s_init)
+    (out, s, err, sf), (yo, so, eo) = _both(d, save=True, storage=O.BF16)
+    assert out.dtype == torch.bfloat16
+    assert rel_err(out.float().cpu().numpy(), yo) < BF16_TOL
+    assert rel_err(s.float().cpu().numpy(), O.round_to(so, O.BF16)) < BF16_TOL
+    assert rel_err(sf.cpu().numpy(), so) < BF16_TOL
+
+
+def test_tc_bf16_cfg2_geometry_full_length():
+    d = dense_inputs(1, 4, 4096, 512, 64, torch.bfloat16, seed=12)
+    (out, s, _, _), (yo, so, _) = _both(d, storage=O.BF16)
+    assert rel_err(out.float().cpu().numpy(), yo) < BF16_TOL
+    assert rel_err(s.float().cpu().numpy(), O.round_to(so, O.BF16)) < BF16_TOL
+
+
+def test_auto_selects_tc_for_bf16_dh64():
+    d = dense_inputs(2, 2, 128, 256, 64, torch.bfloat16, seed=2)
+    g = {n: (t.cuda() if t is not None else None) for n, t in d.items()}
+    a = (g["q"], g["k"], g["v"], g["beta"], g["wk"], g["wq"], g["decay"])
+    o_auto, _, _, _ = ext.forward(*a)
+    o_tc, _, _, _ = ext.forward(*a, algo=TC)
+    o_seq, _, _, _ = ext.forward(*a, algo=_lib.ALGO_SEQUENTIAL)
+    assert torch.equal(o_auto, o_tc)
+    assert rel_err(o_tc.float().cpu().numpy(), o_seq.float().cpu().numpy()) < BF16_TOL

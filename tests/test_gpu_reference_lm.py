@@ -4,8 +4,8 @@ CUDA extension (built from its sources into oracle/_ref) and on this repository'
 drop-in (deltagrid_b200.hsru_delta_cuda).  Everything but the recurrence is the
 reference's torch code, so the two runs differ only in the kernels.
 
-Checked: prefill logits and memory states (dense forward), greedy decode logits
-(dense step), and, in fp32, every parameter gradient of a language-modelling loss
+Checked: prefill logits and memory states (dense forward), decode logits (dense
+step; both runs decode the reference run's greedy tokens), and, in fp32, every parameter gradient of a language-modelling loss
 (dense forward with save_for_backward plus the analytic backward, through the
 reference's _DeltaGridAutogradFunction).  Bars, max|a-b|/max|b|: 1e-4 in fp32; in
 fp16 / bf16 5e-3 / 2e-2 (the two kernel sets round the same fp32 sums in a
@@ -43,20 +43,29 @@ def _model(dtype, slots=128, dynamic=True, seed=0):
     return m.cuda().to(dtype).eval()
 
 
-def _prefill_and_decode(model, ids, steps, backend):
+def _prefill_and_decode(model, ids, steps, backend, tokens=None):
+    """Prefill, then `steps` decode steps.  Without `tokens` the decode is greedy and the
+    chosen tokens are returned; with `tokens` (a greedy run's choices) those are fed, so
+    that two backends decode the same sequence: a near-tied argmax may otherwise pick a
+    different token on one backend and every later logit then differs."""
     use_backend(backend)
+    chosen = []
     with torch.no_grad():
         out = model(ids, return_state=True)
         logits, states = out.logits, out.state
-        tok = logits[:, -1].argmax(-1, keepdim=True)
+        tok = logits[:, -1].argmax(-1, keepdim=True) if tokens is None else tokens[0]
         dec = []
         for i in range(steps):
+            chosen.append(tok)
             lg, states = model.step(tok, states=states, seq_offset=ids.shape[1] + i)
             dec.append(lg)
-            tok = lg[:, -1].argmax(-1, keepdim=True)
+            if tokens is None:
+                tok = lg[:, -1].argmax(-1, keepdim=True)
+            elif i + 1 < steps:
+                tok = tokens[i + 1]
     torch.cuda.synchronize()
     mem = [s for s in _state_tensors(states)]
-    return logits, torch.cat(dec, 1), mem
+    return logits, torch.cat(dec, 1), mem, chosen
 
 
 def _state_tensors(states):
@@ -70,8 +79,8 @@ def _state_tensors(states):
 def test_reference_lm_prefill_and_decode(dtype, slots, dynamic):
     model = _model(dtype, slots, dynamic)
     ids = torch.randint(0, 1000, (4, 96), generator=torch.Generator().manual_seed(1)).cuda()
-    lr, dr, mr = _prefill_and_decode(model, ids, 6, REF_EXT)
-    lo, do, mo = _prefill_and_decode(model, ids, 6, ours)
+    lr, dr, mr, toks = _prefill_and_decode(model, ids, 6, REF_EXT)
+    lo, do, mo, _ = _prefill_and_decode(model, ids, 6, ours, tokens=toks)
     tol = TOL[dtype]
     assert rel_err(_np(lo), _np(lr)) < tol
     assert rel_err(_np(do), _np(dr)) < tol
