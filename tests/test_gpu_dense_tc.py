@@ -93,7 +93,8 @@ BF16_TOL = 8e-3
 
 
 @pytest.mark.parametrize("S,T,dyn,s_init", [(128, 200, False, False), (256, 1000, True, True),
-                                            (512, 333, True, False), (384, 64, False, True)])
+                                            (512, 333, True, False), (384, 64, False, True),
+                                            (256, 1, True, True), (512, 65, False, True)])
 def test_tc_bf16_against_oracle(S, T, dyn, s_init):
     d = dense_inputs(2, 3, T, S, 64, torch.bfloat16, dynamic=dyn, seed=S + T, s_init=s_init)
     (out, s, err, sf), (yo, so, eo) = _both(d, save=True, storage=O.BF16)
