@@ -44,6 +44,11 @@ WORKLOADS = {
     # batch through the recurrence of all 12 layers (12 dense decode steps), states resident
     "cfg5": dict(kind="decode", B=256, H=12, T=1, S=256, Dh=64, L=12, dtype="bfloat16",
                  desc="LM decode recurrence: 12 layers x dense step, B=256 H=12 slots=256 Dh=64 bf16"),
+    # the same LM's prefill: 2048 tokens of the 256-sequence batch through the recurrence of
+    # all 12 layers (12 dense forwards; one layer's inputs serve every layer, the kernel's
+    # work does not depend on the values)
+    "cfg5p": dict(kind="dense", B=256, H=12, T=2048, S=256, Dh=64, L=12, dtype="bfloat16",
+                  desc="LM prefill recurrence: 12 layers x dense forward, B=256 H=12 T=2048 slots=256 Dh=64 bf16"),
 }
 METRIC = "recurrence tokens/sec"
 UNIT = "tokens/s"
@@ -64,9 +69,9 @@ def _algorithmic(w):
     e = 4 if w["dtype"] == "float32" else 2
     ht = B * H * T
     if w["kind"] == "dense":
-        S = w["S"]
+        S, L = w["S"], w.get("L", 1)
         per_ht = (2 * Dh + 2 * S) * e + e              # v, y, wk, wq, beta
-        return ht * per_ht + B * H * S * Dh * e, ht * 6.0 * S * Dh
+        return L * (ht * per_ht + B * H * S * Dh * e), L * ht * 6.0 * S * Dh
     if w["kind"] == "decode":
         S, L = w["S"], w["L"]
         per_lane = 2 * S * Dh * e + 2 * S * e + 2 * Dh * e + 2 * e    # state in+out, wk, wq, v, y, beta, decay
@@ -194,7 +199,7 @@ def launches_per_step(w):
     per layer (dense_step_vec_kernel)."""
     if w["kind"] == "decode":
         return w["L"]
-    return 2 if w["kind"] == "pkm" and w["dtype"] != "float32" else 1
+    return 2 if w["kind"] == "pkm" and w["dtype"] != "float32" else w.get("L", 1)
 
 
 def run_step(ext, w, d, algo=0):
@@ -207,9 +212,10 @@ def run_step(ext, w, d, algo=0):
             ys.append(y)
         return [ys[-1]]
     if w["kind"] == "dense":
-        if algo:
-            return ext.forward(d["q"], d["k"], d["v"], d["beta"], d["wk"], d["wq"], d["decay"], algo=algo)
-        return ext.forward(d["q"], d["k"], d["v"], d["beta"], d["wk"], d["wq"], d["decay"])
+        kw = dict(algo=algo) if algo else {}
+        for _ in range(w.get("L", 1) - 1):         # the LM prefill: every layer's recurrence
+            ext.forward(d["q"], d["k"], d["v"], d["beta"], d["wk"], d["wq"], d["decay"], **kw)
+        return ext.forward(d["q"], d["k"], d["v"], d["beta"], d["wk"], d["wq"], d["decay"], **kw)
     if algo:
         return ext.pkm_forward_algo(d["v"], d["beta"], d["wk"], d["wq"], d["idx"], d["decay"], d["state"], False, algo)
     return ext.pkm_forward(d["v"], d["beta"], d["wk"], d["wq"], d["idx"], d["decay"], d["state"])
@@ -241,7 +247,7 @@ def cpu_baseline_port(w, threads):
                 break
         dt = time.perf_counter() - t0
         tok = reps * Bs * T
-        if w["kind"] == "decode":             # a token of the LM passes the recurrence of L layers
+        if "L" in w:                          # a token of the LM passes the recurrence of L layers
             return dict(value=tok / dt / w["L"], unit=UNIT, cores=threads, kind="port",
                         sample=f"oracle dense_forward, {Bs}x{H} lanes x T={T}, slots={S}, fp32, x{reps}, "
                                f"divided by {w['L']} layers")
