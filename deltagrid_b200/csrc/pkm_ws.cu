@@ -146,7 +146,7 @@ __device__ __forceinline__ uint32_t slot_home(uint32_t x) {
 // the bucket starts), then every row scans its bucket for the latest earlier step
 // with the same slot.  Exact: there is no capacity limit to overflow.
 template <int A>
-__global__ void __launch_bounds__(HZ_THREADS) pkm_hazard_kernel(const int64_t* __restrict__ idx, int16_t* codes,
+__global__ void __launch_bounds__(HZ_THREADS, 3) pkm_hazard_kernel(const int64_t* __restrict__ idx, int16_t* codes,
                                                                 int32_t* status, int T, int64_t total, int D) {
     extern __shared__ __align__(16) uint8_t hz_smem[];
     uint32_t* cnt = reinterpret_cast<uint32_t*>(hz_smem);                 // [HZ_BUCKETS] entries per bucket
