@@ -158,6 +158,7 @@ def make_inputs(w, torch, device, seed=0):
         q = torch.randn(B, H, T, Dh, device=device, generator=g)
         v = torch.randn(B, H, T, Dh, device=device, generator=g).to(dt)
         beta = torch.sigmoid(torch.randn(B, H, T, device=device, generator=g)).to(dt)
+        P = None
         if S == Dh:
             wk, wq = k.to(dt), q.to(dt)
         else:
@@ -167,9 +168,11 @@ def make_inputs(w, torch, device, seed=0):
             P = P.to(device)
             wk = F.normalize(k @ P.T, dim=-1).to(dt)
             wq = (q @ P.T).to(dt)
-        del k, q
+            P = P.to(dt)
         decay = torch.ones(H, device=device, dtype=dt)
-        return dict(q=v, k=v, v=v, beta=beta, wk=wk, wq=wq, decay=decay)
+        # kr, qr, P: the config's own inputs (keys, queries, slot projection) for the
+        # end-to-end leg, which routes them on the device (dense_fused_forward)
+        return dict(q=v, k=v, v=v, beta=beta, wk=wk, wq=wq, decay=decay, kr=k.to(dt), qr=q.to(dt), P=P)
     G, K = w["G"], w["K"]
     total = G * G
     # routing as the layer does it (memory.py:240-289), on the GPU: two router axes of
@@ -446,7 +449,10 @@ def main():
         e2e = {"value": tokens_per_step / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "steps": k2}
     elif not args.no_e2e:
-        names = [n for n in ("v", "beta", "wk", "wq", "idx") if n in d]
+        # dense: the config's inputs k, q, v, beta cross PCIe and the slot routing runs on the
+        # device (dense_fused_forward); PKM: the routed inputs of the reference boundary
+        names = ("kr", "qr", "v", "beta") if w["kind"] == "dense" else [n for n in ("v", "beta", "wk", "wq", "idx")
+                                                                         if n in d]
         host = {n: d[n].to("cpu").pin_memory() for n in names}
         h2d = sum(t.numel() * t.element_size() for t in host.values())
         dev_in = {n: torch.empty_like(d[n]) for n in names}
@@ -462,8 +468,11 @@ def main():
             dd = dict(d)
             dd.update(dev_in)
             if w["kind"] == "dense":
-                dd["q"] = dd["k"] = dd["v"]
-            o = run_step(ext, w, dd, args.algo)
+                for _ in range(w.get("L", 1)):
+                    o = ext.dense_fused_forward(dd["kr"], dd["qr"], dd["v"], dd["beta"], dd["P"], dd["P"], None,
+                                                dd["decay"])
+            else:
+                o = run_step(ext, w, dd, args.algo)
             for src, dst in zip(o[:n_res], res_host):
                 dst.copy_(src, non_blocking=True)
 

@@ -17,6 +17,7 @@ from __future__ import annotations
 from typing import List, Optional
 
 import torch
+import torch.nn.functional as F
 
 from . import _lib
 
@@ -83,7 +84,32 @@ def pkm_fused_forward(k: torch.Tensor, q: torch.Tensor, v: torch.Tensor, beta: t
     return [out, state_c, idx, saved]
 
 
+def dense_fused_forward(k: torch.Tensor, q: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
+                        slot_proj_k: Optional[torch.Tensor], slot_proj_q: Optional[torch.Tensor],
+                        q_scale: Optional[torch.Tensor], decay: torch.Tensor, s_init: Optional[torch.Tensor] = None,
+                        save_for_backward: bool = False) -> List[torch.Tensor]:
+    """Slot routing plus recurrence: what DeltaGridLayer.forward does in dense mode
+    between its projections and out_proj (memory.py:488-512).
+
+    k, q, v [B,H,T,Dh]; beta [B,H,T]; slot_proj_k / slot_proj_q [slots, Dh] (the
+    layer's nn.Linear weights) or None when slots == Dh; q_scale [H] or None.
+    wk = L2-normalise(k P_k^T) and wq = (q P_q^T) q_scale (memory.py:233-236,
+    :489-491), formed by library GEMMs and kept in HBM for the recurrence kernel;
+    returns forward's [out, s_final, err_out, s_final_f].
+    """
+    if (slot_proj_k is None) != (slot_proj_q is None):
+        raise RuntimeError("dense_fused_forward: give both slot projections or neither")
+    if slot_proj_k is not None:
+        wk = F.normalize(F.linear(k, slot_proj_k.to(k.dtype)), p=2, dim=-1)
+        wq = F.linear(q, slot_proj_q.to(q.dtype))
+    else:
+        wk, wq = k, q
+    if q_scale is not None:
+        wq = wq * q_scale.to(dtype=q.dtype).view(1, -1, 1, 1)
+    return forward(q, k, v, beta, wk, wq, decay, s_init, save_for_backward)
+
+
 __all__ = ["forward", "step", "pkm_step", "pkm_forward", "pkm_forward_algo", "backward", "pkm_backward",
-           "device_status", "pkm_fused_forward", "DeltaGridError"]
+           "device_status", "pkm_fused_forward", "dense_fused_forward", "DeltaGridError"]
 
 DeltaGridError = _lib.DeltaGridError
