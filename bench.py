@@ -188,12 +188,16 @@ def make_inputs(w, torch, device, seed=0):
     else:
         q = torch.randn(B, H, T, Dh, device=device, generator=g)
         beta = torch.sigmoid(torch.randn(B, H, T, device=device, generator=g)).to(dt)
-    wk, wq, idx = pkm_route(k.to(dt), q.to(dt), routers, routers, K)
+    kr = k.to(dt)
+    qr = kr if w.get("writes") else q.to(dt)
+    wk, wq, idx = pkm_route(kr, qr, routers, routers, K)
     del k, q
     v = F.normalize(torch.randn(B, H, T, Dh, device=device, generator=g), dim=-1).to(dt)
     decay = torch.ones(H, device=device, dtype=dt)
     state = torch.zeros(B, H, total, Dh, device=device, dtype=dt)
-    return dict(v=v, beta=beta, wk=wk, wq=wq, idx=idx, decay=decay, state=state)
+    # kr, qr, routers: the config's own inputs for the end-to-end leg, which routes them on
+    # the device (pkm_fused_forward)
+    return dict(v=v, beta=beta, wk=wk, wq=wq, idx=idx, decay=decay, state=state, kr=kr, qr=qr, routers=routers)
 
 
 def launches_per_step(w):
@@ -449,10 +453,10 @@ def main():
         e2e = {"value": tokens_per_step / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "steps": k2}
     elif not args.no_e2e:
-        # dense: the config's inputs k, q, v, beta cross PCIe and the slot routing runs on the
-        # device (dense_fused_forward); PKM: the routed inputs of the reference boundary
-        names = ("kr", "qr", "v", "beta") if w["kind"] == "dense" else [n for n in ("v", "beta", "wk", "wq", "idx")
-                                                                         if n in d]
+        # the config's inputs k, q, v, beta cross PCIe and the routing runs on the device:
+        # slot projections (dense_fused_forward) or the product-key router (pkm_fused_forward)
+        # (the write stream's queries are its keys: copied once)
+        names = ("kr", "v", "beta") if w.get("writes") else ("kr", "qr", "v", "beta")
         host = {n: d[n].to("cpu").pin_memory() for n in names}
         h2d = sum(t.numel() * t.element_size() for t in host.values())
         dev_in = {n: torch.empty_like(d[n]) for n in names}
@@ -472,7 +476,9 @@ def main():
                     o = ext.dense_fused_forward(dd["kr"], dd["qr"], dd["v"], dd["beta"], dd["P"], dd["P"], None,
                                                 dd["decay"])
             else:
-                o = run_step(ext, w, dd, args.algo)
+                qr = dd["kr"] if w.get("writes") else dd["qr"]
+                o = ext.pkm_fused_forward(dd["kr"], qr, dd["v"], dd["beta"], dd["routers"], dd["routers"], None,
+                                          dd["decay"], dd["state"], top_k=w["K"])
             for src, dst in zip(o[:n_res], res_host):
                 dst.copy_(src, non_blocking=True)
 
