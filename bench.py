@@ -466,21 +466,59 @@ def main():
         res_host = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs[:n_res]]
         d2h = sum(t.numel() * t.element_size() for t in res_host)
 
-        def e2e_step():
-            for n in names:
-                dev_in[n].copy_(host[n], non_blocking=True)
-            dd = dict(d)
-            dd.update(dev_in)
+        # the step in pieces of the batch (lanes are independent): the copy in of piece i+1
+        # and the copy out of piece i-1 run on their own streams while piece i computes.
+        # Only where a call spans several waves of CTAs (dense: one CTA per lane), so that a
+        # piece costs a share of the compute; a PKM call is one wave of lanes that each run
+        # the whole sequence, and pieces of it would run one after another.
+        npc = 1
+        if w["kind"] == "dense":
+            waves = -(-w["B"] * w["H"] // torch.cuda.get_device_properties(device).multi_processor_count)
+            npc = next(n for n in (4, 2, 1) if n <= waves and w["B"] % n == 0)
+        bs = w["B"] // npc
+        s_h2d, s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+
+        def compute(dd):
             if w["kind"] == "dense":
                 for _ in range(w.get("L", 1)):
                     o = ext.dense_fused_forward(dd["kr"], dd["qr"], dd["v"], dd["beta"], dd["P"], dd["P"], None,
                                                 dd["decay"])
-            else:
-                qr = dd["kr"] if w.get("writes") else dd["qr"]
-                o = ext.pkm_fused_forward(dd["kr"], qr, dd["v"], dd["beta"], dd["routers"], dd["routers"], None,
-                                          dd["decay"], dd["state"], top_k=w["K"])
-            for src, dst in zip(o[:n_res], res_host):
-                dst.copy_(src, non_blocking=True)
+                return o
+            qr = dd["kr"] if w.get("writes") else dd["qr"]
+            return ext.pkm_fused_forward(dd["kr"], qr, dd["v"], dd["beta"], dd["routers"], dd["routers"], None,
+                                         dd["decay"], dd["state"], top_k=w["K"])
+
+        def e2e_step():
+            go = torch.cuda.Event()
+            go.record(stream)
+            s_h2d.wait_event(go)
+            landed = []
+            with torch.cuda.stream(s_h2d):
+                for i in range(npc):
+                    sl = slice(i * bs, (i + 1) * bs)
+                    for n in names:
+                        dev_in[n][sl].copy_(host[n][sl], non_blocking=True)
+                    e = torch.cuda.Event()
+                    e.record(s_h2d)
+                    landed.append(e)
+            for i in range(npc):
+                sl = slice(i * bs, (i + 1) * bs)
+                stream.wait_event(landed[i])
+                dd = dict(d)
+                dd.update({n: t[sl] for n, t in dev_in.items()})
+                if "state" in d:
+                    dd["state"] = d["state"][sl]
+                o = compute(dd)
+                e = torch.cuda.Event()
+                e.record(stream)
+                s_d2h.wait_event(e)
+                with torch.cuda.stream(s_d2h):
+                    for src, dst in zip(o[:n_res], res_host):
+                        src.record_stream(s_d2h)
+                        dst[sl].copy_(src, non_blocking=True)
+            fin = torch.cuda.Event()
+            fin.record(s_d2h)
+            stream.wait_event(fin)
 
         e2e_step()
         torch.cuda.synchronize(device)
