@@ -5,7 +5,7 @@
 A step is one call of the hot path over one batch of synthetic input resident
 in HBM: the dense sequence forward ``hsru_delta_cuda.forward`` (cfg1/cfg2) or the
 PKM sequence forward ``pkm_forward`` (cfg3/cfg4).  The default workload is
-BASELINE config 2 (dense, B=32 H=16 T=4096 Dh=64 slots=512, fp16 storage,
+cfg2, the second BASELINE config (dense, B=32 H=16 T=4096 Dh=64 slots=512, fp16 storage,
 fp32 accumulation), the configuration the headline metric is quoted on.
 
 Multi-GPU (torchrun, one process per GPU): every rank runs the full per-GPU
@@ -40,7 +40,7 @@ WORKLOADS = {
                  desc="PKM fp16 B=16 H=8 T=8192 Dh=64 grid 128x128 top-8, routed keys"),
     "cfg4": dict(kind="pkm", B=8, H=8, T=16384, G=1024, K=8, Dh=64, dtype="float16", writes=True,
                  desc="PKM fp16 B=8 H=8 T=16384 Dh=64 grid 1024x1024 top-8, write stream (beta=1)"),
-    # BASELINE config 4 (the LM) at its decode shape: one step is one token of a 256-sequence
+    # the fifth BASELINE config (the LM) at its decode shape: one step is one token of a 256-sequence
     # batch through the recurrence of all 12 layers (12 dense decode steps), states resident
     "cfg5": dict(kind="decode", B=256, H=12, T=1, S=256, Dh=64, L=12, dtype="bfloat16",
                  desc="LM decode recurrence: 12 layers x dense step, B=256 H=12 slots=256 Dh=64 bf16"),

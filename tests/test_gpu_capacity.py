@@ -1,7 +1,7 @@
 """Associative recall at scale through the whole GPU path: routing (dg_pkm_route),
 the hazard pre-pass and the PKM recurrence.
 
-BASELINE config 4's stream: per lane, 100,000 writes of random unit-norm key /
+cfg4's stream (the fourth BASELINE config): per lane, 100,000 writes of random unit-norm key /
 value pairs (beta = 1, alpha = 1) into a 1024 x 1024 grid (1,048,576 slots, top-8
 per axis, 64 active slots), then 10,000 reads of uniformly chosen earlier keys
 (beta = 0, the query routed like its key); a read succeeds when cos(y, v) > 0.8.

@@ -45,7 +45,7 @@ def test_reference_loop_golden(name):
 
 
 def test_cfg1_fp32():
-    # B=4 H=4 T=512 Dh=64 slots=64, fp32, static decay 1, S0 = 0
+    # cfg1, the first BASELINE config: B=4 H=4 T=512 Dh=64 slots=64, fp32, static decay 1, S0 = 0
     d = dense_inputs(4, 4, 512, 64, 64, torch.float32, seed=0)
     out, s, _, _ = _run(d, torch.float32)
     yo, so, _, _ = _oracle(d, torch.float32)

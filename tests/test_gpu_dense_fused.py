@@ -3,7 +3,7 @@ q_scale multiply of :489-491) followed by the recurrence, from k and q.
 
 Checked: the result is exactly forward() on the wk / wq that routing forms, and it
 matches the CPU oracle run on those (storage-rounded) wk / wq within the fp16 bar
-of 1e-3, at BASELINE config 1's geometry (512 slots, Dh 64) on a few lanes.
+of 1e-3, at cfg2's geometry (512 slots, Dh 64) on a few lanes.
 """
 import numpy as np
 import pytest

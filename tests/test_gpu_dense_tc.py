@@ -60,7 +60,7 @@ def test_tc_decay_and_initial_state(dyn, static_decay):
 
 
 def test_tc_cfg2_geometry_prefix():
-    # slots 512, Dh 64, fp16, wk = normalize(k P^T), wq = q P^T;
+    # cfg2 (the second BASELINE config): slots 512, Dh 64, fp16, wk = normalize(k P^T), wq = q P^T;
     # full T = 4096 on 4 lanes so the CPU oracle stays quick
     d = dense_inputs(1, 4, 4096, 512, 64, torch.float16, seed=11)
     (out, s, _, _), (yo, so, _) = _both(d)

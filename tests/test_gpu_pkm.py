@@ -72,7 +72,7 @@ def test_heavy_row_reuse_ordering():
 
 
 def test_cfg3_shape_prefix():
-    # BASELINE config 2 geometry (128 x 128 slots, top-8, Dh 64, fp16 state) on a
+    # cfg3 geometry (128 x 128 slots, top-8, Dh 64, fp16 state) on a
     # T prefix and fewer lanes so the CPU oracle stays quick
     d = pkm_inputs(4, 4, 256, 128, 8, 64, torch.float16, seed=7)
     out, st, _ = _gpu(d)

@@ -28,7 +28,7 @@ def _c(t):
 
 @need_ref
 @pytest.mark.parametrize("dtype,B,H,T,S,Dh,dyn", [
-    (torch.float32, 4, 4, 512, 64, 64, False),
+    (torch.float32, 4, 4, 512, 64, 64, False),      # cfg1 (the first BASELINE config)
     (torch.float16, 4, 4, 256, 512, 64, False),     # config 1 geometry, fewer lanes
     (torch.float16, 2, 3, 100, 128, 64, True),
     (torch.float32, 2, 2, 64, 256, 32, True),
