@@ -488,6 +488,17 @@ int dispatch_step(const DenseStepParams& p, cudaStream_t s) {
                 default: break;
                 }
             }
+            // fp32 state up to 64 KB a lane (256 slots): staged as well, 3 lanes per SM
+            if constexpr (sizeof(T) == 4) {
+                switch (lane_bytes / (STEPV_THREADS * 16)) {
+                case 1: return launch_step_staged<T, 1>(p, s);
+                case 2: return launch_step_staged<T, 2>(p, s);
+                case 4: return launch_step_staged<T, 4>(p, s);
+                case 8: return launch_step_staged<T, 8>(p, s);
+                case 16: return launch_step_staged<T, 16>(p, s);
+                default: break;
+                }
+            }
             switch (lane_bytes / (STEPV_THREADS * 16)) {
             case 1: return launch_step_vec<T, 1>(p, s);
             case 2: return launch_step_vec<T, 2>(p, s);
