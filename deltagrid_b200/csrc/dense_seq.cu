@@ -364,16 +364,16 @@ __global__ void __launch_bounds__(STEPV_THREADS) dense_step_vec_kernel(DenseStep
 // Decode step, staged: the same thread mapping and arithmetic as dense_step_vec_kernel,
 // but the lane's state goes to shared memory through cp.async (16 bytes a copy) instead
 // of registers, so a thread keeps only its accumulators (wk and wq are re-read, from
-// L1): 5 CTAs (5 lanes, 160 KB of state for bf16 at 256 slots) are in flight per SM
-// instead of 2.  Each thread reads
-// back only the vectors it copied (cp.async.wait_all orders them for that thread).
-template <typename T, int NV>
-__global__ void __launch_bounds__(STEPV_THREADS, 5) dense_step_staged_kernel(DenseStepParams p) {
+// L1).  NT threads per lane (256 here): 5 lanes per SM for bf16 at 256 slots (160 KB
+// of state in flight instead of 2 lanes' 64 KB), 3 for fp32 (64 KB each).  Each thread
+// reads back only the vectors it copied (cp.async.wait_all orders them for that thread).
+template <typename T, int NV, int NT>
+__global__ void __launch_bounds__(NT, NT == 256 ? 5 : 6) dense_step_staged_kernel(DenseStepParams p) {
     constexpr int CPV = 16 / (int)sizeof(T);
     constexpr int NG = 64 / CPV;
-    constexpr int RPW = STEPV_THREADS / NG;
+    constexpr int RPW = NT / NG;
     extern __shared__ __align__(16) uint8_t st_smem[];               // [S][64] state of the lane
-    __shared__ float red[2][STEPV_THREADS / 32][64];
+    __shared__ float red[2][NT / 32][64];
     __shared__ float rr[64];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int cg = tid % NG, rsub = tid / NG;
@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(STEPV_THREADS, 5) dense_step_staged_kernel(Den
     if (tid < 64) {
         float y = 0.f, pr = 0.f;
 #pragma unroll
-        for (int k = 0; k < STEPV_THREADS / 32; ++k) { y += red[0][k][tid]; pr += red[1][k][tid]; }
+        for (int k = 0; k < NT / 32; ++k) { y += red[0][k][tid]; pr += red[1][k][tid]; }
         const T* v = static_cast<const T*>(p.v) + b * p.v_sb + h * p.v_sh;
         static_cast<T*>(p.out)[(int64_t)ln * 64 + tid] = dg::from_f<T>(y);
         rr[tid] = dg::to_f(v[tid]) - pr;
@@ -452,15 +452,15 @@ __global__ void __launch_bounds__(STEPV_THREADS, 5) dense_step_staged_kernel(Den
     }
 }
 
-template <typename T, int NV>
+template <typename T, int NV, int NT>
 int launch_step_staged(const DenseStepParams& p, cudaStream_t s) {
     const int smem = p.S * 64 * (int)sizeof(T);
-    auto kern = dense_step_staged_kernel<T, NV>;
+    auto kern = dense_step_staged_kernel<T, NV, NT>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return dg_host::record_cuda_error(e);
     }
-    kern<<<p.B * p.H, STEPV_THREADS, smem, s>>>(p);
+    kern<<<p.B * p.H, NT, smem, s>>>(p);
     return dg_host::check_launch();
 }
 
@@ -478,24 +478,25 @@ int dispatch_step(const DenseStepParams& p, cudaStream_t s) {
         const int64_t lane_bytes = (int64_t)p.S * 64 * sizeof(T);
         const bool al = ((uintptr_t)p.s_prev & 15) == 0 && ((uintptr_t)p.s_next & 15) == 0;
         if (al && lane_bytes % (STEPV_THREADS * 16) == 0) {
-            // 16-bit state up to 32 KB a lane: staged through shared memory (5 lanes per SM)
+            // 16-bit state up to 32 KB a lane: staged through shared memory, 5 lanes per SM
+            // (128 threads a lane, 6 lanes per SM, measured slower: each thread's loop doubles)
             if constexpr (sizeof(T) == 2) {
                 switch (lane_bytes / (STEPV_THREADS * 16)) {
-                case 1: return launch_step_staged<T, 1>(p, s);
-                case 2: return launch_step_staged<T, 2>(p, s);
-                case 4: return launch_step_staged<T, 4>(p, s);
-                case 8: return launch_step_staged<T, 8>(p, s);
+                case 1: return launch_step_staged<T, 1, 256>(p, s);
+                case 2: return launch_step_staged<T, 2, 256>(p, s);
+                case 4: return launch_step_staged<T, 4, 256>(p, s);
+                case 8: return launch_step_staged<T, 8, 256>(p, s);
                 default: break;
                 }
             }
             // fp32 state up to 64 KB a lane (256 slots): staged as well, 3 lanes per SM
             if constexpr (sizeof(T) == 4) {
                 switch (lane_bytes / (STEPV_THREADS * 16)) {
-                case 1: return launch_step_staged<T, 1>(p, s);
-                case 2: return launch_step_staged<T, 2>(p, s);
-                case 4: return launch_step_staged<T, 4>(p, s);
-                case 8: return launch_step_staged<T, 8>(p, s);
-                case 16: return launch_step_staged<T, 16>(p, s);
+                case 1: return launch_step_staged<T, 1, 256>(p, s);
+                case 2: return launch_step_staged<T, 2, 256>(p, s);
+                case 4: return launch_step_staged<T, 4, 256>(p, s);
+                case 8: return launch_step_staged<T, 8, 256>(p, s);
+                case 16: return launch_step_staged<T, 16, 256>(p, s);
                 default: break;
                 }
             }
