@@ -85,11 +85,37 @@ __global__ void __launch_bounds__(CW * SG) dense_seq_kernel(DenseSeqParams p) {
         const int nT = min(TT, T_ - t0);
         __syncthreads();
         const int64_t wbase = ((int64_t)lane * T_ + t0) * S;
-        for (int i = tid; i < TT * SP; i += NT) {
-            const int tt = i / SP, m = i - tt * SP;
-            const bool ok = tt < nT && m < S;
-            wk_s[i] = ok ? dg::to_f(wk[wbase + (int64_t)tt * S + m]) : 0.f;
-            wq_s[i] = ok ? dg::to_f(wq[wbase + (int64_t)tt * S + m]) : 0.f;
+        // rows of wk / wq for nT steps are one contiguous run of nT * S elements; when
+        // it needs no padding (S == SP) and is 16-byte aligned, 16-byte loads put every
+        // load of a thread in flight at once instead of one element per iteration
+        constexpr int EV = 16 / (int)sizeof(T);            // elements per 16-byte vector
+        const int64_t run = (int64_t)nT * S;
+        const bool vec = S == SP && run % EV == 0 && ((uintptr_t)(wk + wbase) & 15) == 0 &&
+                         ((uintptr_t)(wq + wbase) & 15) == 0;
+        if (vec) {
+            const uint4* wk16 = reinterpret_cast<const uint4*>(wk + wbase);
+            const uint4* wq16 = reinterpret_cast<const uint4*>(wq + wbase);
+            for (int i = tid; i < (int)(run / EV); i += NT) {
+                const uint4 a = wk16[i], b = wq16[i];
+                const T* ea = reinterpret_cast<const T*>(&a);
+                const T* eb = reinterpret_cast<const T*>(&b);
+#pragma unroll
+                for (int e = 0; e < EV; ++e) {
+                    wk_s[i * EV + e] = dg::to_f(ea[e]);
+                    wq_s[i * EV + e] = dg::to_f(eb[e]);
+                }
+            }
+            for (int i = (int)run + tid; i < TT * SP; i += NT) {      // steps past the end of T
+                wk_s[i] = 0.f;
+                wq_s[i] = 0.f;
+            }
+        } else {
+            for (int i = tid; i < TT * SP; i += NT) {
+                const int tt = i / SP, m = i - tt * SP;
+                const bool ok = tt < nT && m < S;
+                wk_s[i] = ok ? dg::to_f(wk[wbase + (int64_t)tt * S + m]) : 0.f;
+                wq_s[i] = ok ? dg::to_f(wq[wbase + (int64_t)tt * S + m]) : 0.f;
+            }
         }
         const int64_t vbase = ((int64_t)lane * T_ + t0) * Dh + c0;
         for (int i = tid; i < TT * CW; i += NT) {
