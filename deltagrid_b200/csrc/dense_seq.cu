@@ -10,7 +10,9 @@
 // SG threads share a column, each holding SPT slots of it in registers, and
 // the two dot products are finished with an xor-butterfly over those SG lanes.
 // That shortens the dependent FMA chain per step by SG and spreads a lane over
-// ceil(Dh/CW) CTAs.  The per-step inputs (wk, wq, v, beta, alpha) for TT steps
+// ceil(Dh/CW) CTAs.  The prediction wk_t^T S is carried one step ahead
+// (wk_{t+1}^T S_t = alpha_t wk_{t+1}^T S_{t-1} + beta_t (wk_{t+1}.wk_t) r_t), so no
+// reduction sits between one step's state update and the next step's residual.  The per-step inputs (wk, wq, v, beta, alpha) for TT steps
 // are staged in shared memory as fp32 and y/r are staged for coalesced stores.
 // The state stays fp32 for all T and is cast once at the end (delta_kernel.cu:116-121).
 #include "dg_common.cuh"
@@ -52,7 +54,7 @@ __global__ void __launch_bounds__(CW * SG) dense_seq_kernel(DenseSeqParams p) {
     float* v_s = wq_s + TT * SP;       // [TT][CW]
     float* y_s = v_s + TT * CW;        // [TT][CW]
     float* r_s = y_s + TT * CW;        // [TT][CW]
-    float* ab_s = r_s + TT * CW;       // [TT][2]  (alpha, beta)
+    float* ab_s = r_s + TT * CW;       // [TT][3]  (alpha, beta, beta * wk_{t+1}.wk_t)
 
     const T* __restrict__ v = static_cast<const T*>(p.v);
     const T* __restrict__ beta = static_cast<const T*>(p.beta);
@@ -124,40 +126,72 @@ __global__ void __launch_bounds__(CW * SG) dense_seq_kernel(DenseSeqParams p) {
         }
         for (int i = tid; i < nT; i += NT) {
             const int64_t bt = (int64_t)lane * T_ + t0 + i;
-            ab_s[2 * i] = p.dynamic_decay ? dg::to_f(decay[bt]) : alpha_static;
-            ab_s[2 * i + 1] = dg::to_f(beta[bt]);
+            ab_s[3 * i] = p.dynamic_decay ? dg::to_f(decay[bt]) : alpha_static;
+            ab_s[3 * i + 1] = dg::to_f(beta[bt]);
+            ab_s[3 * i + 2] = 0.f;
+        }
+        __syncthreads();
+        // beta_t (wk_{t+1} . wk_t) for t < nT - 1: with it each step's prediction follows
+        // from the one before (below).  Row i starts at slot i mod SP, so the threads of a
+        // warp read distinct banks.
+        for (int i = tid; i < nT - 1; i += NT) {
+            const float* a = wk_s + i * SP;
+            const float* b = a + SP;
+            float g0 = 0.f, g1 = 0.f;
+#pragma unroll 4
+            for (int n = 0; n < SP; n += 2) {
+                const int m0 = (i + n) & (SP - 1), m1 = (i + n + 1) & (SP - 1);
+                g0 = fmaf(a[m0], b[m0], g0);
+                g1 = fmaf(a[m1], b[m1], g1);
+            }
+            ab_s[3 * i + 2] = ab_s[3 * i + 1] * (g0 + g1);
         }
         __syncthreads();
 
+        // pr = wk_t . S_{t-1} for the chunk's first step, reduced directly
+        float pr;
+        {
+            const float4* wk4 = reinterpret_cast<const float4*>(wk_s);
+            float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+            for (int j4 = 0; j4 < SPT / 4; ++j4) {
+                const float4 b = wk4[g + SG * j4];
+                p0 = fmaf(b.x, st[4 * j4 + 0], p0);
+                p1 = fmaf(b.y, st[4 * j4 + 1], p1);
+                p0 = fmaf(b.z, st[4 * j4 + 2], p0);
+                p1 = fmaf(b.w, st[4 * j4 + 3], p1);
+            }
+            pr = p0 + p1;
+#pragma unroll
+            for (int o = 1; o < SG; o <<= 1) pr += __shfl_xor_sync(DG_FULL_MASK, pr, o);
+        }
+
+        // Step t reduces y_t = wq_t . S_{t-1} and x = wk_{t+1} . S_{t-1} together; then
+        //     wk_{t+1} . S_t = alpha_t x + beta_t (wk_{t+1} . wk_t) r_t,
+        // so the next step's residual needs no reduction of S_t, and the state update can
+        // issue before this step's butterflies finish.  Consecutive steps' reductions
+        // overlap (two steps per unrolled body).
+#pragma unroll 2
         for (int tt = 0; tt < nT; ++tt) {
             const float4* wk4 = reinterpret_cast<const float4*>(wk_s + tt * SP);
             const float4* wq4 = reinterpret_cast<const float4*>(wq_s + tt * SP);
-            float y0 = 0.f, y1 = 0.f, p0 = 0.f, p1 = 0.f;
+            const float4* wn4 = reinterpret_cast<const float4*>(wk_s + min(tt + 1, nT - 1) * SP);
+            float y0 = 0.f, y1 = 0.f, x0 = 0.f, x1 = 0.f;
 #pragma unroll
             for (int j4 = 0; j4 < SPT / 4; ++j4) {
                 const float4 a = wq4[g + SG * j4];
-                const float4 b = wk4[g + SG * j4];
+                const float4 b = wn4[g + SG * j4];
                 y0 = fmaf(a.x, st[4 * j4 + 0], y0);
-                p0 = fmaf(b.x, st[4 * j4 + 0], p0);
+                x0 = fmaf(b.x, st[4 * j4 + 0], x0);
                 y1 = fmaf(a.y, st[4 * j4 + 1], y1);
-                p1 = fmaf(b.y, st[4 * j4 + 1], p1);
+                x1 = fmaf(b.y, st[4 * j4 + 1], x1);
                 y0 = fmaf(a.z, st[4 * j4 + 2], y0);
-                p0 = fmaf(b.z, st[4 * j4 + 2], p0);
+                x0 = fmaf(b.z, st[4 * j4 + 2], x0);
                 y1 = fmaf(a.w, st[4 * j4 + 3], y1);
-                p1 = fmaf(b.w, st[4 * j4 + 3], p1);
+                x1 = fmaf(b.w, st[4 * j4 + 3], x1);
             }
-            float y = y0 + y1, pr = p0 + p1;
-#pragma unroll
-            for (int o = 1; o < SG; o <<= 1) {
-                y += __shfl_xor_sync(DG_FULL_MASK, y, o);
-                pr += __shfl_xor_sync(DG_FULL_MASK, pr, o);
-            }
+            const float al = ab_s[3 * tt], bt = ab_s[3 * tt + 1], bg = ab_s[3 * tt + 2];
             const float r = v_s[tt * CW + cl] - pr;
-            if (g == 0) {
-                y_s[tt * CW + cl] = y;
-                r_s[tt * CW + cl] = r;
-            }
-            const float al = ab_s[2 * tt], bt = ab_s[2 * tt + 1];
 #pragma unroll
             for (int j4 = 0; j4 < SPT / 4; ++j4) {
                 const float4 b = wk4[g + SG * j4];
@@ -166,6 +200,17 @@ __global__ void __launch_bounds__(CW * SG) dense_seq_kernel(DenseSeqParams p) {
                 st[4 * j4 + 2] = fmaf(al, st[4 * j4 + 2], (bt * b.z) * r);
                 st[4 * j4 + 3] = fmaf(al, st[4 * j4 + 3], (bt * b.w) * r);
             }
+            float y = y0 + y1, x = x0 + x1;
+#pragma unroll
+            for (int o = 1; o < SG; o <<= 1) {
+                y += __shfl_xor_sync(DG_FULL_MASK, y, o);
+                x += __shfl_xor_sync(DG_FULL_MASK, x, o);
+            }
+            if (g == 0) {
+                y_s[tt * CW + cl] = y;
+                r_s[tt * CW + cl] = r;
+            }
+            pr = fmaf(al, x, bg * r);
         }
         __syncthreads();
         T* __restrict__ out = static_cast<T*>(p.out);
@@ -195,7 +240,7 @@ template <typename T, int SG, int SPT, int CW>
 int launch_seq(DenseSeqParams p, cudaStream_t stream) {
     constexpr int SP = SG * SPT;
     constexpr size_t kSmemBudget = 96 * 1024;
-    const size_t per_step = (2 * SP + 3 * CW + 2) * sizeof(float);
+    const size_t per_step = (2 * SP + 3 * CW + 3) * sizeof(float);
     int TT = (int)std::min<size_t>(64, kSmemBudget / per_step);
     TT = std::max(1, std::min(TT, p.T));
     p.TT = TT;
