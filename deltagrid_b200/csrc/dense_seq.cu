@@ -12,8 +12,9 @@
 // That shortens the dependent FMA chain per step by SG and spreads a lane over
 // ceil(Dh/CW) CTAs.  The prediction wk_t^T S is carried one step ahead
 // (wk_{t+1}^T S_t = alpha_t wk_{t+1}^T S_{t-1} + beta_t (wk_{t+1}.wk_t) r_t), so no
-// reduction sits between one step's state update and the next step's residual.  The per-step inputs (wk, wq, v, beta, alpha) for TT steps
-// are staged in shared memory as fp32 and y/r are staged for coalesced stores.
+// reduction sits between one step's state update and the next step's residual.
+// The per-step inputs (wk, wq, v, beta, alpha) for TT steps are staged in shared
+// memory as fp32 and y/r are staged for coalesced stores.
 // The state stays fp32 for all T and is cast once at the end (delta_kernel.cu:116-121).
 #include "dg_common.cuh"
 
@@ -239,9 +240,18 @@ __global__ void __launch_bounds__(CW * SG) dense_seq_kernel(DenseSeqParams p) {
 template <typename T, int SG, int SPT, int CW>
 int launch_seq(DenseSeqParams p, cudaStream_t stream) {
     constexpr int SP = SG * SPT;
-    constexpr size_t kSmemBudget = 96 * 1024;
+    // Each chunk costs a round trip to stage its inputs.  When the grid fits in one wave
+    // (a CTA per SM at most), shared memory is not shared between CTAs, so chunks grow
+    // to 200 KB and up to 256 steps; otherwise 96 KB keeps two CTAs per SM.
+    int dev = 0, nsm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        nsm = 0;
+    const int64_t ctas = (int64_t)((p.Dh + CW - 1) / CW) * p.B * p.H;
+    const bool one_wave = ctas <= nsm;
+    const size_t kSmemBudget = (one_wave ? 200 : 96) * 1024;
     const size_t per_step = (2 * SP + 3 * CW + 3) * sizeof(float);
-    int TT = (int)std::min<size_t>(64, kSmemBudget / per_step);
+    int TT = (int)std::min<size_t>(one_wave ? 256 : 64, kSmemBudget / per_step);
     TT = std::max(1, std::min(TT, p.T));
     p.TT = TT;
     const size_t smem = per_step * TT;
