@@ -14,7 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdeltagrid_b200.so")
 
 DTYPE_F32, DTYPE_F64, DTYPE_F16, DTYPE_BF16 = 0, 1, 2, 3
-ALGO_AUTO, ALGO_SEQUENTIAL, ALGO_CHUNKED_TC = 0, 1, 2
+ALGO_AUTO, ALGO_SEQUENTIAL, ALGO_CHUNKED_TC, ALGO_CHUNKED_TC_ROWS = 0, 1, 2, 3
 PKM_AUTO, PKM_ONE_STEP, PKM_PIPELINED, PKM_WARP_SPECIALIZED = 0, 1, 2, 3
 DEVCHK_INDEX_RANGE = 0x1
 
@@ -30,6 +30,8 @@ _SIGS = {
     "dg_last_cuda_error": [],
     "dg_dense_forward": [_I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P],
     "dg_dense_forward_ex": [_I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _P],
+    "dg_dense_forward_ex2": [_I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _I, _P],
+    "dg_set_wait_limit": [ctypes.c_uint],
     "dg_dense_step": [_I, _I, _I, _I, _I, _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
                       _P, _I, _I64, _I64, _P, _P, _P, _P],
     "dg_pkm_forward": [_I, _I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P],
@@ -48,7 +50,7 @@ _SIGS = {
     "dg_pkm_backward": [_I, _I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P,
                         _P, _P],
 }
-_RESTYPE = {"dg_status_string": ctypes.c_char_p, "dg_pkm_forward_workspace_size": ctypes.c_size_t,
+_RESTYPE = {"dg_status_string": ctypes.c_char_p, "dg_set_wait_limit": ctypes.c_uint, "dg_pkm_forward_workspace_size": ctypes.c_size_t,
             "dg_dense_backward_workspace_size": ctypes.c_size_t}
 
 _lib = None

@@ -122,13 +122,13 @@ std::vector<Tensor> forward(const Tensor& q, const Tensor& k, const Tensor& v, c
         if (!is_fp32) s_final_f = at::empty({B, H, S, Dh}, opt.dtype(at::kFloat));
     }
     const c10::cuda::CUDAGuard guard(v_c.device());
-    check(dg_dense_forward_ex(code, (int)B, (int)H, (int)T, (int)S, (int)Dh, v_c.data_ptr(), beta_c.data_ptr(),
-                              wk_c.data_ptr(), wq_c.data_ptr(), decay_c.data_ptr(), decay_c.dim() > 1 ? 1 : 0,
-                              ptr_or_null(s_init_c), out.data_ptr(), s_final.data_ptr(),
-                              err_out.defined() ? err_out.data_ptr<float>() : nullptr,
-                              (save_for_backward && !is_fp32) ? s_final_f.data_ptr<float>() : nullptr, algo,
-                              stream_of(v_c)),
-          "dg_dense_forward_ex");
+    check(dg_dense_forward_ex2(code, (int)B, (int)H, (int)T, (int)S, (int)Dh, v_c.data_ptr(), beta_c.data_ptr(),
+                               wk_c.data_ptr(), wq_c.data_ptr(), decay_c.data_ptr(), decay_c.dim() > 1 ? 1 : 0,
+                               ptr_or_null(s_init_c), out.data_ptr(), s_final.data_ptr(),
+                               err_out.defined() ? err_out.data_ptr<float>() : nullptr,
+                               (save_for_backward && !is_fp32) ? s_final_f.data_ptr<float>() : nullptr,
+                               status_word(v_c.device()).data_ptr<int32_t>(), algo, stream_of(v_c)),
+          "dg_dense_forward_ex2");
     return {out, s_final, err_out, s_final_f};
 }
 

@@ -4,6 +4,9 @@
 namespace dg_host {
 
 static thread_local int g_last_cuda_error = 0;
+static unsigned int g_wait_limit = 1u << 22;
+
+uint32_t wait_limit() { return __atomic_load_n(&g_wait_limit, __ATOMIC_RELAXED); }
 
 int record_cuda_error(cudaError_t e) {
     g_last_cuda_error = (int)e;
@@ -20,6 +23,10 @@ int dense_forward_chunked_tc(int dtype, int B, int H, int T, int S, int Dh, cons
                              int dynamic_decay, const void* s_init, void* out, void* s_final,
                              float* err_out, float* s_final_f, cudaStream_t stream);
 bool dense_chunked_tc_supports(int dtype, int B, int H, int T, int S, int Dh);
+int dense_forward_chunked_t(int dtype, int B, int H, int T, int S, int Dh, const void* v, const void* beta,
+                            const void* wk, const void* wq, const void* decay, int dynamic_decay, const void* s_init,
+                            void* out, void* s_final, float* err_out, float* s_final_f, int32_t* status,
+                            cudaStream_t stream);
 int dense_step(int dtype, int B, int H, int S, int Dh, const void* v, int64_t v_sb, int64_t v_sh,
                const void* beta, int64_t beta_sb, int64_t beta_sh, const void* wk, int64_t wk_sb,
                int64_t wk_sh, const void* wq, int64_t wq_sb, int64_t wq_sh, const void* decay,
@@ -73,6 +80,18 @@ int dg_dense_forward_ex(int dtype, int B, int H, int T, int slots, int dh, const
                         const void* beta, const void* wk, const void* wq, const void* decay,
                         int dynamic_decay, const void* s_init, void* out, void* s_final,
                         float* err_out, float* s_final_f, int algo, void* stream) {
+    return dg_dense_forward_ex2(dtype, B, H, T, slots, dh, v, beta, wk, wq, decay, dynamic_decay, s_init, out,
+                                s_final, err_out, s_final_f, nullptr, algo, stream);
+}
+
+unsigned int dg_set_wait_limit(unsigned int polls) {
+    return __atomic_exchange_n(&g_wait_limit, polls, __ATOMIC_RELAXED);
+}
+
+int dg_dense_forward_ex2(int dtype, int B, int H, int T, int slots, int dh, const void* v,
+                         const void* beta, const void* wk, const void* wq, const void* decay,
+                         int dynamic_decay, const void* s_init, void* out, void* s_final,
+                         float* err_out, float* s_final_f, int32_t* dev_status, int algo, void* stream) {
     if (!valid_dtype(dtype) || B <= 0 || H <= 0 || T < 0 || slots <= 0 || dh <= 0)
         return DG_ERR_INVALID_ARGUMENT;
     // with T == 0 the per-step tensors are empty (their pointers may be null):
@@ -83,8 +102,11 @@ int dg_dense_forward_ex(int dtype, int B, int H, int T, int slots, int dh, const
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (T == 0) algo = DG_DENSE_SEQUENTIAL;
     const bool tc_ok = dense_chunked_tc_supports(dtype, B, H, T, slots, dh);
-    if (algo == DG_DENSE_CHUNKED_TC && !tc_ok) return DG_ERR_UNSUPPORTED;
-    if (algo == DG_DENSE_CHUNKED_TC || (algo == DG_DENSE_AUTO && tc_ok))
+    if ((algo == DG_DENSE_CHUNKED_TC || algo == DG_DENSE_CHUNKED_TC_ROWS) && !tc_ok) return DG_ERR_UNSUPPORTED;
+    if (algo == DG_DENSE_CHUNKED_TC)
+        return dense_forward_chunked_t(dtype, B, H, T, slots, dh, v, beta, wk, wq, decay, dynamic_decay, s_init,
+                                       out, s_final, err_out, s_final_f, dev_status, s);
+    if (algo == DG_DENSE_CHUNKED_TC_ROWS || (algo == DG_DENSE_AUTO && tc_ok))
         return dense_forward_chunked_tc(dtype, B, H, T, slots, dh, v, beta, wk, wq, decay,
                                         dynamic_decay, s_init, out, s_final, err_out, s_final_f, s);
     if (algo != DG_DENSE_AUTO && algo != DG_DENSE_SEQUENTIAL) return DG_ERR_INVALID_ARGUMENT;

@@ -1,0 +1,611 @@
+// dense_chunk_t.cu -- chunkwise (WY/UT form) dense delta-rule recurrence on tcgen05,
+// with the state held transposed: S^T (Dh rows x slots) on TMEM lanes.
+//
+// Same recurrence and chunk algebra as dense_chunk_tc.cu (src/cpp/delta_kernel.cu:78-112,
+// src/modules/memory.py:325-410); C = 64 steps per chunk, a_i = prod_{l<=i} alpha_l,
+// aprev_i = a_{i-1}:
+//     L  = strict_lower(aprev_i beta_j / a_j  k_i.k_j),     T = (I + L)^{-1}
+//     R  = T (V - aprev o (K S0))
+//     Y  = aprev o (Q S0) + strict_lower(aprev_i / a_j  q_i.k_j) (beta o R)
+//     S1 = a_{C-1} S0 + K^T diag(a_{C-1} beta_j / a_j) R
+//
+// Why transposed: with Dh = 64 on the M side of every product, the state is an M = 64
+// accumulator (rows on 16 of each 32 TMEM lanes) and its 16-bit copy is the A operand of
+// [K;Q] S0 read straight from TMEM (the tcgen05 "A in tensor memory" form).  Nothing of
+// the state passes through shared memory; [K;Q] (the chunk's wk / wq tiles) is the only
+// shared-memory operand of the big product, and the state copy is a TMEM -> TMEM pass.
+//
+// Per chunk, all MMAs are M = 64 (D at TMEM lane offset 0 unless stated):
+//   P2  D2 = S0^T [K;Q]^T     A: S0^T copy (TMEM)  B: [K;Q] rows (smem, K-major), N = 128
+//   P3  R^T = X^T T^T         A: X^T (TMEM)        B: T rows (smem, K-major)
+//   P4  Yi^T = (bR)^T Mqk^T   A: (beta R)^T (TMEM) B: Mqk columns (smem, MN-major)
+//   P5  S^T += R'^T K         A: R'^T (smem)       B: K (smem, MN-major), D at lane offset 16
+//   G   D1 = K [K;Q]^T        A, B: next chunk's K, [K;Q] slices streamed through a ring
+// Warpgroup 0 runs the state chain (S0 copy, P2, X, P3, R, P4/P5, Y); its thread 0 issues
+// its TMA loads and MMAs.  Warpgroup 1 works one chunk ahead on what depends only on the
+// inputs: it streams the next chunk's [K;Q] through a two-slot ring for the Gram G, forms
+// L and Mqk, inverts I + L in fp32 and hands T and Mqk over as fp16 tiles.  So the Gram
+// and the inverse run beside the chain instead of on it.
+//
+// Inputs fp16 or bf16 (kind::f16: both operands of one MMA share a type, so the S0 and R'
+// copies are in the input type; T, X, beta R and Mqk are formed here and are fp16).
+// Dh = 64, slots in {128, 256, 384, 512}.  Every mbarrier wait is bounded (a launch
+// parameter); a wait that gives up flags DG_DEVCHK_TIMEOUT, and the CTA drains the copies
+// and MMAs it issued, frees its TMEM and returns.
+#include "chunk_common.cuh"
+
+namespace {
+
+using namespace dgc;
+
+constexpr uint32_t SLICE = 16384;        // [K rows 0-63 | Q rows 0-63] of 64 slots, 16-bit, 128B swizzle
+constexpr uint32_t LANE16 = 16u << 16;   // TMEM address of the upper 16 lanes of each quarter
+constexpr uint32_t DRAIN_LIMIT = 1u << 22;
+
+struct TParams {
+    const void* beta;
+    const void* decay;
+    const void* s_init;
+    void* out;
+    void* s_final;
+    float* err_out;
+    float* s_final_f;
+    int32_t* status;
+    int H, T, nchunks, dynamic_decay;
+    uint32_t wait_limit;   // polls of a bounded wait (each at most ~1 us); 0 gives up at once
+};
+
+template <int S>
+struct TLayout {
+    static constexpr int NSL = S / 64;
+    static constexpr uint32_t KQ = 0;                       // this chunk's [K;Q] slices
+    static constexpr uint32_t RING = KQ + NSL * SLICE;      // next chunk's slices, two slots
+    static constexpr uint32_t TT = RING + 2 * SLICE;        // T (rows i, K-major)
+    static constexpr uint32_t MQ = TT + 8192;               // Mqk (rows j, MN-major)
+    static constexpr uint32_t RT = MQ + 8192;               // R'^T (rows d, K-major)
+    static constexpr uint32_t VT = RT + 8192;               // V (rows t, TMA)
+    static constexpr uint32_t LT = VT + 8192;               // fp32 [64][68] inverse scratch
+    static constexpr uint32_t SC0 = LT + 64 * 68 * 4;       // WG0: aprev, beta, a_end / a, atot; two chunks
+    static constexpr uint32_t SC1 = SC0 + 2 * 4 * 64 * 4;   // WG1: aprev, beta / a, 1 / a
+    static constexpr uint32_t BAR = SC1 + 3 * 64 * 4;       // mbarriers, TMEM base, abort flag
+    static constexpr uint32_t BYTES = BAR + 16 * 8 + 16;
+    // TMEM columns (lane offset 0 unless stated)
+    static constexpr uint32_t A0 = 0;          // S0^T copy, S / 2 columns, live during P2
+    static constexpr uint32_t XA = 0;          // X^T (P3 A), 32 columns, after P2
+    static constexpr uint32_t D3 = 32;         // R^T, 64
+    static constexpr uint32_t BA = 96;         // (beta R)^T (P4 A), 32
+    static constexpr uint32_t D4 = 128;        // Y intra-chunk part, 64
+    static constexpr uint32_t D2 = 256;        // [K S0 | Q S0]^T, 128
+    static constexpr uint32_t D1 = 384;        // next chunk's K [K;Q]^T, 128
+    // the state S^T: lane offset 16, columns [0, S)
+};
+static_assert(TLayout<512>::BYTES + 1024 <= 232448, "shared memory");
+
+enum Bars { B_K = 0, B_Q, B_V, B_P2, B_P3, B_P4, B_P5, B_T, B_MQ, B_RF0, B_RF1, B_RE0, B_RE1, B_G, B_D0, B_D1, NBARS };
+
+template <typename TI> constexpr uint32_t idesc_in(int N, int b_mn) { return tc::make_idesc(64, N, Io<TI>::kBf16, 0, b_mn); }
+constexpr uint32_t IDESC_P3 = tc::make_idesc(64, 64, 0, 0, 0);
+constexpr uint32_t IDESC_P4 = tc::make_idesc(64, 64, 0, 0, 1);
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) { return Io<__half>::pack2(a, b); }
+
+// bounded wait that also gives up when another role has already given up
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_t limit, volatile int* abort_flag) {
+    for (uint32_t i = 0; i < limit; ++i) {
+        if (tc::mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+    }
+    return false;
+}
+
+template <int S, typename TI>
+__global__ void __launch_bounds__(256, 1)
+    dense_chunk_t_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmq,
+                         const __grid_constant__ CUtensorMap tmv, TParams p) {
+    using Ly = TLayout<S>;
+    constexpr int NSL = Ly::NSL;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* kq = sm + Ly::KQ;
+    uint8_t* ring = sm + Ly::RING;
+    uint8_t* tt = sm + Ly::TT;
+    uint8_t* mqt = sm + Ly::MQ;
+    uint8_t* rt = sm + Ly::RT;
+    uint8_t* vt = sm + Ly::VT;
+    float* lt = reinterpret_cast<float*>(sm + Ly::LT);
+    float* sc0_base = reinterpret_cast<float*>(sm + Ly::SC0);
+    float* sc1 = reinterpret_cast<float*>(sm + Ly::SC1);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ly::BAR);
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 16) + 1;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int q4 = warp & 3;                  // TMEM lane quarter of this warp
+    const int r16 = lane & 15, half = lane >> 4;
+    const int lane_bh = blockIdx.x;
+    const int h = lane_bh % p.H;
+    const int T_ = p.T, NC = p.nchunks;
+    const int64_t lane_base = (int64_t)lane_bh * T_;
+    const TI* beta = static_cast<const TI*>(p.beta);
+    const TI* decay = static_cast<const TI*>(p.decay);
+    const uint32_t lim = p.wait_limit;
+
+    if (warp == 0) tc::tmem_alloc(tmem_holder, 512);
+    if (tid == 0) {
+        for (int i = 0; i < NBARS; ++i) tc::mbar_init(bars + i, 1);
+        *abort_flag = 0;
+        tc::fence_barrier_init();
+        tc::prefetch_tmap(&tmk);
+        tc::prefetch_tmap(&tmq);
+        tc::prefetch_tmap(&tmv);
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    const uint32_t tq0 = tmem + ((uint32_t)(32 * q4) << 16);      // this warp's rows, lane offset 0
+    const uint32_t tq1 = tq0 + LANE16;                              // the state's rows
+    const float alpha_static = p.dynamic_decay ? 1.f : dg::to_f(decay[h]);
+    const int row = 16 * q4 + r16;           // Dh row (WG0) or chunk row j (WG1) of this thread
+    const int cb = 32 * half;                // first chunk step / slot of this thread's half
+
+    // copies and MMAs this CTA has in flight, drained before exit after a failed wait
+    bool pend_k = false, pend_q = false, pend_v = false;
+    uint32_t par_k = 0, par_q = 0, par_v = 0;    // phase parity of the load in flight
+    uint32_t pend_ring = 0;                  // bit s: ring slot s has a load in flight
+    uint32_t ring_par[2] = {0u, 0u};         // and the phase parity that load completes
+    bool failed = false;
+
+    if (warp < 4) {
+        // ============================ WG0: the state chain ============================
+        {   // initial state -> S^T (lane offset 16): thread (row d, half) holds slots [64g + 32 half, +32)
+            const TI* s_init = static_cast<const TI*>(p.s_init);
+            for (int g = 0; g < NSL; ++g) {
+                uint32_t r[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    float v = 0.f;
+                    if (s_init) v = dg::to_f(s_init[((int64_t)lane_bh * S + 64 * g + cb + i) * DH + row]);
+                    r[i] = __float_as_uint(v);
+                }
+                tc::tmem_st16x2_32(tq1 + 64 * g, r);
+            }
+            tc::tmem_wait_st();
+        }
+        if (tid == 0 && NC > 0) {
+            tc::mbar_expect_tx(bars + B_K, NSL * 8192);
+            for (int s = 0; s < NSL; ++s) tc::tma_load_3d(kq + s * SLICE, &tmk, bars + B_K, 64 * s, 0, lane_bh);
+            tc::mbar_expect_tx(bars + B_Q, NSL * 8192);
+            for (int s = 0; s < NSL; ++s) tc::tma_load_3d(kq + s * SLICE + 8192, &tmq, bars + B_Q, 64 * s, 0, lane_bh);
+            tc::mbar_expect_tx(bars + B_V, 8192);
+            tc::tma_load_3d(vt, &tmv, bars + B_V, 0, 0, lane_bh);
+            pend_k = pend_q = pend_v = true;
+            par_k = par_q = par_v = 0;
+        }
+        tc::tc_fence_before();
+        tc::group_sync(BAR_WG0);
+        for (int c = 0; c < NC && !failed; ++c) {
+            const int t0 = c * CH;
+            const uint32_t par = (uint32_t)(c & 1);
+            float* sc0 = sc0_base + (c & 1) * 256;     // this chunk's scalars (the previous chunk may still read the other half)
+            if (warp == 0) {      // chunk scalars: aprev_t, beta_t, a_end / a_t, atot
+                const ChunkScalars cs = chunk_scalars(beta, decay, p.dynamic_decay, alpha_static, lane_base, t0, T_, lane);
+                reinterpret_cast<float2*>(sc0)[lane] = make_float2(cs.ap0, cs.ap1);
+                reinterpret_cast<float2*>(sc0 + 64)[lane] = make_float2(cs.b0, cs.b1);
+                reinterpret_cast<float2*>(sc0 + 128)[lane] = make_float2(cs.atot / cs.a0, cs.atot / cs.a1);
+                if (lane == 0) sc0[192] = cs.atot;
+            }
+            // the previous update is complete (state and K tiles), this chunk's K and Q have landed
+            bool bad = (c > 0 && !wait_bar(bars + B_P5, par ^ 1u, lim, abort_flag));
+            bad = bad || !wait_bar(bars + B_K, par, lim, abort_flag) || !wait_bar(bars + B_Q, par, lim, abort_flag);
+            if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
+            if (tid == 0) pend_k = pend_q = false;
+            tc::tc_fence_after();
+            const float atot = sc0[192];
+            // S0^T (fp32, lane offset 16) -> 16-bit copy (lane offset 0), scaled by atot in place;
+            // [K;Q] S0 issued 128 slots at a time as the copy proceeds
+            for (int g2 = 0; g2 < NSL; g2 += 2) {
+#pragma unroll
+                for (int gg = 0; gg < 2; ++gg) {
+                    const int g = g2 + gg;
+                    if (g < NSL) {
+                        uint32_t r[32], pk[16];
+                        tc::tmem_ld16x2_32(tq1 + 64 * g, r);
+                        tc::tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            pk[i] = Io<TI>::pack2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+                        tc::tmem_st16x2_16(tq0 + Ly::A0 + 32 * g, pk);
+                        if (atot != 1.f) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(atot * __uint_as_float(r[i]));
+                            tc::tmem_st16x2_32(tq1 + 64 * g, r);
+                        }
+                    }
+                }
+                tc::tmem_wait_st();
+                tc::tc_fence_before();
+                tc::group_sync(BAR_WG0);
+                if (tid == 0) {
+                    tc::tc_fence_after();
+                    for (int g = g2; g < g2 + 2 && g < NSL; ++g)
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            tc::mma_f16_ts(tmem + Ly::D2, tmem + Ly::A0 + 32 * g + 8 * kk,
+                                           tc::make_desc(tc::smem_u32(kq + g * SLICE) + 32 * kk, 16, 1024),
+                                           idesc_in<TI>(128, 0), (g | kk) != 0);
+                }
+            }
+            if (tid == 0) tc::mma_commit(bars + B_P2);
+            // X^T = V^T - (K S0)^T diag(aprev)  -> 16-bit P3 operand in TMEM
+            bad = !wait_bar(bars + B_P2, par, lim, abort_flag) || !wait_bar(bars + B_V, par, lim, abort_flag);
+            if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
+            tc::tc_fence_after();
+            if (tid == 0) {
+                pend_v = false;
+                if (c + 1 < NC) {        // the Q tiles are free: the next chunk's Q
+                    tc::mbar_expect_tx(bars + B_Q, NSL * 8192);
+                    for (int s = 0; s < NSL; ++s)
+                        tc::tma_load_3d(kq + s * SLICE + 8192, &tmq, bars + B_Q, 64 * s, t0 + CH, lane_bh);
+                    pend_q = true;
+                    par_q = par ^ 1u;
+                }
+            }
+            {
+                uint32_t r[32], pk[16];
+                tc::tmem_ld16x2_32(tq0 + Ly::D2, r);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int t = cb + 2 * i;
+                    const float v0 = dg::to_f(*reinterpret_cast<const TI*>(vt + t * 128 + ((((row >> 3) ^ (t & 7))) << 4) + (row & 7) * 2));
+                    const float v1 = dg::to_f(*reinterpret_cast<const TI*>(vt + (t + 1) * 128 + ((((row >> 3) ^ ((t + 1) & 7))) << 4) + (row & 7) * 2));
+                    pk[i] = pack_h2(v0 - sc0[t] * __uint_as_float(r[2 * i]), v1 - sc0[t + 1] * __uint_as_float(r[2 * i + 1]));
+                }
+                tc::tmem_st16x2_16(tq0 + Ly::XA, pk);
+                tc::tmem_wait_st();
+            }
+            tc::tc_fence_before();
+            tc::group_sync(BAR_WG0);
+            if (tid == 0) {
+                tc::tc_fence_after();
+                if (c + 1 < NC) {        // the V tile is free: the next chunk's V
+                    tc::mbar_expect_tx(bars + B_V, 8192);
+                    tc::tma_load_3d(vt, &tmv, bars + B_V, 0, t0 + CH, lane_bh);
+                    pend_v = true;
+                    par_v = par ^ 1u;
+                }
+            }
+            // R^T = X^T T^T once warpgroup 1 has written T of this chunk
+            bad = !wait_bar(bars + B_T, par, lim, abort_flag);
+            if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
+            if (tid == 0) {
+                tc::tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    tc::mma_f16_ts(tmem + Ly::D3, tmem + Ly::XA + 8 * kk,
+                                   tc::make_desc(tc::smem_u32(tt) + 32 * kk, 16, 1024), IDESC_P3, kk != 0);
+                tc::mma_commit(bars + B_P3);
+            }
+            bad = !wait_bar(bars + B_P3, par, lim, abort_flag);
+            if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
+            tc::tc_fence_after();
+            {   // residuals: err_out, R'^T (update operand, smem), (beta R)^T (P4 operand, TMEM)
+                uint32_t r[32], pk[16];
+                tc::tmem_ld16x2_32(tq0 + Ly::D3, r);
+                tc::tmem_wait_ld();
+                float rr[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) rr[i] = __uint_as_float(r[i]);
+                if (p.err_out) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int t = t0 + cb + i;
+                        if (t < T_) p.err_out[(lane_base + t) * DH + row] = rr[i];
+                    }
+                }
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    uint4 w;
+                    const int t = cb + 8 * cc;
+                    w.x = Io<TI>::pack2(sc0[128 + t] * sc0[64 + t] * rr[8 * cc], sc0[128 + t + 1] * sc0[64 + t + 1] * rr[8 * cc + 1]);
+                    w.y = Io<TI>::pack2(sc0[128 + t + 2] * sc0[64 + t + 2] * rr[8 * cc + 2], sc0[128 + t + 3] * sc0[64 + t + 3] * rr[8 * cc + 3]);
+                    w.z = Io<TI>::pack2(sc0[128 + t + 4] * sc0[64 + t + 4] * rr[8 * cc + 4], sc0[128 + t + 5] * sc0[64 + t + 5] * rr[8 * cc + 5]);
+                    w.w = Io<TI>::pack2(sc0[128 + t + 6] * sc0[64 + t + 6] * rr[8 * cc + 6], sc0[128 + t + 7] * sc0[64 + t + 7] * rr[8 * cc + 7]);
+                    *reinterpret_cast<uint4*>(rt + tc::sw128(row, 4 * half + cc)) = w;
+                }
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    pk[i] = pack_h2(sc0[64 + cb + 2 * i] * rr[2 * i], sc0[64 + cb + 2 * i + 1] * rr[2 * i + 1]);
+                tc::tmem_st16x2_16(tq0 + Ly::BA, pk);
+                tc::tmem_wait_st();
+            }
+            tc::fence_proxy_async();
+            tc::tc_fence_before();
+            bad = !wait_bar(bars + B_MQ, par, lim, abort_flag);
+            if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
+            if (tid == 0) {                  // Y intra-chunk part, then S^T += R'^T K
+                tc::tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    tc::mma_f16_ts(tmem + Ly::D4, tmem + Ly::BA + 8 * kk,
+                                   tc::make_desc(tc::smem_u32(mqt) + kk * 2048, 8192, 1024), IDESC_P4, kk != 0);
+                tc::mma_commit(bars + B_P4);
+#pragma unroll
+                for (int nt = 0; nt < (S + 255) / 256; ++nt) {
+                    const int n = (S - 256 * nt) >= 256 ? 256 : S - 256 * nt;
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc::mma_f16(tmem + LANE16 + 256 * nt, tc::make_desc(tc::smem_u32(rt) + 32 * kk, 16, 1024),
+                                    tc::make_desc(tc::smem_u32(kq + 4 * nt * SLICE) + kk * 2048, SLICE, 1024),
+                                    idesc_in<TI>(n, 1), 1u);
+                }
+                tc::mma_commit(bars + B_P5);
+            }
+            bad = !wait_bar(bars + B_P4, par, lim, abort_flag);
+            if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
+            tc::tc_fence_after();
+            {   // Y^T = (Q S0)^T diag(aprev) + Yi^T
+                uint32_t yi[32], qs[32];
+                tc::tmem_ld16x2_32(tq0 + Ly::D4, yi);
+                tc::tmem_ld16x2_32(tq0 + Ly::D2 + 64, qs);
+                tc::tmem_wait_ld();
+                TI* out = static_cast<TI*>(p.out);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int t = t0 + cb + i;
+                    if (t < T_)
+                        out[(lane_base + t) * DH + row] =
+                            dg::from_f<TI>(fmaf(sc0[cb + i], __uint_as_float(qs[i]), __uint_as_float(yi[i])));
+                }
+            }
+            tc::tc_fence_before();
+            if (tid == 0 && c + 1 < NC) {    // the K tiles are free once the update is done: the next chunk's K
+                if (wait_bar(bars + B_P5, par, lim, abort_flag)) {
+                    tc::mbar_expect_tx(bars + B_K, NSL * 8192);
+                    for (int s = 0; s < NSL; ++s) tc::tma_load_3d(kq + s * SLICE, &tmk, bars + B_K, 64 * s, t0 + CH, lane_bh);
+                    pend_k = true;
+                    par_k = par ^ 1u;
+                } else {
+                    *abort_flag = 1;
+                }
+            }
+        }
+        // final state: S^T -> s_final / s_final_f through a shared-memory transpose (the K/Q tiles are free)
+        if (!failed && NC > 0) {
+            bool bad = !wait_bar(bars + B_P5, (uint32_t)((NC - 1) & 1), lim, abort_flag);
+            if (tc::group_sync_or(BAR_WG0, bad)) failed = true;
+        }
+        if (!failed) {
+            tc::tc_fence_after();
+            float* stg = reinterpret_cast<float*>(kq);       // [64 slots][65]
+            TI* s_fin = static_cast<TI*>(p.s_final);
+            for (int g = 0; g < NSL; ++g) {
+                uint32_t r[32];
+                tc::tmem_ld16x2_32(tq1 + 64 * g, r);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) stg[(cb + i) * 65 + row] = __uint_as_float(r[i]);
+                tc::group_sync(BAR_WG0);
+                const int sr = tid >> 1, d0 = 32 * (tid & 1);
+                const int64_t o = ((int64_t)lane_bh * S + 64 * g + sr) * DH + d0;
+                float x[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) x[i] = stg[sr * 65 + d0 + i];
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc)
+                    reinterpret_cast<uint4*>(s_fin + o)[cc] =
+                        make_uint4(Io<TI>::pack2(x[8 * cc], x[8 * cc + 1]), Io<TI>::pack2(x[8 * cc + 2], x[8 * cc + 3]),
+                                   Io<TI>::pack2(x[8 * cc + 4], x[8 * cc + 5]), Io<TI>::pack2(x[8 * cc + 6], x[8 * cc + 7]));
+                if (p.s_final_f) {
+#pragma unroll
+                    for (int qq = 0; qq < 8; ++qq)
+                        reinterpret_cast<float4*>(p.s_final_f + o)[qq] =
+                            make_float4(x[4 * qq], x[4 * qq + 1], x[4 * qq + 2], x[4 * qq + 3]);
+                }
+                tc::group_sync(BAR_WG0);
+            }
+        }
+    } else {
+        // ================= WG1: T = (I + L)^{-1} and Mqk, one chunk ahead =================
+        const int t1 = tid - 128;
+        uint32_t ring_uses = 0;
+        for (int n = 0; n < NC && !failed; ++n) {
+            const int t0 = n * CH;
+            const uint32_t par = (uint32_t)(n & 1);
+            if (warp == 4) {
+                const ChunkScalars cs = chunk_scalars(beta, decay, p.dynamic_decay, alpha_static, lane_base, t0, T_, lane);
+                reinterpret_cast<float2*>(sc1)[lane] = make_float2(cs.ap0, cs.ap1);
+                reinterpret_cast<float2*>(sc1 + 64)[lane] = make_float2(cs.b0 / cs.a0, cs.b1 / cs.a1);
+                reinterpret_cast<float2*>(sc1 + 128)[lane] = make_float2(1.f / cs.a0, 1.f / cs.a1);
+            }
+            if (tid == 128) {        // Gram D1 = K [K;Q]^T over the chunk's slices, streamed two at a time
+                bool ok = true;
+                auto issue_load = [&](int s) {
+                    const uint32_t slot = (ring_uses + s) & 1u;
+                    uint8_t* dst = ring + slot * SLICE;
+                    tc::mbar_expect_tx(bars + B_RF0 + slot, SLICE);
+                    tc::tma_load_3d(dst, &tmk, bars + B_RF0 + slot, 64 * s, t0, lane_bh);
+                    tc::tma_load_3d(dst + 8192, &tmq, bars + B_RF0 + slot, 64 * s, t0, lane_bh);
+                    pend_ring |= 1u << slot;
+                    ring_par[slot] = ((ring_uses + s) >> 1) & 1u;
+                };
+                auto slot_free = [&](int s) -> bool {   // the MMAs that last read this slot are done
+                    const uint32_t u = ring_uses + s;
+                    if (u < 2) return true;
+                    return wait_bar(bars + B_RE0 + (u & 1u), ((u >> 1) - 1) & 1u, lim, abort_flag);
+                };
+                ok = slot_free(0);
+                if (ok) issue_load(0);
+                if (ok && NSL > 1) { ok = slot_free(1); if (ok) issue_load(1); }
+                for (int s = 0; s < NSL && ok; ++s) {
+                    const uint32_t u = ring_uses + s, slot = u & 1u;
+                    ok = wait_bar(bars + B_RF0 + slot, (u >> 1) & 1u, lim, abort_flag);
+                    if (!ok) break;
+                    pend_ring &= ~(1u << slot);
+                    tc::tc_fence_after();
+                    const uint32_t base = tc::smem_u32(ring + slot * SLICE);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc::mma_f16(tmem + Ly::D1, tc::make_desc(base + 32 * kk, 16, 1024),
+                                    tc::make_desc(base + 32 * kk, 16, 1024), idesc_in<TI>(128, 0), (s | kk) != 0);
+                    tc::mma_commit(bars + B_RE0 + slot);
+                    if (s + 2 < NSL) {
+                        ok = slot_free(s + 2);
+                        if (ok) issue_load(s + 2);
+                    }
+                }
+                ring_uses += NSL;
+                if (ok) tc::mma_commit(bars + B_G);
+                else *abort_flag = 1;
+            }
+            bool bad = !wait_bar(bars + B_G, par, lim, abort_flag);
+            if (tc::group_sync_or(BAR_WG1, bad)) { failed = true; break; }
+            tc::tc_fence_after();
+            float mq[32];
+            {   // L rows (fp32 scratch) and this thread's Mqk column j = row (registers)
+                uint32_t g[32];
+                tc::tmem_ld16x2_32(tq0 + Ly::D1, g);
+                tc::tmem_wait_ld();
+                const float ap_j = sc1[row];
+                float l[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int jj = cb + i;      // column of L in row `row`
+                    l[i] = (jj < row) ? ap_j * sc1[64 + jj] * __uint_as_float(g[i]) : 0.f;
+                }
+                float4* dst = reinterpret_cast<float4*>(lt + row * LDT + cb);
+#pragma unroll
+                for (int qq = 0; qq < 8; ++qq) dst[qq] = make_float4(l[4 * qq], l[4 * qq + 1], l[4 * qq + 2], l[4 * qq + 3]);
+                tc::tmem_ld16x2_32(tq0 + Ly::D1 + 64, g);
+                tc::tmem_wait_ld();
+                const float ia_j = sc1[128 + row];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int ii = cb + i;      // Mqk[ii][row] = aprev_ii / a_row  q_ii . k_row, row < ii
+                    mq[i] = (ii > row) ? sc1[ii] * ia_j * __uint_as_float(g[i]) : 0.f;
+                }
+            }
+            tc::tc_fence_before();
+            tc::group_sync(BAR_WG1);
+            invert_unit_lower(lt, t1);
+            // T of this chunk replaces the previous one once P3 of the previous chunk is done
+            bad = (n > 0) && !wait_bar(bars + B_P3, par ^ 1u, lim, abort_flag);
+            if (tc::group_sync_or(BAR_WG1, bad)) { failed = true; break; }
+            if (t1 < 64) {
+                float tr[64];
+                const float4* src = reinterpret_cast<const float4*>(lt + t1 * LDT);
+#pragma unroll
+                for (int qq = 0; qq < 16; ++qq) {
+                    const float4 v = src[qq];
+                    tr[4 * qq] = v.x; tr[4 * qq + 1] = v.y; tr[4 * qq + 2] = v.z; tr[4 * qq + 3] = v.w;
+                }
+                st_row16(tt, t1, tr);
+            }
+            tc::fence_proxy_async();
+            tc::group_sync(BAR_WG1);
+            if (t1 == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bars + B_T)) : "memory");
+            // Mqk likewise once P4 of the previous chunk is done
+            bad = (n > 0) && !wait_bar(bars + B_P4, par ^ 1u, lim, abort_flag);
+            if (tc::group_sync_or(BAR_WG1, bad)) { failed = true; break; }
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                uint4 w;
+                w.x = pack_h2(mq[8 * cc], mq[8 * cc + 1]);
+                w.y = pack_h2(mq[8 * cc + 2], mq[8 * cc + 3]);
+                w.z = pack_h2(mq[8 * cc + 4], mq[8 * cc + 5]);
+                w.w = pack_h2(mq[8 * cc + 6], mq[8 * cc + 7]);
+                *reinterpret_cast<uint4*>(mqt + tc::sw128(row, 4 * half + cc)) = w;
+            }
+            tc::fence_proxy_async();
+            tc::group_sync(BAR_WG1);
+            if (t1 == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bars + B_MQ)) : "memory");
+        }
+    }
+
+    if (failed) *abort_flag = 1;
+    // after a failed wait, the copies and MMAs this CTA issued must finish before its shared
+    // memory and TMEM go away: each issuing thread waits for its loads in flight and for a
+    // commit of its own MMAs (bounded; in the normal path all of these are already complete)
+    if (tid == 0 || tid == 128) {
+        if (tid == 0) {
+            if (pend_k) tc::mbar_wait(bars + B_K, par_k, DRAIN_LIMIT);
+            if (pend_q) tc::mbar_wait(bars + B_Q, par_q, DRAIN_LIMIT);
+            if (pend_v) tc::mbar_wait(bars + B_V, par_v, DRAIN_LIMIT);
+        } else {
+            for (int sl = 0; sl < 2; ++sl)
+                if (pend_ring & (1u << sl)) tc::mbar_wait(bars + B_RF0 + sl, ring_par[sl], DRAIN_LIMIT);
+        }
+        uint64_t* dbar = bars + (tid == 0 ? B_D0 : B_D1);
+        tc::mma_commit(dbar);
+        tc::mbar_wait(dbar, 0, DRAIN_LIMIT);
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && *abort_flag) dg::flag_status(p.status, DG_DEVCHK_TIMEOUT);
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+template <int S, typename TI>
+int launch_t(const void* v, const void* beta, const void* wk, const void* wq, const void* decay, int dynamic_decay,
+             const void* s_init, void* out, void* s_final, float* err_out, float* s_final_f, int B, int H, int T,
+             int32_t* status, uint32_t wait_limit, cudaStream_t stream) {
+    const int lanes = B * H;
+    CUtensorMap mk, mq, mv;
+    const bool bf = Io<TI>::kBf16 != 0;
+    if (!make_map(&mk, wk, S, T, lanes, bf) || !make_map(&mq, wq, S, T, lanes, bf) || !make_map(&mv, v, DH, T, lanes, bf))
+        return DG_ERR_UNSUPPORTED;
+    TParams prm{beta, decay, s_init, out, s_final, err_out, s_final_f, status, H, T, (T + CH - 1) / CH, dynamic_decay,
+                wait_limit};
+    const size_t smem = TLayout<S>::BYTES + 1024;
+    auto kern = dense_chunk_t_kernel<S, TI>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return dg_host::record_cuda_error(e);
+    kern<<<lanes, 256, smem, stream>>>(mk, mq, mv, prm);
+    return dg_host::check_launch();
+}
+
+template <typename TI>
+int launch_t_slots(int S, const void* v, const void* beta, const void* wk, const void* wq, const void* decay,
+                   int dynamic_decay, const void* s_init, void* out, void* s_final, float* err_out, float* s_final_f,
+                   int B, int H, int T, int32_t* status, uint32_t wl, cudaStream_t stream) {
+    switch (S) {
+    case 128: return launch_t<128, TI>(v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f, B, H, T, status, wl, stream);
+    case 256: return launch_t<256, TI>(v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f, B, H, T, status, wl, stream);
+    case 384: return launch_t<384, TI>(v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f, B, H, T, status, wl, stream);
+    case 512: return launch_t<512, TI>(v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f, B, H, T, status, wl, stream);
+    default: return DG_ERR_UNSUPPORTED;
+    }
+}
+
+}  // namespace
+
+namespace dg_host {
+
+uint32_t wait_limit();
+
+int dense_forward_chunked_t(int dtype, int B, int H, int T, int S, int Dh, const void* v, const void* beta,
+                            const void* wk, const void* wq, const void* decay, int dynamic_decay, const void* s_init,
+                            void* out, void* s_final, float* err_out, float* s_final_f, int32_t* status,
+                            cudaStream_t stream) {
+    if (!((dtype == DG_DTYPE_F16 || dtype == DG_DTYPE_BF16) && Dh == DH && T > 0 &&
+          (S == 128 || S == 256 || S == 384 || S == 512)))
+        return DG_ERR_UNSUPPORTED;
+    const uintptr_t mis = (uintptr_t)v | (uintptr_t)wk | (uintptr_t)wq | (uintptr_t)s_final |
+                          (uintptr_t)(s_final_f ? (void*)s_final_f : s_final);
+    if (mis & 15) return DG_ERR_MISALIGNED;
+    const uint32_t wl = wait_limit();
+    if (dtype == DG_DTYPE_BF16)
+        return launch_t_slots<__nv_bfloat16>(S, v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out,
+                                             s_final_f, B, H, T, status, wl, stream);
+    return launch_t_slots<__half>(S, v, beta, wk, wq, decay, dynamic_decay, s_init, out, s_final, err_out, s_final_f,
+                                  B, H, T, status, wl, stream);
+}
+
+}  // namespace dg_host

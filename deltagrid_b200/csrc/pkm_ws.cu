@@ -85,6 +85,7 @@ struct WsParams {
     int dynamic_decay;
     const int16_t* codes;       // [lanes, T, 64] from pkm_hazard_kernel
     void* saved;                // [lanes, T, A, Dh] rows as gathered at each step, or null
+    uint64_t wait_ns;           // bound of one wait (wall time); 0 gives up without waiting
 };
 
 struct MetaLayout {
@@ -277,16 +278,18 @@ __device__ __forceinline__ bool mbar_try_wait_long(uint64_t* bar, uint32_t parit
         : "memory");
     return ok != 0;
 }
-// Bounded mbarrier wait: gives up when another role aborted or after 2 s of
-// wall time, flagging DG_DEVCHK_TIMEOUT.
+// Bounded mbarrier wait: gives up when another role aborted or after `wait_ns` of
+// wall time (2 s by default; 0 gives up at once), flagging DG_DEVCHK_TIMEOUT.
 __device__ __forceinline__ bool ws_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                        int32_t* status) {
-    if (mbar_try_wait_long(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (true) {
+                                        int32_t* status, uint64_t wait_ns) {
+    if (wait_ns != 0) {
         if (mbar_try_wait_long(bar, parity)) return true;
-        if (*abort_flag) return false;
-        if (globaltimer_ns() - t0 > 2000000000ull) break;
+        const uint64_t t0 = globaltimer_ns();
+        while (true) {
+            if (mbar_try_wait_long(bar, parity)) return true;
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > wait_ns) break;
+        }
     }
     dg::flag_status(status, DG_DEVCHK_TIMEOUT);
     *abort_flag = 1;
@@ -439,7 +442,7 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
         for (int c = 0; c + 2 < nchunks; ++c) {
             // chunk c+2 reuses the buffer of chunk c-1
             if (c >= 1) {
-                const bool ok = ws_wait(mfree + ((c - 1) % NC), ((c - 1) / NC) & 1, abort_flag, p.status);
+                const bool ok = ws_wait(mfree + ((c - 1) % NC), ((c - 1) / NC) & 1, abort_flag, p.status, p.wait_ns);
                 if (!__all_sync(DG_FULL_MASK, ok)) break;
             }
             load_chunk(c + 2);
@@ -452,8 +455,8 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
             const int sl = t % R;
             const int c = t / CHS, ts = t % CHS;
             bool ok = true;
-            if (ts == 0) ok = ws_wait(mfull + (c % NC), (c / NC) & 1, abort_flag, p.status);
-            if (ok && t >= D) ok = ws_wait(done + ((t - D) % R), ((t - D) / R) & 1, abort_flag, p.status);
+            if (ts == 0) ok = ws_wait(mfull + (c % NC), (c / NC) & 1, abort_flag, p.status, p.wait_ns);
+            if (ok && t >= D) ok = ws_wait(done + ((t - D) % R), ((t - D) / R) & 1, abort_flag, p.status, p.wait_ns);
             if (!ok) break;
             const uint8_t* mc = meta + (c % NC) * ML.bytes;
             const int64_t* midx = reinterpret_cast<const int64_t*>(mc + ML.idx) + ts * A;
@@ -500,7 +503,7 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
             const int sl = s % R;
             const int cn = s / CHS, ts = s % CHS;
             const uint8_t* mc = meta + (cn % NC) * ML.bytes;
-            bool ok = ws_wait(full + sl, (s / R) & 1, abort_flag, p.status);
+            bool ok = ws_wait(full + sl, (s / R) & 1, abort_flag, p.status, p.wait_ns);
             if (!__all_sync(DG_FULL_MASK, ok)) break;
             const int16_t* fw = reinterpret_cast<const int16_t*>(mc + ML.code) + ts * 64;
             // rows forwarded from a step another warp of this slice took: that warp must
@@ -516,7 +519,7 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
                     const int d = __ffs(dm) - 1;
                     dm &= dm - 1;
                     const int w = s - d;
-                    ok = ws_wait(dsl + (w % R) * NSL + sli, (w / R) & 1, abort_flag, p.status);
+                    ok = ws_wait(dsl + (w % R) * NSL + sli, (w / R) & 1, abort_flag, p.status, p.wait_ns);
                     ok = __all_sync(DG_FULL_MASK, ok);
                 }
                 if (!ok) break;
@@ -670,6 +673,8 @@ int launch_ws(const WsParams& p, int lanes, cudaStream_t stream) {
 
 namespace dg_host {
 
+uint32_t wait_limit();
+
 size_t pkm_ws_workspace_bytes(int B, int H, int T) { return (size_t)B * H * T * 64 * sizeof(int16_t); }
 
 bool pkm_ws_supports(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
@@ -705,7 +710,10 @@ int pkm_forward_ws(int dtype, int B, int H, int T, int A, int64_t total, int Dh,
     hz<<<hz_grid, HZ_THREADS, hz_smem, stream>>>(idx, codes, status, T, total, D);
     int rc = check_launch();
     if (rc != DG_OK) return rc;
-    WsParams p{v, beta, wk, wq, idx, decay, state, out, status, H, T, A, Dh, parts, total, dynamic_decay, codes, saved};
+    // the default poll budget (2^22) maps to 2 s of waiting; 0 gives up at once
+    const uint64_t wait_ns = (uint64_t)wait_limit() * 2000000000ull / (1ull << 22);
+    WsParams p{v, beta, wk, wq, idx, decay, state, out, status, H, T, A, Dh, parts, total, dynamic_decay, codes, saved,
+               wait_ns};
     if (dtype == DG_DTYPE_F16)
         return PB == 128 ? launch_ws<__half, 128, kDepthFull>(p, lanes, stream)
                          : launch_ws<__half, 64, kDepthHalf>(p, lanes, stream);

@@ -52,7 +52,8 @@ def device_status(device=None, clear: bool = True) -> int:
     """Synchronizes and returns the kernel self-check bits recorded on ``device``.
 
     Bit 0x1 (DG_DEVCHK_INDEX_RANGE) means a PKM slot index was outside
-    [0, total_slots): that row was skipped.
+    [0, total_slots): that row was skipped.  Bit 0x4 (DG_DEVCHK_TIMEOUT) means a
+    bounded wait inside a kernel gave up: that launch's results are invalid.
     """
     device = torch.device(device if device is not None else torch.cuda.current_device())
     if device.type != "cuda":
@@ -63,6 +64,13 @@ def device_status(device=None, clear: bool = True) -> int:
     if clear:
         w.zero_()
     return val
+
+
+def set_wait_limit(polls: int) -> int:
+    """Sets the poll budget of the kernels' bounded waits (dg_set_wait_limit) and returns
+    the previous one.  0 makes every such wait give up at once: the launch then flags
+    DG_DEVCHK_TIMEOUT (0x4) in device_status() and its results are invalid."""
+    return int(_lib.lib().dg_set_wait_limit(int(polls)))
 
 
 def pkm_fused_forward(k: torch.Tensor, q: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
@@ -110,6 +118,6 @@ def dense_fused_forward(k: torch.Tensor, q: torch.Tensor, v: torch.Tensor, beta:
 
 
 __all__ = ["forward", "step", "pkm_step", "pkm_forward", "pkm_forward_algo", "backward", "pkm_backward",
-           "device_status", "pkm_fused_forward", "dense_fused_forward", "DeltaGridError"]
+           "device_status", "set_wait_limit", "pkm_fused_forward", "dense_fused_forward", "DeltaGridError"]
 
 DeltaGridError = _lib.DeltaGridError

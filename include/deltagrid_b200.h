@@ -49,7 +49,10 @@ typedef enum dg_status {
 typedef enum dg_dense_algo {
     DG_DENSE_AUTO = 0,       /* chunkwise tensor-core kernel where it applies, else sequential */
     DG_DENSE_SEQUENTIAL = 1, /* CUDA-core recurrence, S resident for all T (any dtype) */
-    DG_DENSE_CHUNKED_TC = 2  /* chunkwise WY/UT form on tcgen05 (f16/bf16, Dh = 64) */
+    DG_DENSE_CHUNKED_TC = 2, /* chunkwise WY/UT form on tcgen05, state columns on TMEM lanes
+                                (f16/bf16, Dh = 64, slots 128/256/384/512) */
+    DG_DENSE_CHUNKED_TC_ROWS = 3 /* the same algebra with state rows on TMEM lanes (the
+                                    earlier layout; kept as a second GPU reference) */
 } dg_dense_algo;
 
 /* PKM sequence-forward kernel selector for dg_pkm_forward_ex */
@@ -95,6 +98,23 @@ int dg_dense_forward_ex(int dtype, int B, int H, int T, int slots, int dh,
                         const void* decay, int dynamic_decay, const void* s_init,
                         void* out, void* s_final, float* err_out, float* s_final_f,
                         int algo, void* stream);
+
+/* dg_dense_forward_ex with a device status word (or NULL) into which the tensor-core
+ * kernel ORs DG_DEVCHK_TIMEOUT when one of its bounded waits gives up.  Same
+ * reference interface as dg_dense_forward (binding.cpp:36-113). */
+int dg_dense_forward_ex2(int dtype, int B, int H, int T, int slots, int dh,
+                         const void* v, const void* beta, const void* wk, const void* wq,
+                         const void* decay, int dynamic_decay, const void* s_init,
+                         void* out, void* s_final, float* err_out, float* s_final_f,
+                         int32_t* dev_status, int algo, void* stream);
+
+/* Poll budget of the bounded waits inside the tensor-core dense kernel and the
+ * warp-specialised PKM kernel (launches made after the call).  Default 4194304 polls,
+ * seconds of waiting; 0 makes every such wait give up at once, which drives the
+ * kernels' timeout path (DG_DEVCHK_TIMEOUT, results invalid) without a hung wait.
+ * Returns the previous value.  No reference counterpart (the reference kernels have
+ * no waits). */
+unsigned int dg_set_wait_limit(unsigned int polls);
 
 /*
  * Dense single decode step with (batch, head) element strides.

@@ -4,7 +4,8 @@
     python oracle/build_ref_cuda.py
 
 Compiles src/cpp/binding.cpp and src/cpp/delta_kernel.cu where they lie in the
-reference checkout (DELTAGRID_REF, default /root/reference) with
+reference checkout (located by ``oracle/refpath.py``: DELTAGRID_REF, else
+``oracle/reference.cfg``) with
 torch.utils.cpp_extension for sm_100a, under the module name
 ``ref_hsru_delta_cuda`` (binding.cpp:523 registers TORCH_EXTENSION_NAME, so the
 rename needs no source change).  All outputs go to oracle/_ref/, which is
@@ -24,7 +25,9 @@ NAME = "ref_hsru_delta_cuda"
 
 
 def build() -> str:
-    ref = os.environ.get("DELTAGRID_REF", "/root/reference")
+    sys.path.insert(0, HERE)
+    from refpath import reference_root
+    ref = reference_root()
     src = os.path.join(ref, "src", "cpp")
     os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")
     os.environ.setdefault("MAX_JOBS", "8")

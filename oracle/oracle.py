@@ -309,5 +309,9 @@ def ref_f32_time(mode, H, Dh, steps, contexts, slots=0, G0=0, G1=0, topk=0, dyn=
 
 
 def ref_fxp_time(mode, H, Dh, steps, contexts, slots=0, G0=0, G1=0, topk=0, dyn=False):
+    """Seconds for steps x contexts Q16.16 engine steps (contexts spread over the host
+    threads), and the projection-only share."""
     R = ref_lib()
-    return float(R.ref_fxp_time(mode, H, Dh, slots, G0, G1, topk, int(dyn), steps, contexts))
+    proj = ctypes.c_double(0.0)
+    t = R.ref_fxp_time(mode, H, Dh, slots, G0, G1, topk, int(dyn), steps, contexts, ctypes.byref(proj))
+    return float(t), float(proj.value)

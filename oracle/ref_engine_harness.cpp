@@ -319,9 +319,13 @@ double ref_f32_time(int mode, int H, int Dh, int slots, int G0, int G1, int topk
     return std::chrono::duration<double>(t1 - t0).count();
 }
 
-// Same timing for the Q16.16 engine step (deltagrid_fxp.cpp:181-413).
+// Same timing for the Q16.16 engine step (deltagrid_fxp.cpp:181-413).  That engine has
+// no threading of its own, so the contexts (independent batch rows) are spread over the
+// host threads, one context per thread at a time; proj_seconds receives the time of the
+// same number of projection-only calls (qkv/beta projection, out_proj, LayerNorm) spread
+// the same way.
 double ref_fxp_time(int mode, int H, int Dh, int slots, int G0, int G1, int topk, int dyn,
-                    int steps, int contexts) {
+                    int steps, int contexts, double* proj_seconds) {
     std::vector<FxpLayer> layers(contexts);
     std::vector<std::vector<int32_t>> states(contexts);
     for (int c = 0; c < contexts; ++c) {
@@ -333,11 +337,25 @@ double ref_fxp_time(int mode, int H, int Dh, int slots, int G0, int G1, int topk
     Rng r(99);
     for (auto& x : h) x = DG_FLOAT_TO_FXP(r.normal());
     auto t0 = std::chrono::steady_clock::now();
-    for (int s = 0; s < steps; ++s)
-        for (int c = 0; c < contexts; ++c)
+#pragma omp parallel for schedule(static, 1)
+    for (int c = 0; c < contexts; ++c)
+        for (int s = 0; s < steps; ++s)
             dg_memory_layer_step_fxp(&layers[c].ctx, layers[c].mem, h.data(), states[c].data(),
                                      layers[c].ctx.mem_out_buf);
     auto t1 = std::chrono::steady_clock::now();
+    if (proj_seconds) {
+        auto p0 = std::chrono::steady_clock::now();
+#pragma omp parallel for schedule(static, 1)
+        for (int c = 0; c < contexts; ++c)
+            for (int s = 0; s < steps; ++s) {
+                DGFxpContext& x = layers[c].ctx;
+                dg_matmul_fxp(h.data(), layers[c].mem.proj_qkv_beta, nullptr, x.packed_qkvb_buf, 3 * D + H, D);
+                dg_matmul_fxp(x.yt_buf, layers[c].mem.out_proj, nullptr, x.mem_proj_buf, D, D);
+                dg_layernorm_fxp(x.mem_proj_buf, D, layers[c].mem.norm.weight, layers[c].mem.norm.bias, x.mem_out_buf);
+            }
+        auto p1 = std::chrono::steady_clock::now();
+        *proj_seconds = std::chrono::duration<double>(p1 - p0).count();
+    }
     return std::chrono::duration<double>(t1 - t0).count();
 }
 

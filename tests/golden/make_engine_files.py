@@ -1,8 +1,8 @@
 """Generate the engine-file fixtures under tests/golden/engine_files/ from the
 reference itself.
 
-Run where the reference project is importable (default ``/root/reference``;
-override with ``DELTAGRID_REF``) and ``oracle/_ref/libdg_ref_engine.so`` is built
+Run where the reference project is importable (located by ``oracle/refpath.py``:
+``DELTAGRID_REF``, else ``oracle/reference.cfg``) and ``oracle/_ref/libdg_ref_engine.so`` is built
 (``make -C oracle ref``):
 
     python tests/golden/make_engine_files.py
@@ -37,7 +37,10 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 OUT = os.path.join(HERE, "engine_files")
-REF = os.environ.get("DELTAGRID_REF", "/root/reference")
+sys.path.insert(0, os.path.join(REPO, "oracle"))
+from refpath import reference_root  # noqa: E402
+
+REF = reference_root()
 sys.path.insert(0, REF)
 
 from src.models.continuous import DeltaGridContinuous  # noqa: E402  (reference package)

@@ -1,7 +1,7 @@
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
-Run in a checkout where the reference project is importable (default
-``/root/reference``; override with ``DELTAGRID_REF``) and where
+Run in a checkout where the reference project is importable (located by
+``oracle/refpath.py``: ``DELTAGRID_REF``, else ``oracle/reference.cfg``) and where
 ``oracle/_ref/libdg_ref_engine.so`` has been built (``make -C oracle ref``):
 
     python tests/golden/make_golden.py
@@ -38,7 +38,10 @@ import torch.nn.functional as F
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("DELTAGRID_REF", "/root/reference")
+sys.path.insert(0, os.path.join(REPO, "oracle"))
+from refpath import reference_root  # noqa: E402
+
+REF = reference_root()
 sys.path.insert(0, REF)
 sys.path.insert(0, REPO)
 

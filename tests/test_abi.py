@@ -17,7 +17,7 @@ def _declared_symbols():
     for h in glob.glob(os.path.join(REPO, "include", "*.h")):
         src = open(h).read()
         src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-        for m in re.finditer(r"^\s*(?:const\s+)?(?:int|size_t|void|const char\*|char\*)\s*\*?\s*(dg_\w+)\s*\(",
+        for m in re.finditer(r"^\s*(?:const\s+)?(?:unsigned\s+int|int|size_t|void|const char\*|char\*)\s*\*?\s*(dg_\w+)\s*\(",
                              src, flags=re.M):
             names.add(m.group(1))
     return sorted(names)

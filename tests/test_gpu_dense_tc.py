@@ -1,4 +1,6 @@
-"""Chunkwise tensor-core dense forward (tcgen05, algo 2) against the CPU oracle.
+"""Chunkwise tensor-core dense forward (tcgen05) against the CPU oracle, for both
+layouts: state columns on TMEM lanes (algo 2, the default) and state rows on TMEM
+lanes (algo 3, the earlier kernel).
 
 The oracle runs the per-step recurrence with an fp32 state on the storage-quantised
 inputs (delta_kernel.cu:64-121 semantics).  The chunked kernel evaluates the
@@ -21,11 +23,14 @@ if torch.cuda.is_available():
     from deltagrid_b200 import hsru_delta_cuda as ext
 
 TC = 2
+TC_ROWS = 3
+ALGOS = [TC, TC_ROWS]
+AUTO_TC = TC_ROWS      # the tensor-core kernel AUTO picks
 
 
-def _both(d, save=False, storage=O.F16):
+def _both(d, save=False, storage=O.F16, algo=TC):
     g = {n: (t.cuda() if t is not None else None) for n, t in d.items()}
-    r = ext.forward(g["q"], g["k"], g["v"], g["beta"], g["wk"], g["wq"], g["decay"], g["s_init"], save, algo=TC)
+    r = ext.forward(g["q"], g["k"], g["v"], g["beta"], g["wk"], g["wq"], g["decay"], g["s_init"], save, algo=algo)
     s0 = to_np32(d["s_init"]) if d["s_init"] is not None else None
     yo, so, eo = O.dense_forward(to_np32(d["v"]), to_np32(d["beta"]), to_np32(d["wk"]), to_np32(d["wq"]),
                                  to_np32(d["decay"]), s0, want_err=True)
@@ -33,39 +38,76 @@ def _both(d, save=False, storage=O.F16):
 
 
 @pytest.mark.parametrize("S", [128, 256, 384, 512])
-def test_tc_small(S):
+@pytest.mark.parametrize("algo", ALGOS)
+def test_tc_small(algo, S):
     d = dense_inputs(1, 2, 64, S, 64, torch.float16, seed=S)
-    (out, s, _, _), (yo, so, _) = _both(d)
+    (out, s, _, _), (yo, so, _) = _both(d, algo=algo)
     assert rel_err(out.float().cpu().numpy(), yo) < 1e-3
     assert rel_err(s.float().cpu().numpy(), O.round_to(so, O.F16)) < 1e-3
 
 
 @pytest.mark.parametrize("T", [1, 63, 65, 200, 1000])
-def test_tc_ragged_lengths(T):
+@pytest.mark.parametrize("algo", ALGOS)
+def test_tc_ragged_lengths(algo, T):
     d = dense_inputs(2, 2, T, 256, 64, torch.float16, seed=T)
-    (out, s, _, _), (yo, so, _) = _both(d)
+    (out, s, _, _), (yo, so, _) = _both(d, algo=algo)
     assert rel_err(out.float().cpu().numpy(), yo) < 1e-3
     assert rel_err(s.float().cpu().numpy(), O.round_to(so, O.F16)) < 1e-3
 
 
 @pytest.mark.parametrize("dyn,static_decay", [(True, 1.0), (False, 0.999)])
-def test_tc_decay_and_initial_state(dyn, static_decay):
+@pytest.mark.parametrize("algo", ALGOS)
+def test_tc_decay_and_initial_state(algo, dyn, static_decay):
     d = dense_inputs(2, 3, 300, 512, 64, torch.float16, dynamic=dyn, seed=7, s_init=True,
                      static_decay=static_decay)
-    (out, s, err, sf), (yo, so, eo) = _both(d, save=True)
+    (out, s, err, sf), (yo, so, eo) = _both(d, save=True, algo=algo)
     assert rel_err(out.float().cpu().numpy(), yo) < 1e-3
     assert rel_err(s.float().cpu().numpy(), O.round_to(so, O.F16)) < 1e-3
     assert rel_err(sf.cpu().numpy(), so) < 1e-3
     assert rel_err(err.cpu().numpy(), eo) < 1e-3
 
 
-def test_tc_cfg2_geometry_prefix():
+@pytest.mark.parametrize("algo", ALGOS)
+def test_tc_cfg2_geometry_prefix(algo):
     # cfg2 (the second BASELINE config): slots 512, Dh 64, fp16, wk = normalize(k P^T), wq = q P^T;
     # full T = 4096 on 4 lanes so the CPU oracle stays quick
     d = dense_inputs(1, 4, 4096, 512, 64, torch.float16, seed=11)
-    (out, s, _, _), (yo, so, _) = _both(d)
+    (out, s, _, _), (yo, so, _) = _both(d, algo=algo)
     assert rel_err(out.float().cpu().numpy(), yo) < 1e-3
     assert rel_err(s.float().cpu().numpy(), O.round_to(so, O.F16)) < 1e-3
+
+
+def test_tc_layouts_agree():
+    d = dense_inputs(2, 4, 700, 512, 64, torch.float16, dynamic=True, seed=5, s_init=True)
+    g = {n: (t.cuda() if t is not None else None) for n, t in d.items()}
+    a = (g["q"], g["k"], g["v"], g["beta"], g["wk"], g["wq"], g["decay"], g["s_init"])
+    o1, s1, _, _ = ext.forward(*a, algo=TC_ROWS)
+    o2, s2, _, _ = ext.forward(*a, algo=TC)
+    assert rel_err(o2.float().cpu().numpy(), o1.float().cpu().numpy()) < 1e-3
+    assert rel_err(s2.float().cpu().numpy(), s1.float().cpu().numpy()) < 1e-3
+
+
+def test_tc_wait_timeout_flags_status():
+    """With the wait budget set to zero every bounded wait in the kernel gives up at once:
+    the launch must return (no hung wait), flag DG_DEVCHK_TIMEOUT in the device status
+    word, and leave the context usable for the next, normal launch."""
+    d = dense_inputs(1, 2, 200, 256, 64, torch.float16, seed=9)
+    g = {n: (t.cuda() if t is not None else None) for n, t in d.items()}
+    a = (g["q"], g["k"], g["v"], g["beta"], g["wk"], g["wq"], g["decay"])
+    ext.device_status()
+    old = ext.set_wait_limit(0)
+    try:
+        ext.forward(*a, algo=TC)
+        torch.cuda.synchronize()
+    finally:
+        ext.set_wait_limit(old)
+    assert ext.device_status() & 0x4
+    out, s, _, _ = ext.forward(*a, algo=TC)
+    torch.cuda.synchronize()
+    assert ext.device_status() == 0
+    yo, so = O.dense_forward(to_np32(d["v"]), to_np32(d["beta"]), to_np32(d["wk"]), to_np32(d["wq"]),
+                             to_np32(d["decay"]))
+    assert rel_err(out.float().cpu().numpy(), O.round_to(yo, O.F16)) < 1e-3
 
 
 def test_tc_matches_sequential_kernel():
@@ -83,7 +125,7 @@ def test_auto_selects_tc_for_fp16_dh64():
     g = {n: (t.cuda() if t is not None else None) for n, t in d.items()}
     a = (g["q"], g["k"], g["v"], g["beta"], g["wk"], g["wq"], g["decay"])
     o_auto, _, _, _ = ext.forward(*a)
-    o_tc, _, _, _ = ext.forward(*a, algo=TC)
+    o_tc, _, _, _ = ext.forward(*a, algo=AUTO_TC)
     assert torch.equal(o_auto, o_tc)
     with pytest.raises(RuntimeError, match="unsupported"):
         ext.forward(*(t.float() for t in a), algo=TC)
@@ -95,18 +137,20 @@ BF16_TOL = 8e-3
 @pytest.mark.parametrize("S,T,dyn,s_init", [(128, 200, False, False), (256, 1000, True, True),
                                             (512, 333, True, False), (384, 64, False, True),
                                             (256, 1, True, True), (512, 65, False, True)])
-def test_tc_bf16_against_oracle(S, T, dyn, s_init):
+@pytest.mark.parametrize("algo", ALGOS)
+def test_tc_bf16_against_oracle(algo, S, T, dyn, s_init):
     d = dense_inputs(2, 3, T, S, 64, torch.bfloat16, dynamic=dyn, seed=S + T, s_init=s_init)
-    (out, s, err, sf), (yo, so, eo) = _both(d, save=True, storage=O.BF16)
+    (out, s, err, sf), (yo, so, eo) = _both(d, save=True, storage=O.BF16, algo=algo)
     assert out.dtype == torch.bfloat16
     assert rel_err(out.float().cpu().numpy(), yo) < BF16_TOL
     assert rel_err(s.float().cpu().numpy(), O.round_to(so, O.BF16)) < BF16_TOL
     assert rel_err(sf.cpu().numpy(), so) < BF16_TOL
 
 
-def test_tc_bf16_cfg2_geometry_full_length():
+@pytest.mark.parametrize("algo", ALGOS)
+def test_tc_bf16_cfg2_geometry_full_length(algo):
     d = dense_inputs(1, 4, 4096, 512, 64, torch.bfloat16, seed=12)
-    (out, s, _, _), (yo, so, _) = _both(d, storage=O.BF16)
+    (out, s, _, _), (yo, so, _) = _both(d, storage=O.BF16, algo=algo)
     assert rel_err(out.float().cpu().numpy(), yo) < BF16_TOL
     assert rel_err(s.float().cpu().numpy(), O.round_to(so, O.BF16)) < BF16_TOL
 
@@ -116,7 +160,7 @@ def test_auto_selects_tc_for_bf16_dh64():
     g = {n: (t.cuda() if t is not None else None) for n, t in d.items()}
     a = (g["q"], g["k"], g["v"], g["beta"], g["wk"], g["wq"], g["decay"])
     o_auto, _, _, _ = ext.forward(*a)
-    o_tc, _, _, _ = ext.forward(*a, algo=TC)
+    o_tc, _, _, _ = ext.forward(*a, algo=AUTO_TC)
     o_seq, _, _, _ = ext.forward(*a, algo=_lib.ALGO_SEQUENTIAL)
     assert torch.equal(o_auto, o_tc)
     assert rel_err(o_tc.float().cpu().numpy(), o_seq.float().cpu().numpy()) < BF16_TOL

@@ -177,3 +177,21 @@ def test_ws_saved_rows_match_one_step_kernel():
     for a, b in zip(res[WS], res[ONE]):
         assert rel_err(a.numpy(), b.numpy()) < 1e-3
     assert torch.count_nonzero(res[WS][2][1, 2, 7, 5]) == 0
+
+
+def test_ws_wait_timeout_flags_status():
+    """With the wait budget at zero every bounded wait of the warp-specialised kernel gives
+    up at once: the launch returns (no hung wait), DG_DEVCHK_TIMEOUT is flagged, and the next
+    normal launch on the same context is correct."""
+    d = pkm_inputs(1, 2, 128, 16, 8, 64, torch.float16, seed=4)
+    ext.device_status(clear=True)
+    old = ext.set_wait_limit(0)
+    try:
+        _run(d, WS)
+    finally:
+        ext.set_wait_limit(old)
+    assert ext.device_status() & 0x4
+    out, st = _run(d, WS)
+    assert ext.device_status() == 0
+    yo, so = _oracle(d, torch.float16)
+    assert rel_err(out.float().cpu().numpy(), yo) < TOL[torch.float16]
