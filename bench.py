@@ -1,22 +1,32 @@
 """DeltaGrid recurrence benchmark on B200 -- one JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg2] [--impl ours|reference]
+                    [--scaling strong|weak]
 
 A step is one call of the hot path over one batch of synthetic input resident
-in HBM: the dense sequence forward ``hsru_delta_cuda.forward`` (cfg1/cfg2) or the
-PKM sequence forward ``pkm_forward`` (cfg3/cfg4).  The default workload is
-cfg2, the second BASELINE config (dense, B=32 H=16 T=4096 Dh=64 slots=512, fp16 storage,
-fp32 accumulation), the configuration the headline metric is quoted on.
+in HBM: the dense sequence forward ``hsru_delta_cuda.forward`` (cfg1/cfg2/cfg5p),
+the PKM sequence forward ``pkm_forward`` (cfg3/cfg4) or 12 layers of the decode
+``step`` (cfg5).  The default workload is cfg2, the second BASELINE config (dense,
+B=32 H=16 T=4096 Dh=64 slots=512, fp16 storage, fp32 accumulation), the
+configuration the headline metric is quoted on.  At N = 1 the line also carries
+a ``workloads`` record: the same device timing and roofline for cfg1, cfg3,
+cfg4, cfg5 and cfg5p.
 
-Multi-GPU (torchrun, one process per GPU): every rank runs the full per-GPU
-workload on its own batch shard (weak scaling, no collective on the data
-path); the timed region is bracketed by a barrier and device syncs, and the
-reported time is the max over ranks (NCCL all-reduce MAX afterwards).
-Inputs exceed L2 (126 MB), so no flush is needed between iterations.
+Multi-GPU (torchrun, one process per GPU): strong scaling by default -- the
+workload's global batch is split into contiguous batch shards, one per rank,
+with all H heads of a row on its rank (``--scaling weak`` gives every rank the
+full batch instead).  No collective touches the data path; the timed region is
+bracketed by a barrier and device syncs, and the reported time is the max over
+ranks (NCCL all-reduce MAX afterwards).  Inputs exceed L2 (126 MB), so no flush
+is needed between iterations.
 
-``--impl reference`` times the reference's own CPU implementation of the path
-(the C++ engine compiled from the reference sources into oracle/_ref, else the
-oracle port) on the host cores, on rank 0 only.
+``cpu_baseline`` is the reference's own fp32 C++ engine (compiled from the
+reference sources into oracle/_ref), recurrence only, on all host cores.
+
+``--impl reference`` times the reference's own implementations (rank 0 only):
+its fp32 C++ engine on all host cores is the line's value; beside it, named legs
+for its Q16.16 engine, its PyTorch per-step loop and chunk_forward on the CPU,
+and its own CUDA kernel built for sm_100a on this GPU (oracle/ref_legs.py).
 """
 from __future__ import annotations
 
@@ -292,42 +302,98 @@ def cpu_baseline_port(w, threads):
 
 
 def reference_arm(args, w):
-    """Times the reference's own CPU implementation (oracle/_ref engine, else the port)."""
+    """The reference's own implementations of the path (rank 0 only): the fp32 C++
+    engine (recurrence only, all host cores) is the value; the other legs ride along."""
     threads = os.cpu_count() or 1
+    # set explicitly: under torchrun OMP_NUM_THREADS arrives as 1
+    os.environ["OMP_NUM_THREADS"] = str(threads)
     from oracle import oracle as O
+    from oracle import ref_legs as RL
     out = {"metric": METRIC, "unit": UNIT, "higher_is_better": True, "impl": "reference",
            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "dtype": "f32",
-           "data": "synthetic", "config": {"workload": args.workload, **{k: v for k, v in w.items()}}}
+           "data": "synthetic", "config": {"workload": args.workload, **{k: v for k, v in w.items()}},
+           "host": {"cores": threads, "cpu": _cpu_model()}}
+    base = None
     if O.ref_available():
-        os.environ.setdefault("OMP_NUM_THREADS", str(threads))
-        H, Dh = w["H"], w["Dh"]
-        if w["kind"] in ("dense", "decode"):
-            mode = 0 if w["S"] == Dh else 1
-            kw = dict(slots=w["S"]) if mode == 1 else {}
-        else:
-            mode = 2
-            kw = dict(G0=w["G"], G1=w["G"], topk=w["K"])
-        contexts = 1 if w["kind"] == "pkm" and w["G"] >= 1024 else min(w["B"], 4)
-        steps = 8 if w["kind"] in ("dense", "decode") and w["S"] >= 256 else 64
-        per_token = w.get("L", 1)             # decode: a token passes the recurrence of every layer
-        O.ref_f32_time(mode, H, Dh, 2, contexts, **kw)               # warm-up
-        vals, projs = [], []
+        O.set_threads(threads)
+        vals = []
         for _ in range(max(1, args.steps)):
-            t, p = O.ref_f32_time(mode, H, Dh, steps, contexts, **kw)
-            vals.append(contexts * steps / t / per_token)
-            projs.append(p / t)
-        value = statistics.median(vals)
-        sample = (f"reference C++ engine dg_memory_layer_step (deltagrid_math.cpp:174-417), "
-                  f"{contexts} context(s) x {H} heads x {steps} steps per timing, fp32, OpenMP over heads")
-        out.update(value=value, ms_per_step=1e3 * contexts * steps / value,
-                   cpu_baseline=dict(value=value, unit=UNIT, cores=threads, kind="reference", sample=sample),
-                   projection_time_share=statistics.median(projs))
+            base = RL.engine_f32(w, threads, budget_s=0.5)
+            vals.append(base["value"])
+        base["value"] = statistics.median(vals)
+        out.update(value=base["value"], cpu_baseline=base)
     else:
-        cb = cpu_baseline_port(w, threads)
-        out.update(value=cb["value"], cpu_baseline=cb)
+        base = cpu_baseline_port(w, threads)
+        out.update(value=base["value"], cpu_baseline=base)
+    legs = {}
+    for name, fn in (("engine_q16", RL.engine_q16), ("pytorch_loop", RL.pytorch_loop),
+                     ("pytorch_chunk", RL.pytorch_chunk)):
+        try:
+            r = fn(w, threads, budget_s=2.0)
+        except Exception as e:          # a leg that cannot run here is reported, not fatal
+            r = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+        if r is not None:
+            legs[name] = r
+    out["cpu_legs"] = legs
+    try:
+        import torch
+        if torch.cuda.is_available():
+            dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+            torch.cuda.set_device(dev)
+            r = RL.gpu_kernel(w, make_inputs, torch, dev)
+            if r is not None:
+                out["gpu_reference_kernel"] = r
+    except Exception as e:
+        out["gpu_reference_kernel"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
     out["e2e"] = {"value": out["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     out["vs_baseline"] = None
     print(json.dumps(out))
+
+
+def _cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _roofline(w, launch_ms, traffic=None):
+    hbm, _, peak_src = _peaks()
+    bytes_alg, flops_alg = _algorithmic(w)
+    achieved = bytes_alg / (launch_ms / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+            "traffic": traffic, "peak_source": peak_src, "algorithmic_bytes_per_launch": bytes_alg,
+            "launch_ms": launch_ms, "kernels_timed": launches_per_step(w),
+            "tensor_tflops_achieved": flops_alg / (launch_ms / 1e3) / 1e12}
+
+
+def _sub_workload(name, ext, torch, device, steps=5, warmup=3, algo=0):
+    """Device timing and roofline of another workload on this GPU (the `workloads` record)."""
+    w = dict(WORKLOADS[name])
+    d = make_inputs(w, torch, device, seed=1000)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(warmup):
+        run_step(ext, w, d, algo)
+    torch.cuda.synchronize(device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * steps)]
+    with Clocks(device.index) as clk:
+        for i in range(steps):
+            ev[2 * i].record(stream)
+            run_step(ext, w, d, algo)
+            ev[2 * i + 1].record(stream)
+        torch.cuda.synchronize(device)
+    ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(steps)]
+    m = statistics.mean(ms)
+    del d
+    torch.cuda.empty_cache()
+    rl = _roofline(w, m)
+    return {"desc": w["desc"], "ms_per_step": m, "value": w["B"] * w["T"] / (m / 1e3), "unit": UNIT,
+            "roofline": {k: rl[k] for k in ("bound", "achieved", "peak", "unit", "frac", "peak_source",
+                                               "algorithmic_bytes_per_launch", "kernels_timed")},
+            "steps": steps, "clocks": clk.summary()}
 
 
 def main():
@@ -344,6 +410,9 @@ def main():
     ap.add_argument("--seq", type=int, default=0, help="override the sequence length T (small profiling cases)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-workloads", action="store_true", help="skip the other workloads' record (N = 1)")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="strong: the global batch is split over the ranks; weak: every rank runs the full batch")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     w = dict(WORKLOADS[args.workload])
@@ -373,6 +442,12 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
 
+    # this rank's batch shard (strong scaling) or the whole batch (weak)
+    global_B = w["B"] if args.scaling == "strong" else w["B"] * world
+    if args.scaling == "strong" and world > 1:
+        from deltagrid_b200.shard import shard_range
+        b0, b1 = shard_range(w["B"], world, rank)
+        w["B"] = b1 - b0
     d = make_inputs(w, torch, device, seed=1000 + rank)
     stream = torch.cuda.current_stream(device)
 
@@ -409,7 +484,7 @@ def main():
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         total_ms = float(tt.item())
     ms_per_step = total_ms / args.steps
-    tokens_per_step = w["B"] * w["T"] * world
+    tokens_per_step = global_B * w["T"]
     value = tokens_per_step / (ms_per_step / 1e3)
 
     # end to end through the public API: pinned host inputs in, result out, every step
@@ -557,39 +632,52 @@ def main():
     if rank != 0:
         return
 
-    hbm, tflops, peak_src = _peaks()
-    bytes_alg, flops_alg = _algorithmic(w)
     launch_ms = statistics.mean(per_launch_ms)
-    achieved_gbs = bytes_alg / (launch_ms / 1e3) / 1e9
     traffic = None
     tr_file = os.path.join(HERE, "profiles", f"traffic_{args.workload}.txt")
-    if os.path.exists(tr_file):
+    if os.path.exists(tr_file) and w["B"] == WORKLOADS[args.workload]["B"]:
         for line in open(tr_file):
             if line.startswith("dram_bytes_per_launch:"):
                 traffic = float(line.split(":")[1])
-    roofline = {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s",
-                "frac": achieved_gbs / hbm, "traffic": traffic, "peak_source": peak_src,
-                "algorithmic_bytes_per_launch": bytes_alg, "launch_ms": launch_ms,
-                "kernels_timed": launches_per_step(w),
-                "tensor_tflops_achieved": flops_alg / (launch_ms / 1e3) / 1e12}
+    roofline = _roofline(w, launch_ms, traffic)
+
+    del d
+    torch.cuda.empty_cache()
+    workloads = None
+    if world == 1 and not args.no_workloads and args.workload == "cfg2" and args.batch == 0 and args.seq == 0:
+        workloads = {}
+        for name in ("cfg1", "cfg3", "cfg4", "cfg5", "cfg5p"):
+            workloads[name] = _sub_workload(name, ext, torch, device)
 
     cpu = None
     if not args.no_cpu and world == 1:
-        cpu = cpu_baseline_port(w, os.cpu_count() or 1)
+        threads = os.cpu_count() or 1
+        os.environ["OMP_NUM_THREADS"] = str(threads)
+        from oracle import oracle as O
+        cpu = None
+        if O.ref_available():
+            from oracle import ref_legs as RL
+            cpu = RL.engine_f32(WORKLOADS[args.workload], threads, budget_s=3.0)
+        if cpu is None:
+            cpu = cpu_baseline_port(WORKLOADS[args.workload], threads)
+        cpu["host_cpu"] = _cpu_model()
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": {"float16": "f16", "float32": "f32", "bfloat16": "bf16"}[w["dtype"]],
         "data": "synthetic (seeded, BASELINE distributions, resident in HBM; inputs > L2, no flush)",
-        "config": {"workload": f"{args.workload}: {w['desc']}", "global_batch": w["B"] * world,
-                   "per_gpu_batch": w["B"], "seq_len": w["T"], "parallelism": f"dp{world} (batch shards)",
+        "config": {"workload": f"{args.workload}: {WORKLOADS[args.workload]['desc']}", "global_batch": global_B,
+                   "per_gpu_batch": w["B"], "seq_len": w["T"],
+                   "parallelism": f"dp{world} (batch shards, {args.scaling} scaling)",
                    "l2": "inputs larger than L2 (no flush)"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": args.steps * launches_per_step(w),
         "clocks": clk.summary(),
         "verify": {"output_checksums_per_rank": verify},
     }
+    if workloads is not None:
+        line["workloads"] = workloads
     print(json.dumps(line))
 
 

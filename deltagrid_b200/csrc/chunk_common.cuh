@@ -75,17 +75,12 @@ struct ChunkScalars {
     float atot;         // a_{C-1}
 };
 
-template <typename TI>
-__device__ __forceinline__ ChunkScalars chunk_scalars(const TI* beta, const TI* decay, int dyn,
-                                                      float alpha_static, int64_t lane_base, int t0, int T_,
-                                                      int lane) {
+// The scan of chunk_scalars on gate values already in registers (lane l: beta and alpha
+// of steps 2l and 2l+1; alpha = 1 and beta = 0 beyond T).
+__device__ __forceinline__ ChunkScalars gate_scalars(float b0, float b1, float al0, float al1, int lane) {
     ChunkScalars c;
-    const int t = t0 + 2 * lane;
-    const bool ok0 = t < T_, ok1 = t + 1 < T_;
-    const float al0 = ok0 ? (dyn ? dg::to_f(decay[lane_base + t]) : alpha_static) : 1.f;
-    const float al1 = ok1 ? (dyn ? dg::to_f(decay[lane_base + t + 1]) : alpha_static) : 1.f;
-    c.b0 = ok0 ? dg::to_f(beta[lane_base + t]) : 0.f;
-    c.b1 = ok1 ? dg::to_f(beta[lane_base + t + 1]) : 0.f;
+    c.b0 = b0;
+    c.b1 = b1;
     float incl = al0 * al1;              // inclusive scan of pair products over lanes
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -100,6 +95,18 @@ __device__ __forceinline__ ChunkScalars chunk_scalars(const TI* beta, const TI* 
     c.a1 = c.a0 * al1;
     c.atot = __shfl_sync(DG_FULL_MASK, incl, 31);
     return c;
+}
+
+template <typename TI>
+__device__ __forceinline__ ChunkScalars chunk_scalars(const TI* beta, const TI* decay, int dyn,
+                                                      float alpha_static, int64_t lane_base, int t0, int T_,
+                                                      int lane) {
+    const int t = t0 + 2 * lane;
+    const bool ok0 = t < T_, ok1 = t + 1 < T_;
+    const float al0 = ok0 ? (dyn ? dg::to_f(decay[lane_base + t]) : alpha_static) : 1.f;
+    const float al1 = ok1 ? (dyn ? dg::to_f(decay[lane_base + t + 1]) : alpha_static) : 1.f;
+    return gate_scalars(ok0 ? dg::to_f(beta[lane_base + t]) : 0.f, ok1 ? dg::to_f(beta[lane_base + t + 1]) : 0.f,
+                        al0, al1, lane);
 }
 // value of step i from the pair registers (all lanes must call)
 __device__ __forceinline__ float pick(float v0, float v1, int i) {
