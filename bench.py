@@ -404,7 +404,8 @@ def main():
     ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--algo", type=int, default=0,
-                    help="kernel selector: dense 0 auto, 1 sequential, 2 chunked tcgen05; "
+                    help="kernel selector: dense 0 auto, 1 sequential, 2 chunked tcgen05 (state columns on TMEM "
+                         "lanes), 3 chunked tcgen05 (state rows on TMEM lanes); "
                          "PKM 0 auto, 1 one step, 2 pipelined, 3 warp-specialised")
     ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (small profiling cases)")
     ap.add_argument("--seq", type=int, default=0, help="override the sequence length T (small profiling cases)")

@@ -103,10 +103,10 @@ int dg_dense_forward_ex2(int dtype, int B, int H, int T, int slots, int dh, cons
     if (T == 0) algo = DG_DENSE_SEQUENTIAL;
     const bool tc_ok = dense_chunked_tc_supports(dtype, B, H, T, slots, dh);
     if ((algo == DG_DENSE_CHUNKED_TC || algo == DG_DENSE_CHUNKED_TC_ROWS) && !tc_ok) return DG_ERR_UNSUPPORTED;
-    if (algo == DG_DENSE_CHUNKED_TC)
+    if (algo == DG_DENSE_CHUNKED_TC || (algo == DG_DENSE_AUTO && tc_ok))
         return dense_forward_chunked_t(dtype, B, H, T, slots, dh, v, beta, wk, wq, decay, dynamic_decay, s_init,
                                        out, s_final, err_out, s_final_f, dev_status, s);
-    if (algo == DG_DENSE_CHUNKED_TC_ROWS || (algo == DG_DENSE_AUTO && tc_ok))
+    if (algo == DG_DENSE_CHUNKED_TC_ROWS)
         return dense_forward_chunked_tc(dtype, B, H, T, slots, dh, v, beta, wk, wq, decay,
                                         dynamic_decay, s_init, out, s_final, err_out, s_final_f, s);
     if (algo != DG_DENSE_AUTO && algo != DG_DENSE_SEQUENTIAL) return DG_ERR_INVALID_ARGUMENT;

@@ -25,7 +25,7 @@ if torch.cuda.is_available():
 TC = 2
 TC_ROWS = 3
 ALGOS = [TC, TC_ROWS]
-AUTO_TC = TC_ROWS      # the tensor-core kernel AUTO picks
+AUTO_TC = TC           # the tensor-core kernel AUTO picks
 
 
 def _both(d, save=False, storage=O.F16, algo=TC):

@@ -1,0 +1,152 @@
+"""deltagrid_b200.layer.DeltaGridLayer -- the repository's inference/training layer on
+the B200 kernels -- against the reference layer and the CPU oracle.
+
+* Parameters: same names and shapes as the reference DeltaGridLayer
+  (src/modules/memory.py:135-226), so one state_dict loads into both (CPU test).
+* Sparse Delta-PKM inference at the cfg3 shape (B=16, H=8, 128 x 128 slots, top-8,
+  Dh=64, fp16 state of 256 MiB): the fused router and the sequence kernel on the
+  caller's state in place.  Checked against the oracle router and recurrence fed the
+  layer's own projections, that the returned state is the tensor passed in, and that
+  the call's peak allocation stays far below one state (no clone, no compaction, no
+  saved rows; memory.py:452-464 and _autograd.py:93-133 make all three).
+* Dense and PKM forward, step and training gradients against the reference layer
+  running on this drop-in with the same weights.
+Bars, max|a-b|/max|b|: 1e-3 for fp16 results, 1e-4 for fp32 forward results and
+gradients (the two layers' torch code runs the same ops; the recurrence is the same
+kernel or, for routing, the exact router against torch's GEMM top-k).
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err
+from oracle import oracle as O
+from oracle.reference_pkg import load_reference_package, use_backend
+
+DG = load_reference_package()
+need_ref = pytest.mark.skipif(DG is None, reason="reference package (baseline/_ref) absent")
+
+
+def _pair(seed=0, **kw):
+    from deltagrid_b200.layer import DeltaGridLayer
+    torch.manual_seed(seed)
+    ref = DG.modules.memory.DeltaGridLayer(**kw)
+    ours = DeltaGridLayer(**kw)
+    ours.load_state_dict(ref.state_dict())
+    return ref, ours
+
+
+@need_ref
+@pytest.mark.parametrize("kw", [dict(d_model=128, num_heads=2, num_slots=256),
+                                dict(d_model=128, num_heads=2, grid_dim=(16, 16), top_k=4),
+                                dict(d_model=64, num_heads=2, grid_dim=(4, 8), dynamic_decay=False)])
+def test_state_dict_interchange(kw):
+    ref, ours = _pair(**kw)
+    a, b = ref.state_dict(), ours.state_dict()
+    assert list(a) == list(b)
+    for n in a:
+        assert a[n].shape == b[n].shape and torch.equal(a[n], b[n]), n
+
+
+@pytest.mark.gpu
+def test_pkm_inference_cfg3_shape_in_place():
+    from deltagrid_b200.layer import DeltaGridLayer
+    torch.manual_seed(3)
+    B, H, T, G, K, Dh = 16, 8, 128, 128, 8, 64
+    layer = DeltaGridLayer(d_model=H * Dh, num_heads=H, grid_dim=(G, G), top_k=K).cuda().half().eval()
+    x = torch.randn(B, T, H * Dh, device="cuda").half()
+    state = torch.zeros(B, H, G * G, Dh, device="cuda", dtype=torch.float16)
+    state_bytes = state.numel() * state.element_size()
+    with torch.no_grad():
+        layer.requires_grad_(False)
+        q, k, v, beta, decay = layer._project(x)
+        torch.cuda.synchronize()
+        torch.cuda.reset_peak_memory_stats()
+        base = torch.cuda.memory_allocated()
+        out, st = layer(x, state)
+        torch.cuda.synchronize()
+        peak = torch.cuda.max_memory_allocated() - base
+    assert st.data_ptr() == state.data_ptr()
+    assert peak < 0.25 * state_bytes, (peak, state_bytes)
+    # the oracle fed the same projections: routing (exact, sequential fp32) then the recurrence
+    kq = lambda t: t.float().cpu().numpy()
+    wts = [p.weight.float().cpu().numpy() for p in (*layer.axes_proj_k, *layer.axes_proj_q)]
+    wk, wq, idx, _ = O.pkm_route(kq(k), kq(q), *wts, K, layer.q_scale.float().cpu().numpy()[:, None])
+    wk, wq = O.round_to(wk, O.F16), O.round_to(wq, O.F16)
+    dec = decay.half().float().cpu().numpy()
+    yo, so = O.pkm_forward(kq(v), kq(beta.squeeze(-1).half()), wk, wq, idx, dec,
+                           np.zeros((B, H, G * G, Dh), np.float32), O.F16)
+    # y before out_proj: recompute the layer's readout from the oracle's y
+    y_ref = torch.from_numpy(O.round_to(yo, O.F16)).cuda().half().transpose(1, 2).reshape(B, T, H * Dh)
+    with torch.no_grad():
+        out_ref = layer.norm(layer.out_proj(y_ref))
+    assert rel_err(st.float().cpu().numpy(), so) < 1e-3
+    assert rel_err(out.float().cpu().numpy(), out_ref.float().cpu().numpy()) < 1e-2
+
+
+@pytest.mark.gpu
+@need_ref
+@pytest.mark.parametrize("dtype,kw", [
+    (torch.float32, dict(d_model=128, num_heads=2, num_slots=256)),
+    (torch.float16, dict(d_model=128, num_heads=2, num_slots=512, dynamic_decay=False)),
+    (torch.float32, dict(d_model=64, num_heads=2, grid_dim=(4, 8))),
+])
+def test_dense_forward_and_step_match_reference_layer(dtype, kw):
+    from deltagrid_b200 import hsru_delta_cuda as ext
+    ref, ours = _pair(seed=1, **kw)
+    ref, ours = ref.cuda().to(dtype).eval(), ours.cuda().to(dtype).eval()
+    use_backend(ext)
+    x = torch.randn(2, 80, kw["d_model"], device="cuda").to(dtype)
+    with torch.no_grad():
+        ro, rs = ref(x)
+        mo, ms = ours(x)
+        tol = 1e-4 if dtype == torch.float32 else 1e-3
+        assert rel_err(mo.float().cpu(), ro.float().cpu()) < tol
+        assert rel_err(ms.float().cpu(), rs.float().cpu()) < tol
+        xs = torch.randn(2, 1, kw["d_model"], device="cuda").to(dtype)
+        r1, rs1 = ref.step(xs, rs)
+        m1, ms1 = ours.step(xs, ms)
+        assert rel_err(m1.float().cpu(), r1.float().cpu()) < tol
+        assert rel_err(ms1.float().cpu(), rs1.float().cpu()) < tol
+
+
+@pytest.mark.gpu
+@need_ref
+def test_pkm_forward_and_step_match_reference_layer():
+    from deltagrid_b200 import hsru_delta_cuda as ext
+    ref, ours = _pair(seed=2, d_model=128, num_heads=2, grid_dim=(32, 32), top_k=8)
+    ref, ours = ref.cuda().float().eval(), ours.cuda().float().eval()
+    use_backend(ext)
+    x = torch.randn(2, 64, 128, device="cuda")
+    with torch.no_grad():
+        s0 = 0.1 * torch.randn(2, 2, 1024, 64, device="cuda")
+        ro, rs = ref(x, s0.clone())
+        mo, ms = ours(x, s0.clone())
+        assert rel_err(mo.cpu(), ro.cpu()) < 1e-4
+        assert rel_err(ms.cpu(), rs.cpu()) < 1e-4
+        xs = torch.randn(2, 1, 128, device="cuda")
+        r1, rs1 = ref.step(xs, rs.clone())
+        m1, ms1 = ours.step(xs, ms.clone())
+        assert rel_err(m1.cpu(), r1.cpu()) < 1e-4
+        assert rel_err(ms1.cpu(), rs1.cpu()) < 1e-4
+
+
+@pytest.mark.gpu
+@need_ref
+@pytest.mark.parametrize("kw", [dict(d_model=128, num_heads=2, num_slots=128),
+                                dict(d_model=128, num_heads=2, grid_dim=(16, 16), top_k=4)])
+def test_training_gradients_match_reference_layer(kw):
+    from deltagrid_b200 import hsru_delta_cuda as ext
+    ref, ours = _pair(seed=4, **kw)
+    ref, ours = ref.cuda().float(), ours.cuda().float()
+    use_backend(ext)
+    x = torch.randn(2, 48, 128, device="cuda", requires_grad=True)
+    for m in (ref, ours):
+        out, st = m(x)
+        (out.square().mean() + 0.1 * st.float().square().mean()).backward()
+    gr = dict(ref.named_parameters())
+    for n, p in ours.named_parameters():
+        if p.grad is None:
+            assert gr[n].grad is None or float(gr[n].grad.abs().max()) == 0.0, n
+            continue
+        assert rel_err(p.grad.cpu(), gr[n].grad.cpu()) < 1e-4, n
