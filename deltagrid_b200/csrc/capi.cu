@@ -8,6 +8,21 @@ static unsigned int g_wait_limit = 1u << 22;
 
 uint32_t wait_limit() { return __atomic_load_n(&g_wait_limit, __ATOMIC_RELAXED); }
 
+// per-device multiprocessor counts (0 = not yet queried; the count is never 0)
+static int g_sm_count[64];
+
+int sm_count(int device, int* out) {
+    if (device < 0 || device >= 64) return DG_ERR_UNSUPPORTED;
+    int n = __atomic_load_n(&g_sm_count[device], __ATOMIC_RELAXED);
+    if (n == 0) {
+        cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        __atomic_store_n(&g_sm_count[device], n, __ATOMIC_RELAXED);
+    }
+    *out = n;
+    return DG_OK;
+}
+
 int record_cuda_error(cudaError_t e) {
     g_last_cuda_error = (int)e;
     return DG_ERR_CUDA;
@@ -103,7 +118,12 @@ int dg_dense_forward_ex2(int dtype, int B, int H, int T, int slots, int dh, cons
     if (T == 0) algo = DG_DENSE_SEQUENTIAL;
     const bool tc_ok = dense_chunked_tc_supports(dtype, B, H, T, slots, dh);
     if ((algo == DG_DENSE_CHUNKED_TC || algo == DG_DENSE_CHUNKED_TC_ROWS) && !tc_ok) return DG_ERR_UNSUPPORTED;
-    if (algo == DG_DENSE_CHUNKED_TC || (algo == DG_DENSE_AUTO && tc_ok))
+    // AUTO keeps bf16 states of more than 256 slots on the sequential kernel: there the
+    // tensor-core kernels take single bf16 copies of the state and residual operands,
+    // ~2e-3 from an fp32-state recurrence, outside the 1e-3 bar (at <= 256 slots the
+    // default kernel carries them as bf16 hi + lo pairs)
+    const bool tc_auto = tc_ok && !(dtype == DG_DTYPE_BF16 && slots > 256);
+    if (algo == DG_DENSE_CHUNKED_TC || (algo == DG_DENSE_AUTO && tc_auto))
         return dense_forward_chunked_t(dtype, B, H, T, slots, dh, v, beta, wk, wq, decay, dynamic_decay, s_init,
                                        out, s_final, err_out, s_final_f, dev_status, s);
     if (algo == DG_DENSE_CHUNKED_TC_ROWS)

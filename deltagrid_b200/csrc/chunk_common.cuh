@@ -35,6 +35,14 @@ template <> struct Io<__nv_bfloat16> {
         return *reinterpret_cast<uint32_t*>(&h);
     }
     __device__ static float2 unpack2(uint32_t u) { return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u)); }
+    // the bf16 pair of what pack2 leaves out: a = hi + lo with both halves bf16, so a
+    // product taken over hi and lo separately sees ~16 significant bits of a
+    __device__ static uint32_t pack2_lo(float a, float b) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        const float2 hf = __bfloat1622float2(h);
+        __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+        return *reinterpret_cast<uint32_t*>(&l);
+    }
 };
 constexpr int LDT = 68;                 // fp32 row stride of the L/T scratch
 

@@ -37,6 +37,11 @@
 //
 // Inputs fp16 or bf16 (kind::f16: both operands of one MMA share a type, so the S0 and R'
 // copies are in the input type; T, X, beta R and Mqk are formed here and are fp16).
+// With bf16 inputs and slots <= 256 the S0 and R' copies are each a bf16 pair hi + lo
+// (the lo half is the rounding residue of the hi half) and [K;Q] S0 and the update take
+// two MMAs per step, one per half: ~16 significant bits of the state and residual reach
+// the products instead of bf16's 8.  (At 384 and 512 slots the lo half of S0 does not
+// fit the TMEM the copy may use; there a single bf16 copy is taken.)
 // Dh = 64, slots in {128, 256, 384, 512}.  Every wait is bounded (a launch parameter);
 // one that gives up flags DG_DEVCHK_TIMEOUT, and the CTA drains the copies and MMAs it
 // issued, frees its TMEM and returns.
@@ -65,7 +70,7 @@ struct TParams {
     uint32_t wait_limit;   // polls of a bounded wait (each at most ~1 us); 0 gives up at once
 };
 
-template <int S>
+template <int S, bool HILO>
 struct TLayout {
     static constexpr int NSL = S / 64;
     static constexpr uint32_t KQ = 0;                       // this chunk's [K;Q] slices
@@ -73,14 +78,15 @@ struct TLayout {
     static constexpr uint32_t TT = RING + NRING * 8192;     // T (rows i, K-major)
     static constexpr uint32_t MQ = TT + 8192;               // Mqk (rows j, MN-major)
     static constexpr uint32_t RT = MQ + 8192;               // R'^T (rows d, K-major); then the y tile (rows t)
-    static constexpr uint32_t VT = RT + 8192;               // V (rows t, TMA)
+    static constexpr uint32_t RL = RT + 8192;               // R'^T lo half (HILO)
+    static constexpr uint32_t VT = RL + (HILO ? 8192 : 0);  // V (rows t, TMA)
     static constexpr uint32_t LT = VT + 8192;               // fp32 [64][68] inverse scratch
     static constexpr uint32_t SC0 = LT + 64 * 68 * 4;       // WG0: aprev, beta, a_end / a, 1 / a, atot; two chunks
     static constexpr uint32_t SC1 = SC0 + 2 * 5 * 64 * 4;   // WG1: aprev, beta / a, 1 / a; two chunks
     static constexpr uint32_t BAR = SC1 + 2 * 3 * 64 * 4;   // mbarriers, TMEM base, abort flag
     static constexpr uint32_t BYTES = BAR + 40 * 8 + 16;
     // TMEM columns (lane offset 0 unless stated)
-    static constexpr uint32_t A0 = 0;          // S0^T copy, S / 2 columns, live during P2
+    static constexpr uint32_t A0 = 0;          // S0^T copy, S / 2 columns (lo half after it: HILO), live during P2
     static constexpr uint32_t XA = 0;          // X^T (P3 A), 32 columns, after P2
     static constexpr uint32_t D3 = 32;         // R^T, 64
     static constexpr uint32_t BA = 96;         // (beta R)^T (P4 A), 32
@@ -90,7 +96,8 @@ struct TLayout {
     static constexpr uint32_t D5 = 448;        // this chunk's K Q^T, 64
     // the state S^T: lane offset 16, columns [0, S)
 };
-static_assert(TLayout<512>::BYTES + 1024 <= 232448, "shared memory");
+static_assert(TLayout<512, false>::BYTES + 1024 <= 232448, "shared memory");
+static_assert(TLayout<256, true>::BYTES + 1024 <= 232448, "shared memory");
 
 enum Bars {
     B_K = 0, B_Q, B_V,                       // TMA: this chunk's K, Q, V
@@ -134,7 +141,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     dense_chunk_t_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmq,
                          const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmy,
                          TParams p) {
-    using Ly = TLayout<S>;
+    constexpr bool HILO = Io<TI>::kBf16 != 0 && S <= 256;
+    using Ly = TLayout<S, HILO>;
     constexpr int NSL = Ly::NSL;
     constexpr int NG = NSL / 2;              // S0^T copy groups of 128 slots
     extern __shared__ uint8_t smem_raw[];
@@ -144,6 +152,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint8_t* tt = sm + Ly::TT;
     uint8_t* mqt = sm + Ly::MQ;
     uint8_t* rt = sm + Ly::RT;
+    uint8_t* rl = sm + Ly::RL;
     uint8_t* vt = sm + Ly::VT;
     uint8_t* yt = rt;
     float* lt = reinterpret_cast<float*>(sm + Ly::LT);
@@ -234,6 +243,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int i = 0; i < 16; ++i) pk[i] = Io<TI>::pack2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
                 tc::tmem_st16x2_16(tq0 + Ly::A0 + 64 * g2 + 32, pk);
+                if constexpr (HILO) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        pk[i] = Io<TI>::pack2_lo(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+                    tc::tmem_st16x2_16(tq0 + Ly::A0 + S / 2 + 64 * g2, pk);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        pk[i] = Io<TI>::pack2_lo(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+                    tc::tmem_st16x2_16(tq0 + Ly::A0 + S / 2 + 64 * g2 + 32, pk);
+                }
                 if (atot != 1.f) {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
@@ -288,12 +307,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {
                     const int t = cb + 8 * cc;
-                    uint32_t w[4];
+                    float rp[8];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        w[e] = Io<TI>::pack2(sc0[128 + t + 2 * e] * sc0[64 + t + 2 * e] * rr[8 * cc + 2 * e],
-                                             sc0[128 + t + 2 * e + 1] * sc0[64 + t + 2 * e + 1] * rr[8 * cc + 2 * e + 1]);
-                    *reinterpret_cast<uint4*>(rt + tc::sw128(row, 4 * half + cc)) = make_uint4(w[0], w[1], w[2], w[3]);
+                    for (int e = 0; e < 8; ++e) rp[e] = sc0[128 + t + e] * sc0[64 + t + e] * rr[8 * cc + e];
+                    *reinterpret_cast<uint4*>(rt + tc::sw128(row, 4 * half + cc)) =
+                        make_uint4(Io<TI>::pack2(rp[0], rp[1]), Io<TI>::pack2(rp[2], rp[3]),
+                                   Io<TI>::pack2(rp[4], rp[5]), Io<TI>::pack2(rp[6], rp[7]));
+                    if constexpr (HILO)
+                        *reinterpret_cast<uint4*>(rl + tc::sw128(row, 4 * half + cc)) =
+                            make_uint4(Io<TI>::pack2_lo(rp[0], rp[1]), Io<TI>::pack2_lo(rp[2], rp[3]),
+                                       Io<TI>::pack2_lo(rp[4], rp[5]), Io<TI>::pack2_lo(rp[6], rp[7]));
                 }
 #pragma unroll
                 for (int i = 0; i < 16; ++i)
@@ -485,9 +508,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const int g = 2 * grp + gg;
-                        tc::mma_f16_ts(tmem + Ly::D2, tmem + Ly::A0 + 32 * g + 8 * kk,
-                                       tc::make_desc(tc::smem_u32(kq + g * SLICE) + 32 * kk, 16, 1024),
-                                       idesc_in<TI>(128, 0), (g | kk) != 0);
+                        const uint64_t bd = tc::make_desc(tc::smem_u32(kq + g * SLICE) + 32 * kk, 16, 1024);
+                        tc::mma_f16_ts(tmem + Ly::D2, tmem + Ly::A0 + 32 * g + 8 * kk, bd, idesc_in<TI>(128, 0),
+                                       (g | kk) != 0);
+                        if constexpr (HILO)
+                            tc::mma_f16_ts(tmem + Ly::D2, tmem + Ly::A0 + S / 2 + 32 * g + 8 * kk, bd,
+                                           idesc_in<TI>(128, 0), 1u);
                     }
             }
             if (!ok) break;
@@ -527,10 +553,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int nt = 0; nt < (S + 255) / 256; ++nt) {
                 const int n = (S - 256 * nt) >= 256 ? 256 : S - 256 * nt;
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    tc::mma_f16(tmem + LANE16 + 256 * nt, tc::make_desc(tc::smem_u32(rt) + 32 * kk, 16, 1024),
-                                tc::make_desc(tc::smem_u32(kq + 4 * nt * SLICE) + kk * 2048, SLICE, 1024),
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t bd = tc::make_desc(tc::smem_u32(kq + 4 * nt * SLICE) + kk * 2048, SLICE, 1024);
+                    tc::mma_f16(tmem + LANE16 + 256 * nt, tc::make_desc(tc::smem_u32(rt) + 32 * kk, 16, 1024), bd,
                                 idesc_in<TI>(n, 1), 1u);
+                    if constexpr (HILO)
+                        tc::mma_f16(tmem + LANE16 + 256 * nt, tc::make_desc(tc::smem_u32(rl) + 32 * kk, 16, 1024), bd,
+                                    idesc_in<TI>(n, 1), 1u);
+                }
             }
             tc::mma_commit(bars + B_P5);
             ok = wait_bar(bars + B_MD, par, lim, abort_flag);
@@ -642,7 +672,7 @@ int launch_t(const void* v, const void* beta, const void* wk, const void* wq, co
         return DG_ERR_UNSUPPORTED;
     TParams prm{v, beta, decay, s_init, s_final, err_out, s_final_f, status, H, T, (T + CH - 1) / CH, dynamic_decay,
                 wait_limit};
-    const size_t smem = TLayout<S>::BYTES + 1024;
+    const size_t smem = TLayout<S, Io<TI>::kBf16 != 0 && S <= 256>::BYTES + 1024;
     auto kern = dense_chunk_t_kernel<S, TI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return dg_host::record_cuda_error(e);

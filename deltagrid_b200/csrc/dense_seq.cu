@@ -243,10 +243,12 @@ int launch_seq(DenseSeqParams p, cudaStream_t stream) {
     // Each chunk costs a round trip to stage its inputs.  When the grid fits in one wave
     // (a CTA per SM at most), shared memory is not shared between CTAs, so chunks grow
     // to 200 KB and up to 256 steps; otherwise 96 KB keeps two CTAs per SM.
-    int dev = 0, nsm = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-        nsm = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return dg_host::record_cuda_error(e);
+    int nsm = 0;
+    const int rc = dg_host::sm_count(dev, &nsm);
+    if (rc != DG_OK) return rc;
     const int64_t ctas = (int64_t)((p.Dh + CW - 1) / CW) * p.B * p.H;
     const bool one_wave = ctas <= nsm;
     const size_t kSmemBudget = (one_wave ? 200 : 96) * 1024;

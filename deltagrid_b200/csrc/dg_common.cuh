@@ -62,6 +62,8 @@ inline int check_launch() {
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? DG_OK : record_cuda_error(e);
 }
+// multiprocessor count of a device, queried once per device and cached
+int sm_count(int device, int* out);
 inline size_t dtype_size(int dtype) {
     switch (dtype) {
     case DG_DTYPE_F32: return 4;

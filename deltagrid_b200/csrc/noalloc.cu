@@ -12,11 +12,15 @@
 // The only scratch any PKM kernel here uses is the warp-specialised kernel's
 // per-row hazard codes (B*H*T*64 int16, written in full by its pre-pass before
 // they are read, so nothing in the array has to start at zero).  The array is a
-// file-scope __device__ object of kNoAllocBytes.  Set-up: the first call of this
-// entry point on a device, with that device current, looks up the array's
-// address there (cudaGetSymbolAddress, return code checked) and caches it; that
-// first call should come before any stream capture.  Calls whose scratch need
-// exceeds the array are rejected with DG_ERR_WORKSPACE before any launch.
+// file-scope __device__ object of kNoAllocBytes.  Set-up: every call made outside
+// stream capture, with the device current, looks up the array's address there
+// (cudaGetSymbolAddress, return code checked; cheap once the module is loaded) and
+// caches it per device; a call made while its stream is capturing uses the cached
+// address, so the first call on a device should come before any stream capture.
+// Looking the address up again outside capture means that a device reset, which can
+// reload the module at another address, leaves no stale address behind for later
+// uncaptured calls.  Calls whose scratch need exceeds the array are rejected with
+// DG_ERR_WORKSPACE before any launch.
 // Calls that overlap in time on one device share the array and race: the
 // caller serializes them (one stream, or events between streams).
 #include <mutex>
@@ -34,14 +38,18 @@ std::mutex g_mu;
 void* g_addr[kMaxDevices];       // device address of g_noalloc_scratch per device, set once
 bool g_addr_set[kMaxDevices];
 
-// address of the scratch array on the current device (looked up once per device)
-int scratch_address(void** out) {
+// address of the scratch array on the current device: looked up on every call outside
+// stream capture, taken from the per-device cache under capture
+int scratch_address(cudaStream_t stream, void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return dg_host::record_cuda_error(e);
     if (dev < 0 || dev >= kMaxDevices) return DG_ERR_UNSUPPORTED;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(stream, &cs);
+    if (e != cudaSuccess) return dg_host::record_cuda_error(e);
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_addr_set[dev]) {
+    if (cs == cudaStreamCaptureStatusNone || !g_addr_set[dev]) {
         void* a = nullptr;
         e = cudaGetSymbolAddress(&a, g_noalloc_scratch);
         if (e != cudaSuccess) return dg_host::record_cuda_error(e);
@@ -69,10 +77,10 @@ int dg_pkm_forward_noalloc(int dtype, int B, int H, int T, int active, int64_t t
                            int32_t* dev_status, void* stream) {
     const size_t need = dg_pkm_forward_workspace_size(dtype, B, H, T, active, total_slots, dh, DG_PKM_AUTO);
     if (need > kNoAllocBytes) return DG_ERR_WORKSPACE;
-    // the set-up runs on the first call on a device whether or not this call
-    // needs scratch, so a later call (possibly under capture) only reads the cache
+    // the look-up runs whether or not this call needs scratch, so that the cache is set
+    // before any call made under capture
     void* addr = nullptr;
-    const int rc = scratch_address(&addr);
+    const int rc = scratch_address(static_cast<cudaStream_t>(stream), &addr);
     if (rc != DG_OK) return rc;
     void* ws = need ? addr : nullptr;
     return dg_pkm_forward_ex(dtype, B, H, T, active, total_slots, dh, v, beta, wk, wq, idx, decay, dynamic_decay,

@@ -47,7 +47,8 @@ typedef enum dg_status {
 
 /* dense-forward algorithm selector for dg_dense_forward_ex */
 typedef enum dg_dense_algo {
-    DG_DENSE_AUTO = 0,       /* chunkwise tensor-core kernel where it applies, else sequential */
+    DG_DENSE_AUTO = 0,       /* chunkwise tensor-core kernel where it applies (f16; bf16 up to
+                                256 slots), else sequential */
     DG_DENSE_SEQUENTIAL = 1, /* CUDA-core recurrence, S resident for all T (any dtype) */
     DG_DENSE_CHUNKED_TC = 2, /* chunkwise WY/UT form on tcgen05, state columns on TMEM lanes
                                 (f16/bf16, Dh = 64, slots 128/256/384/512) */
@@ -213,9 +214,12 @@ int dg_pkm_backward(int dtype, int B, int H, int T, int active, int64_t total_sl
  * whose memory is reserved up front and must not grow or fragment between
  * requests, or code under a memory manager or in a context that forbids
  * allocation.  Scratch comes from a fixed 16 MiB device array inside this
- * library.  Set-up: the first call on a device (that device current) looks up
- * the array's address there and caches it, so make that first call before any
- * stream capture.  Calls needing more scratch than the array holds
+ * library.  Set-up: every call made outside stream capture (its device current)
+ * looks up the array's address there and caches it; a call made under capture uses
+ * the cached address, so make the first call on a device before any stream capture.
+ * A device reset can move the array; the next uncaptured call picks up its new
+ * address (a capture recorded before the reset holds the old one).  Calls needing
+ * more scratch than the array holds
  * (dg_pkm_forward_workspace_size > 16 MiB, i.e. B*H*T > 131072 on the
  * warp-specialised kernel) return DG_ERR_WORKSPACE without launching.  Calls that
  * overlap in time on one device share the array and race: serialize them. */

@@ -66,6 +66,25 @@ def test_sequential_shapes(dtype, S, Dh):
     assert rel_err(s.float().cpu().numpy(), so) < TOL[dtype]
 
 
+@pytest.mark.parametrize("B,H,T,S,dyn,s_init", [
+    (16, 16, 200, 64, False, False),    # 256 lanes: more CTAs than SMs (64-step chunks), ragged last chunk
+    (2, 2, 300, 64, True, True),        # one wave (256-step chunks): per-step decay and s_init across chunks
+    (2, 3, 333, 48, True, False),       # padded slots, several chunks
+    (1, 2, 300, 1000, False, True),     # padded slots beyond 512, several chunks
+])
+def test_sequential_chunk_boundaries(B, H, T, S, dyn, s_init):
+    """The sequential kernel stages inputs in chunks of up to 256 steps (64 when the grid
+    spans more than one wave) and carries the next step's key prediction across the
+    chunk boundary: multi-chunk runs on both staging sizes, ragged last chunks,
+    per-step decay and an initial state crossing the boundaries, padded slot counts."""
+    d = dense_inputs(B, H, T, S, 64, torch.float32, dynamic=dyn, seed=B * H + T + S, s_init=s_init,
+                     static_decay=0.999)
+    out, s, _, _ = _run(d, torch.float32, algo=_lib.ALGO_SEQUENTIAL)
+    yo, so, _, _ = _oracle(d, torch.float32)
+    assert rel_err(out.cpu().numpy(), yo) < TOL[torch.float32]
+    assert rel_err(s.cpu().numpy(), so) < TOL[torch.float32]
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
 def test_save_for_backward_outputs(dtype):
     d = dense_inputs(2, 2, 50, 64, 64, dtype, dynamic=True, seed=5, s_init=True)

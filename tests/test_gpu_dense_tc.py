@@ -136,15 +136,23 @@ BF16_TOL = 8e-3
 
 @pytest.mark.parametrize("S,T,dyn,s_init", [(128, 200, False, False), (256, 1000, True, True),
                                             (512, 333, True, False), (384, 64, False, True),
-                                            (256, 1, True, True), (512, 65, False, True)])
+                                            (256, 1, True, True), (512, 65, False, True),
+                                            (256, 2048, False, False)])
 @pytest.mark.parametrize("algo", ALGOS)
 def test_tc_bf16_against_oracle(algo, S, T, dyn, s_init):
+    """bf16 storage.  The default kernel at <= 256 slots carries the state and residual
+    operands as bf16 hi + lo pairs: its fp32 final state and fp32 residuals meet the fp16
+    bar of 1e-3; the bf16-rounded outputs are held to one bf16 ulp (8e-3).  Elsewhere
+    (384 / 512 slots, and the rows-layout kernel) the operand copies are single bf16
+    values and every output is held to 8e-3."""
     d = dense_inputs(2, 3, T, S, 64, torch.bfloat16, dynamic=dyn, seed=S + T, s_init=s_init)
     (out, s, err, sf), (yo, so, eo) = _both(d, save=True, storage=O.BF16, algo=algo)
     assert out.dtype == torch.bfloat16
+    tight = 1e-3 if (algo == TC and S <= 256) else BF16_TOL
     assert rel_err(out.float().cpu().numpy(), yo) < BF16_TOL
     assert rel_err(s.float().cpu().numpy(), O.round_to(so, O.BF16)) < BF16_TOL
-    assert rel_err(sf.cpu().numpy(), so) < BF16_TOL
+    assert rel_err(sf.cpu().numpy(), so) < tight
+    assert rel_err(err.cpu().numpy(), eo) < tight
 
 
 @pytest.mark.parametrize("algo", ALGOS)

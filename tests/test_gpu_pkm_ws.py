@@ -195,3 +195,35 @@ def test_ws_wait_timeout_flags_status():
     assert ext.device_status() == 0
     yo, so = _oracle(d, torch.float16)
     assert rel_err(out.float().cpu().numpy(), yo) < TOL[torch.float16]
+
+
+def test_ws_cfg3_full_length():
+    """The cfg3 shape (128 x 128 slots, top-8, fp16 state) at its full T = 8192 on 2 lanes."""
+    d = pkm_inputs(1, 2, 8192, 128, 8, 64, torch.float16, dynamic=False, seed=31, s_init_scale=0.0)
+    out, st = _run(d, WS)
+    assert ext.device_status(clear=True) == 0
+    yo, so = _oracle(d, torch.float16)
+    assert rel_err(out.float().cpu().numpy(), yo) < 1e-3
+    assert rel_err(st.float().cpu().numpy(), so) < 1e-3
+
+
+def test_cfg4_grid_write_stream_full_length():
+    """The cfg4 grid (1024 x 1024 = 1,048,576 slots, 128 MiB of fp16 state per lane) with
+    its write stream -- unit keys and values, beta = 1, alpha = 1 -- routed by the GPU
+    router from N(0, 1/64) routers, at the full T = 16384 of one launch on 2 lanes, against
+    the oracle fed the same routed indices and weights."""
+    from deltagrid_b200.route import pkm_route
+    import torch.nn.functional as F
+    g = torch.Generator().manual_seed(41)
+    B, H, T, G, Dh = 1, 2, 16384, 1024, 64
+    routers = [torch.randn(G, Dh, generator=g) / Dh ** 0.5 for _ in range(2)]
+    k = F.normalize(torch.randn(B, H, T, Dh, generator=g), dim=-1).half()
+    v = F.normalize(torch.randn(B, H, T, Dh, generator=g), dim=-1).half()
+    wk, wq, idx = pkm_route(k.cuda(), k.cuda(), [r.cuda() for r in routers], [r.cuda() for r in routers], 8)
+    d = dict(v=v, beta=torch.ones(B, H, T).half(), wk=wk.cpu(), wq=wq.cpu(), idx=idx.cpu(),
+             decay=torch.ones(H).half(), state=torch.zeros(B, H, G * G, Dh).half())
+    out, st = _run(d, WS)
+    assert ext.device_status(clear=True) == 0
+    yo, so = _oracle(d, torch.float16)
+    assert rel_err(out.float().cpu().numpy(), yo) < 1e-3
+    assert rel_err(st.float().cpu().numpy(), so) < 1e-3

@@ -48,11 +48,11 @@ def test_router_vs_reference_layer_golden():
     wk, wq, idx = pkm_route(k, q, rk, rq, 8)
     *_, margin = O.pkm_route(gld["k"], gld["q"], gld["router_k0"], gld["router_k1"], gld["router_q0"],
                              gld["router_q1"], 8)
-    ok = margin > 1e-5
-    assert ok.mean() > 0.95
-    np.testing.assert_array_equal(idx.cpu().numpy()[ok], gld["idx"][ok])
-    assert rel_err(wk.cpu().numpy()[ok], gld["wk"][ok]) < 1e-5
-    assert rel_err(wq.cpu().numpy()[ok], gld["wq"][ok]) < 1e-5
+    # one near-tie in the fixture (margin <= 1e-5); every token's indices are exact
+    assert int((margin <= 1e-5).sum()) == 1
+    np.testing.assert_array_equal(idx.cpu().numpy(), gld["idx"])
+    assert rel_err(wk.cpu().numpy(), gld["wk"]) < 1e-5
+    assert rel_err(wq.cpu().numpy(), gld["wq"]) < 1e-5
 
 
 def test_router_tie_order_lower_index_first():

@@ -78,3 +78,22 @@ def test_pkm_step_vs_reference_kernel_static_decay():
     my, ms = ext.pkm_step(*a, g["state"].clone())
     assert rel_err(_c(my), _c(ry)) < 1e-5
     assert rel_err(_c(ms), _c(rs)) < 1e-5
+
+
+@need_ref
+@pytest.mark.parametrize("S,T", [(256, 512), (128, 300), (512, 256)])
+def test_dense_bf16_error_not_above_reference_kernel(S, T):
+    """bf16 storage: both kernels against the CPU oracle (fp32 state on the bf16 inputs);
+    this repository's error may not exceed the reference kernel's, on the fp32 final
+    state and the bf16 outputs alike (plus one bf16 ulp of slack on the rounded outputs,
+    where either side's rounding of a near-tie can flip)."""
+    import numpy as np
+    from oracle import oracle as O
+    d = dense_inputs(2, 4, T, S, 64, torch.bfloat16, dynamic=True, seed=S + T + 7)
+    g = {n: (t.cuda() if t is not None else None) for n, t in d.items()}
+    args = (g["q"], g["k"], g["v"], g["beta"], g["wk"], g["wq"], g["decay"])
+    ro, rs, _, rsf = REF.forward(*args, None, True)
+    mo, ms, _, msf = ext.forward(*args, None, True)
+    yo, so = O.dense_forward(*(d[n].float().numpy() for n in ("v", "beta", "wk", "wq", "decay")))
+    assert rel_err(_c(msf), so) <= max(rel_err(_c(rsf), so), 1e-3)
+    assert rel_err(_c(mo), O.round_to(yo, O.BF16)) <= rel_err(_c(ro), O.round_to(yo, O.BF16)) + 2 ** -8

@@ -43,11 +43,16 @@ def test_router_golden(name):
         qs = np.broadcast_to(g["q_scale"][None, :, None], g["k"].shape[:-1])
     wk, wq, idx, margin = O.pkm_route(g["k"], g["q"], g["router_k0"], g["router_k1"],
                                       g["router_q0"], g["router_q1"], top_k, q_scale=qs)
-    ok = margin > 1e-5            # documented near-tie exclusion
-    assert ok.mean() > 0.95
-    np.testing.assert_array_equal(idx[ok], g["idx"][ok])
-    assert rel_err(wk[ok], g["wk"][ok]) < FP32_TOL
-    assert rel_err(wq[ok], g["wq"][ok]) < FP32_TOL
+    # near-ties: tokens whose top-k / (k+1)-th score gap is within 1e-5 on either axis,
+    # where torch's GEMM order (the fixture) and the sequential fp32 order could rank
+    # differently.  Their number per fixture is pinned; every token, near-ties included,
+    # matches the fixture exactly.
+    near = int((margin <= 1e-5).sum())
+    print(f"router golden pin {name}: {margin.size} tokens, {near} near-tie(s) (margin <= 1e-5), all indices exact")
+    assert near == {"router_g128_k8.npz": 1}.get(name, 0)
+    np.testing.assert_array_equal(idx, g["idx"])
+    assert rel_err(wk, g["wk"]) < FP32_TOL
+    assert rel_err(wq, g["wq"]) < FP32_TOL
 
 
 def test_topk_tie_order_kat():
