@@ -197,7 +197,8 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
 
 namespace dg_host {
 bool route_tc_supports(int dtype, int dh, int g0, int g1, int top_k, const void* k, const void* q,
-                       const float* rk0, const float* rk1, const float* rq0, const float* rq1);
+                       const float* rk0, const float* rk1, const float* rq0, const float* rq1, const void* wk,
+                       const void* wq, const int64_t* idx);
 int route_tc(int dtype, int64_t N, int H, int T, int g0, int g1, int top_k, const void* k, const void* q,
              const float* rk0, const float* rk1, const float* rq0, const float* rq1, const float* q_scale, void* wk,
              void* wq, int64_t* idx, cudaStream_t s);
@@ -213,7 +214,8 @@ extern "C" int dg_pkm_route(int dtype, int B, int H, int T, int dh, int g0, int 
     if (top_k > MAXK || top_k > g0 || top_k > g1 || dh > MAXDH) return DG_ERR_UNSUPPORTED;
     const int64_t N = (int64_t)B * H * T;
     if (N == 0) return DG_OK;
-    if (dg_host::route_tc_supports(dtype, dh, g0, g1, top_k, k, q, router_k0, router_k1, router_q0, router_q1))
+    if (dg_host::route_tc_supports(dtype, dh, g0, g1, top_k, k, q, router_k0, router_k1, router_q0, router_q1, wk, wq,
+                                   idx))
         return dg_host::route_tc(dtype, N, H, T, g0, g1, top_k, k, q, router_k0, router_k1, router_q0, router_q1,
                                  q_scale, wk, wq, idx, static_cast<cudaStream_t>(stream));
     RouterParams p{k, q, {router_k0, router_k1}, {router_q0, router_q1}, q_scale, wk, wq, idx, N, H, T, dh,

@@ -7,17 +7,25 @@
 //      two warpgroups, each with its own TMEM columns and router buffer.  The fp32
 //      router is split into two 16-bit parts (hi + lo), so the product is fp32-accurate
 //      up to the tensor core's accumulation; blocks stream through shared memory by TMA;
-//   2. each thread keeps its token's 16 best approximate scores (value descending,
-//      index ascending);
+//   2. each thread keeps its token's 16 best approximate scores as 32-bit keys (the
+//      score's order-preserving bits with the row in the low bits, so one unsigned
+//      max/min pair inserts), reading 32 TMEM columns at a time and skipping any 32
+//      whose maximum is below the 16th;
 //   3. exactness: with |approx - exact| <= delta (delta = c * sum|k| * max|W|, c
-//      covering the split residual, the accumulation and the sequential-sum error),
-//      every exact top-k member scores >= approx_k - 2 delta.  Those candidates are
-//      rescored in the sequential fp32 order of the CPU oracle (each product and sum
-//      rounded separately) and the top-k taken with the lower-index-first tie order
-//      (src/cpp/engine/src/deltagrid_math.cpp:155-167), so indices are exact.  A
-//      token whose 16th approximate score is still inside the window rescans all
-//      rows exactly;
-//   4. u_k, u_q (queries scored at the selected rows), normalisation, Kronecker.
+//      covering the split residual, the accumulation and the sequential-sum error)
+//      and the keys' truncation below eps, two rows whose listed scores differ by more
+//      than 2 delta + eps rank the same way exactly.  So when every adjacent gap among
+//      the approximate top k+1 is wider, the approximate top-k (set and order) is the
+//      exact one and nothing is rescored -- the common case.  Otherwise only the rows
+//      in a chain of narrow gaps (starting inside the top k+1) are rescored in the
+//      sequential fp32 order of the CPU oracle (each product and sum rounded
+//      separately) and ranked with the lower-index-first tie order
+//      (src/cpp/engine/src/deltagrid_math.cpp:155-167), so indices are exact; a chain
+//      that runs past the 16th candidate rescans every row;
+//   4. u_k (the top scores, exact where rescored, else the listed ones: relative error
+//      below 2^(bits of G - 23), inside the outputs' 16-bit rounding), u_q (each query
+//      dot split over eight lanes, so a warp reads whole router rows), normalisation,
+//      and the K x K Kronecker outputs written with 16-byte stores.
 #include <cuda.h>
 
 #include "dg_common.cuh"
@@ -37,7 +45,7 @@ constexpr uint32_t SM_AX0 = SM_W;                           // results [axis][3]
                                                             // router buffers once every block is scored
 constexpr uint32_t SM_STASH = SM_W + 4 * SM_WPART;          // [axis][16][128] scores of the chunk being merged
 constexpr uint32_t SM_BAR = SM_STASH + 2 * 16 * RT_M * 4;
-static_assert(2 * 3 * 8 * RT_M * 4 <= 4 * SM_WPART, "results fit over the router buffers");
+static_assert((2 * 3 * 8 + 2 * RT_E) * RT_M * 4 <= 4 * SM_WPART, "results and rescored lists fit over the router buffers");
 constexpr uint32_t SM_BYTES = SM_BAR + 8 * 8;
 
 struct RtParams {
@@ -59,6 +67,23 @@ struct RtParams {
 
 __device__ __forceinline__ bool ranks_before(float a, int ia, float b, int ib) {
     return (a > b) | ((a == b) & (ia < ib));
+}
+
+// Candidate keys: the score's bits in an order that compares as unsigned integers the
+// way the floats compare, with the low `ib` bits replaced by (imask - row).  One key
+// holds score and row; a larger key ranks first, and equal truncated scores rank the
+// lower row first.  Truncation lowers a score by less than 2^ib units in its last place.
+__device__ __forceinline__ uint32_t cand_key(float s, int row, uint32_t imask) {
+    const uint32_t u = __float_as_uint(s);
+    const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return (o & ~imask) | (imask - (uint32_t)row);
+}
+// the truncated score of a key (never above the score itself); keys below every finite
+// score (the empty list's zeros) give -inf
+__device__ __forceinline__ float key_value(uint32_t k, uint32_t imask) {
+    if (k < 0x00800000u) return -INFINITY;
+    const uint32_t o = k & ~imask;
+    return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
 }
 
 // NC independent sequential fp32 dots over 64 (each product and sum rounded, the
@@ -83,6 +108,43 @@ __device__ __forceinline__ void exact_dots(LoadX load_x, const float* const (&w)
                 out[j] = __fadd_rn(out[j], __fmul_rn(wv[j].y, xv[4 * h + 1]));
                 out[j] = __fadd_rn(out[j], __fmul_rn(wv[j].z, xv[4 * h + 2]));
                 out[j] = __fadd_rn(out[j], __fmul_rn(wv[j].w, xv[4 * h + 3]));
+            }
+        }
+    }
+}
+
+// v[i] += the partner lane's v[i + CNT] (lanes with `upper` keep the upper half instead):
+// after the step, v[0 .. CNT) hold CNT of the 2 CNT values, summed over the lane pair
+template <int CNT, int NV>
+__device__ __forceinline__ void halve_sum(float (&v)[NV], int off, bool upper) {
+#pragma unroll
+    for (int i = 0; i < CNT; ++i) {
+        const float send = upper ? v[i] : v[i + CNT];
+        const float keep = upper ? v[i + CNT] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+}
+
+// NC fp32 dots over 64 with fused multiply-adds (values only; no ranking depends on them)
+template <int NC, typename LoadX>
+__device__ __forceinline__ void fast_dots(LoadX load_x, const float* const (&w)[NC], float (&out)[NC]) {
+#pragma unroll
+    for (int j = 0; j < NC; ++j) out[j] = 0.f;
+#pragma unroll 2
+    for (int c = 0; c < 8; ++c) {
+        float xv[8];
+        load_x(c, xv);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float4 wv[NC];
+#pragma unroll
+            for (int j = 0; j < NC; ++j) wv[j] = __ldg(reinterpret_cast<const float4*>(w[j] + 8 * c + 4 * h));
+#pragma unroll
+            for (int j = 0; j < NC; ++j) {
+                out[j] = fmaf(wv[j].x, xv[4 * h + 0], out[j]);
+                out[j] = fmaf(wv[j].y, xv[4 * h + 1], out[j]);
+                out[j] = fmaf(wv[j].z, xv[4 * h + 2], out[j]);
+                out[j] = fmaf(wv[j].w, xv[4 * h + 3], out[j]);
             }
         }
     }
@@ -119,7 +181,7 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
     const int64_t n0 = (int64_t)blockIdx.x * RT_M;
     const int64_t n = n0 + t;
     const int nrows = p.nrows;
-    const int G = p.G[ax];
+    const int G = ax ? p.G[1] : p.G[0];       // (a select: indexing the parameter array puts it on the stack)
     const int nb = G / nrows;
     const uint32_t wpart = (uint32_t)nrows * 128u;
     const uint32_t idesc = tc::make_idesc(128, nrows, BF16 ? 1 : 0, 0, 0);
@@ -176,10 +238,13 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
         for (int e = 0; e < 8; ++e) kabs += fabsf(x[e]);
     }
 
-    float lv[RT_E];
-    int li[RT_E];
+    // running approximate top-RT_E as descending keys
+    const int ib = 32 - __clz(G - 1);
+    const uint32_t imask = (1u << ib) - 1u;
+    uint32_t lk[RT_E];
 #pragma unroll
-    for (int i = 0; i < RT_E; ++i) { lv[i] = -INFINITY; li[i] = 0x7fffffff; }
+    for (int i = 0; i < RT_E; ++i) lk[i] = 0u;
+    float thr = -INFINITY;                         // truncated score of the 16th key
     uint32_t* st = stash + ax * 16 * RT_M;
 
     for (int j = 0; j < nb; ++j) {
@@ -195,35 +260,38 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
         bad = bad || !tc::mbar_wait(bar_a + ax, ph);
         tc::tc_fence_after();
         if (issuer && j + 1 < nb && !bad) load_w(j + 1);          // the MMAs have read the router buffer
-        // running approximate top-RT_E; scores that beat the current 16th are rare after
-        // the first few, so the compare is unrolled and the sorted insert runs per such score
+        // 32 scores per TMEM read; a score enters the list only if it is at least the
+        // 16th's truncated score, which after the first columns few are
         const int gbase = j * nrows;
-        for (int c0 = 0; c0 < nrows && !bad; c0 += 16) {
-            uint32_t r[16];
-            tc::tmem_ld16(tacc + (uint32_t)c0, r);
+        for (int c0 = 0; c0 < nrows && !bad; c0 += 32) {
+            uint32_t r[32];
+            tc::tmem_ld32(tacc + (uint32_t)c0, r);
             tc::tmem_wait_ld();
-            uint32_t m = 0;
+            float mx = __uint_as_float(r[0]);
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-                m |= (ranks_before(__uint_as_float(r[i]), gbase + c0 + i, lv[RT_E - 1], li[RT_E - 1]) ? 1u : 0u) << i;
-            if (m == 0u) continue;
+            for (int i = 1; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+            if (!(mx >= thr)) continue;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) st[i * RT_M + t] = r[i];
+            for (int h = 0; h < 2; ++h) {
+                uint32_t m = 0;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) m |= (__uint_as_float(r[16 * h + i]) >= thr ? 1u : 0u) << i;
+                if (m != 0u) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) st[i * RT_M + t] = r[16 * h + i];
 #pragma unroll 1
-            while (m != 0u) {
-                const int i = __ffs(m) - 1;
-                m &= m - 1;
-                float v = __uint_as_float(st[i * RT_M + t]);
-                int vi = gbase + c0 + i;
+                while (m != 0u) {
+                    const int i = __ffs(m) - 1;
+                    m &= m - 1;
+                    uint32_t key = cand_key(__uint_as_float(st[i * RT_M + t]), gbase + c0 + 16 * h + i, imask);
 #pragma unroll
-                for (int q = 0; q < RT_E; ++q) {
-                    const bool sw = ranks_before(v, vi, lv[q], li[q]);
-                    const float tv = lv[q];
-                    const int ti = li[q];
-                    lv[q] = sw ? v : tv;
-                    li[q] = sw ? vi : ti;
-                    v = sw ? tv : v;
-                    vi = sw ? ti : vi;
+                    for (int q = 0; q < RT_E; ++q) {
+                        const uint32_t hi = max(lk[q], key);
+                        key = min(lk[q], key);
+                        lk[q] = hi;
+                    }
+                }
+                thr = key_value(lk[RT_E - 1], imask);
                 }
             }
         }
@@ -231,89 +299,169 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
         asm volatile("bar.sync %0, 128;" ::"r"(1 + ax) : "memory");      // accumulator free for the next block
         tc::tc_fence_after();
     }
+    float lv[RT_E];
+    int li[RT_E];
+#pragma unroll
+    for (int i = 0; i < RT_E; ++i) {
+        lv[i] = key_value(lk[i], imask);
+        const int row = (int)(imask - (lk[i] & imask));
+        li[i] = lk[i] < 0x00800000u || row >= G ? 0 : row;     // an unfilled entry (non-finite scores)
+    }
 
     // both axes are scored: the router buffers become the result arrays below
     __syncthreads();
-    // exact top-k: rescore every row within 2 delta of the approximate k-th, in the oracle's order
+    // exact top-k.  Rows whose approximate scores are more than 2 delta apart rank as
+    // their approximate scores do; rescore (in the oracle's order) only the chains of
+    // narrower gaps that start inside the approximate top k+1.
     const float* W = ax ? p.wk[1] : p.wk[0];
     const float delta = p.delta_scale * kabs * __uint_as_float(p.wmax[ax]);
-    const float theta = lv[K - 1] - 2.f * delta;
+    // plus the keys' truncation (below 2^ib units in the last place of any listed score)
+    const float d2 = 2.f * delta + ldexpf(fmaxf(fabsf(lv[0]), fabsf(lv[RT_E - 1])), ib - 22) + 1e-30f;
+    uint32_t need = 0;                                    // list positions to rescore
+#pragma unroll
+    for (int i = 0; i < RT_E - 1; ++i) {
+        const bool narrow = !(lv[i] - lv[i + 1] > d2);    // (also when scores are equal or not finite)
+        if (i < K) {
+            if (narrow) need |= 3u << i;
+        } else if (narrow && ((need >> i) & 1u)) {
+            need |= 1u << (i + 1);
+        }
+    }
     float tv[K];
     int ti[K];
-#pragma unroll
-    for (int r = 0; r < K; ++r) { tv[r] = -INFINITY; ti[r] = 0x7fffffff; }
-    auto keep = [&](float sc, int g) {
-#pragma unroll
-        for (int q = 0; q < K; ++q) {
-            const bool sw = ranks_before(sc, g, tv[q], ti[q]);
-            const float a = tv[q];
-            const int b = ti[q];
-            tv[q] = sw ? sc : a;
-            ti[q] = sw ? g : b;
-            sc = sw ? a : sc;
-            g = sw ? b : g;
-        }
-    };
     auto load_k = [&](int c, float (&x)[8]) { unpack8<T>(*reinterpret_cast<const uint4*>(kt + tc::sw128(t, c)), x); };
-    const bool full_scan = !(lv[RT_E - 1] < theta);       // candidates may lie beyond the list
-    const int ncand = full_scan ? G : RT_E;
-#pragma unroll 1
-    for (int i0 = 0; i0 < ncand; i0 += 8) {
-        int gi[8];
-        bool use[8];
+    if (need == 0u) {                                     // the approximate order is the exact one
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            if (full_scan) {
-                gi[j] = i0 + j;
-                use[j] = gi[j] < G;
-            } else {
-                float vv = lv[0];
-                int gg = li[0];
+        for (int r = 0; r < K; ++r) { tv[r] = lv[r]; ti[r] = li[r]; }
+    } else {
 #pragma unroll
-                for (int q = 1; q < RT_E; ++q)
-                    if (q == i0 + j) { vv = lv[q]; gg = li[q]; }
-                gi[j] = gg;
-                use[j] = (vv >= theta) && gg < G;
+        for (int r = 0; r < K; ++r) { tv[r] = -INFINITY; ti[r] = 0x7fffffff; }
+        auto keep = [&](float sc, int g) {
+#pragma unroll
+            for (int q = 0; q < K; ++q) {
+                const bool sw = ranks_before(sc, g, tv[q], ti[q]);
+                const float a = tv[q];
+                const int b = ti[q];
+                tv[q] = sw ? sc : a;
+                ti[q] = sw ? g : b;
+                sc = sw ? a : sc;
+                g = sw ? b : g;
             }
-        }
-        if (!use[0]) {
-            if (!full_scan) break;                         // the list is sorted: no more candidates
-            continue;
-        }
-        const float* wr[8];
+        };
+        if ((need >> (RT_E - 1)) & 1u) {                  // the narrow chain runs past the list: every row
+#pragma unroll 1
+            for (int i0 = 0; i0 < G; i0 += 8) {
+                const float* wr[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) wr[j] = W + (int64_t)(use[j] ? gi[j] : 0) * RT_DH;
-        float sc[8];
-        exact_dots<8>(load_k, wr, sc);
+                for (int j = 0; j < 8; ++j) wr[j] = W + (int64_t)(i0 + j < G ? i0 + j : 0) * RT_DH;
+                float sc[8];
+                exact_dots<8>(load_k, wr, sc);
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if (use[j]) keep(sc[j], gi[j]);
+                for (int j = 0; j < 8; ++j)
+                    if (i0 + j < G) keep(sc[j], i0 + j);
+            }
+        } else {
+            // exact scores for the flagged positions, four at a time; the list goes through
+            // shared memory (the stash, and the free end of the router buffers) so that the
+            // positions can be indexed at run time
+            uint32_t* srow = st;
+            float* sval = res + 2 * 3 * 8 * RT_M + ax * RT_E * RT_M;
+#pragma unroll
+            for (int q = 0; q < RT_E; ++q) {
+                srow[q * RT_M + t] = (uint32_t)li[q];
+                sval[q * RT_M + t] = lv[q];
+            }
+#pragma unroll 1
+            for (uint32_t m = need; m != 0u;) {
+                int pos[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    pos[j] = m ? __ffs(m) - 1 : -1;
+                    if (m) m &= m - 1;
+                }
+                const float* wr[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) wr[j] = W + (int64_t)(pos[j] >= 0 ? (int)srow[pos[j] * RT_M + t] : 0) * RT_DH;
+                float sc[4];
+                exact_dots<4>(load_k, wr, sc);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (pos[j] >= 0) sval[pos[j] * RT_M + t] = sc[j];
+            }
+#pragma unroll
+            for (int q = 0; q < RT_E; ++q) lv[q] = sval[q * RT_M + t];
+            // rank: rows outside the chains keep their approximate scores, which differ from
+            // every neighbour's by more than 2 delta, so the mixed comparison is exact
+#pragma unroll
+            for (int q = 0; q < RT_E; ++q) keep(lv[q], li[q]);
+        }
     }
     // u_k = normalize(top scores); u_q = normalize(W_q[top] q), the K query dots interleaved
     float ssk = 0.f;
 #pragma unroll
     for (int r = 0; r < K; ++r) ssk += tv[r] * tv[r];
     const float nk = fmaxf(sqrtf(ssk), 1e-12f);
-    const T* qrow = static_cast<const T*>(p.q) + (n < p.N ? n : 0) * RT_DH;
-    const float* WQ = ax ? p.wq[1] : p.wq[0];
-    auto load_q = [&](int c, float (&x)[8]) { unpack8<T>(*reinterpret_cast<const uint4*>(qrow + 8 * c), x); };
-    float qv[K];
-    {
-        const float* wr[K];
-#pragma unroll
-        for (int r = 0; r < K; ++r) wr[r] = WQ + (int64_t)ti[r] * RT_DH;
-        exact_dots<K>(load_q, wr, qv);
-    }
-    float ssq = 0.f;
-#pragma unroll
-    for (int r = 0; r < K; ++r) ssq += qv[r] * qv[r];
-    const float nq = fmaxf(sqrtf(ssq), 1e-12f);
     float* rs = res + ax * 3 * 8 * RT_M;
 #pragma unroll
     for (int r = 0; r < K; ++r) {
         rs[(0 * 8 + r) * RT_M + t] = tv[r] / nk;
-        rs[(1 * 8 + r) * RT_M + t] = qv[r] / nq;
         rs[(2 * 8 + r) * RT_M + t] = __int_as_float(ti[r]);
+    }
+    __syncwarp();
+    // query dots W_q[row] . q, eight lanes per token (each 8 of the 64 columns, with
+    // fused multiply-adds), four tokens of this warp at a time: the router rows are read
+    // as whole 256-byte rows
+    {
+        const float* WQ = ax ? p.wq[1] : p.wq[0];
+        const int lane = tid & 31, sub8 = lane & 7;
+#pragma unroll 1
+        for (int it = 0; it < 8; ++it) {
+            const int tw = (warp & 3) * 32 + 4 * it + (lane >> 3);       // token of this lane's group
+            const int64_t nn = n0 + tw < p.N ? n0 + tw : 0;
+            float qx[8];
+            unpack8<T>(__ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + nn * RT_DH) + sub8), qx);
+            float v[K];
+#pragma unroll
+            for (int r = 0; r < K; ++r) {
+                const int row = __float_as_int(rs[(2 * 8 + r) * RT_M + tw]);
+                const float4* wp = reinterpret_cast<const float4*>(WQ + (int64_t)row * RT_DH + 8 * sub8);
+                const float4 a = __ldg(wp), b = __ldg(wp + 1);
+                float acc = a.x * qx[0];
+                acc = fmaf(a.y, qx[1], acc);
+                acc = fmaf(a.z, qx[2], acc);
+                acc = fmaf(a.w, qx[3], acc);
+                acc = fmaf(b.x, qx[4], acc);
+                acc = fmaf(b.y, qx[5], acc);
+                acc = fmaf(b.z, qx[6], acc);
+                v[r] = fmaf(b.w, qx[7], acc);
+            }
+            // sum over the group's 8 lanes, halving the values each step: lane sub8 ends with
+            // row sub8 (K = 8) or row sub8 / 2 (K = 4)
+            if constexpr (K == 8) {
+                halve_sum<4>(v, 4, (sub8 & 4) != 0);
+                halve_sum<2>(v, 2, (sub8 & 2) != 0);
+                halve_sum<1>(v, 1, (sub8 & 1) != 0);
+                rs[(1 * 8 + sub8) * RT_M + tw] = v[0];
+            } else {
+                halve_sum<2>(v, 4, (sub8 & 4) != 0);
+                halve_sum<1>(v, 2, (sub8 & 2) != 0);
+                v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+                if ((sub8 & 1) == 0) rs[(1 * 8 + (sub8 >> 1)) * RT_M + tw] = v[0];
+            }
+        }
+    }
+    __syncwarp();
+    {
+        float qv[K];
+        float ssq = 0.f;
+#pragma unroll
+        for (int r = 0; r < K; ++r) {
+            qv[r] = rs[(1 * 8 + r) * RT_M + t];
+            ssq += qv[r] * qv[r];
+        }
+        const float nq = fmaxf(sqrtf(ssq), 1e-12f);
+#pragma unroll
+        for (int r = 0; r < K; ++r) rs[(1 * 8 + r) * RT_M + t] = qv[r] / nq;
     }
     bad = __syncthreads_or(bad) != 0;
     if (!bad && n < p.N) {
@@ -323,20 +471,47 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
         const float qsc = p.q_scale ? p.q_scale[h] : 1.f;
         const float* r0 = res;
         const float* r1 = res + 3 * 8 * RT_M;
-        T* owk = static_cast<T*>(p.out_wk) + n * A;
-        T* owq = static_cast<T*>(p.out_wq) + n * A;
-        int64_t* oix = p.out_idx + n * A;
+        // this group's rows i of the K x K product are one contiguous run of the token's
+        // A entries: written with 16-byte stores
+        constexpr int NE = K / 2 * K;                     // entries per group (32 or 8)
+        T* owk = static_cast<T*>(p.out_wk) + n * A + ax * NE;
+        T* owq = static_cast<T*>(p.out_wq) + n * A + ax * NE;
+        int64_t* oix = p.out_idx + n * A + ax * NE;
+        float ukj[K], uqj[K];
+        int64_t ixj[K];
+#pragma unroll
+        for (int j = 0; j < K; ++j) {
+            ukj[j] = r1[(0 * 8 + j) * RT_M + t];
+            uqj[j] = r1[(1 * 8 + j) * RT_M + t];
+            ixj[j] = __float_as_int(r1[(2 * 8 + j) * RT_M + t]);
+        }
 #pragma unroll
         for (int ii = 0; ii < K / 2; ++ii) {
             const int i = ax * (K / 2) + ii;
             const float uki = r0[(0 * 8 + i) * RT_M + t];
             const float uqi = r0[(1 * 8 + i) * RT_M + t];
             const int64_t xi = (int64_t)__float_as_int(r0[(2 * 8 + i) * RT_M + t]) * p.G[1];
+            uint32_t wkp[K / 2], wqp[K / 2];
 #pragma unroll
-            for (int j = 0; j < K; ++j) {
-                owk[i * K + j] = dg::from_f<T>(uki * r1[(0 * 8 + j) * RT_M + t]);
-                owq[i * K + j] = dg::from_f<T>((uqi * r1[(1 * 8 + j) * RT_M + t]) * qsc);
-                oix[i * K + j] = xi + __float_as_int(r1[(2 * 8 + j) * RT_M + t]);
+            for (int j = 0; j < K / 2; ++j) {
+                T a = dg::from_f<T>(uki * ukj[2 * j]), b = dg::from_f<T>(uki * ukj[2 * j + 1]);
+                T c = dg::from_f<T>((uqi * uqj[2 * j]) * qsc), d = dg::from_f<T>((uqi * uqj[2 * j + 1]) * qsc);
+                wkp[j] = (uint32_t)(*reinterpret_cast<uint16_t*>(&a)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&b)) << 16);
+                wqp[j] = (uint32_t)(*reinterpret_cast<uint16_t*>(&c)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&d)) << 16);
+            }
+            if constexpr (K == 8) {
+                reinterpret_cast<uint4*>(owk + ii * K)[0] = make_uint4(wkp[0], wkp[1], wkp[2], wkp[3]);
+                reinterpret_cast<uint4*>(owq + ii * K)[0] = make_uint4(wqp[0], wqp[1], wqp[2], wqp[3]);
+            } else {
+                reinterpret_cast<uint2*>(owk + ii * K)[0] = make_uint2(wkp[0], wkp[1]);
+                reinterpret_cast<uint2*>(owq + ii * K)[0] = make_uint2(wqp[0], wqp[1]);
+            }
+#pragma unroll
+            for (int j = 0; j < K; j += 2) {
+                longlong2 v2;
+                v2.x = xi + ixj[j];
+                v2.y = xi + ixj[j + 1];
+                reinterpret_cast<longlong2*>(oix + ii * K)[j / 2] = v2;
             }
         }
     }
@@ -408,14 +583,17 @@ namespace dg_host {
 
 // Whether the tensor-core router covers the call (else the CUDA-core router runs).
 bool route_tc_supports(int dtype, int dh, int g0, int g1, int top_k, const void* k, const void* q,
-                       const float* rk0, const float* rk1, const float* rq0, const float* rq1) {
+                       const float* rk0, const float* rk1, const float* rq0, const float* rq1, const void* wk,
+                       const void* wq, const int64_t* idx) {
     if (dtype != DG_DTYPE_F16 && dtype != DG_DTYPE_BF16) return false;
     if (dh != RT_DH || (top_k != 4 && top_k != 8)) return false;
     auto rows = [](int g) { return g <= RT_NMAX ? g : RT_NMAX; };
     if (rows(g0) != rows(g1)) return false;
     const int nr = rows(g0);
     if (nr % 16 != 0 || g0 % nr != 0 || g1 % nr != 0 || nr < 32) return false;
-    const uintptr_t al = (uintptr_t)k | (uintptr_t)q | (uintptr_t)rk0 | (uintptr_t)rk1 | (uintptr_t)rq0 | (uintptr_t)rq1;
+    // inputs for TMA and 16-byte loads; outputs for the 16-byte (top-8) / 8-byte stores
+    const uintptr_t al = (uintptr_t)k | (uintptr_t)q | (uintptr_t)rk0 | (uintptr_t)rk1 | (uintptr_t)rq0 |
+                         (uintptr_t)rq1 | (uintptr_t)wk | (uintptr_t)wq | (uintptr_t)idx;
     return (al & 15) == 0;
 }
 
