@@ -387,13 +387,52 @@ def _sub_workload(name, ext, torch, device, steps=5, warmup=3, algo=0):
         torch.cuda.synchronize(device)
     ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(steps)]
     m = statistics.mean(ms)
+    routed = None
+    if w["kind"] == "pkm":
+        routed = _routed_pkm(w, d, ext, torch, stream, steps)
     del d
     torch.cuda.empty_cache()
     rl = _roofline(w, m)
-    return {"desc": w["desc"], "ms_per_step": m, "value": w["B"] * w["T"] / (m / 1e3), "unit": UNIT,
-            "roofline": {k: rl[k] for k in ("bound", "achieved", "peak", "unit", "frac", "peak_source",
-                                               "algorithmic_bytes_per_launch", "kernels_timed")},
-            "steps": steps, "clocks": clk.summary()}
+    rec = {"desc": w["desc"], "ms_per_step": m, "value": w["B"] * w["T"] / (m / 1e3), "unit": UNIT,
+           "roofline": {k: rl[k] for k in ("bound", "achieved", "peak", "unit", "frac", "peak_source",
+                                              "algorithmic_bytes_per_launch", "kernels_timed")},
+           "steps": steps, "clocks": clk.summary()}
+    if routed is not None:
+        rec["with_routing"] = routed
+    return rec
+
+
+def _routed_pkm(w, d, ext, torch, stream, steps):
+    """The PKM step with its routing in the timed region: pkm_fused_forward from the
+    device-resident keys, queries and router weights (router_tc_kernel, then the hazard
+    pre-pass and pkm_ws_kernel), and the router alone, CUDA events on the stream."""
+    from deltagrid_b200.route import pkm_route
+    qr = d["kr"] if w.get("writes") else d["qr"]
+
+    def fused():
+        return ext.pkm_fused_forward(d["kr"], qr, d["v"], d["beta"], d["routers"], d["routers"], None, d["decay"],
+                                     d["state"], top_k=w["K"])
+
+    def route():
+        return pkm_route(d["kr"], qr, d["routers"], d["routers"], w["K"])
+
+    out = {}
+    for name, fn in (("fused", fused), ("router", route)):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * steps)]
+        for i in range(steps):
+            ev[2 * i].record(stream)
+            fn()
+            ev[2 * i + 1].record(stream)
+        torch.cuda.synchronize()
+        out[name] = statistics.mean(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(steps))
+    toks = w["B"] * w["T"]
+    return {"ms_per_step": out["fused"], "value": toks / (out["fused"] / 1e3), "unit": UNIT,
+            "router_ms": out["router"], "router_ms_per_1M_token_heads": out["router"] * 2 ** 20 / (toks * w["H"]),
+            "router_share": out["router"] / out["fused"],
+            "path": "pkm_fused_forward: router_tc_kernel -> pkm_hazard_kernel -> pkm_ws_kernel (wk, wq, idx via HBM)"}
 
 
 def main():
@@ -641,6 +680,7 @@ def main():
             if line.startswith("dram_bytes_per_launch:"):
                 traffic = float(line.split(":")[1])
     roofline = _roofline(w, launch_ms, traffic)
+    routed = _routed_pkm(w, d, ext, torch, stream, args.steps) if w["kind"] == "pkm" else None
 
     del d
     torch.cuda.empty_cache()
@@ -677,6 +717,8 @@ def main():
         "clocks": clk.summary(),
         "verify": {"output_checksums_per_rank": verify},
     }
+    if routed is not None:
+        line["with_routing"] = routed
     if workloads is not None:
         line["workloads"] = workloads
     print(json.dumps(line))

@@ -7,10 +7,12 @@
 //      two warpgroups, each with its own TMEM columns and router buffer.  The fp32
 //      router is split into two 16-bit parts (hi + lo), so the product is fp32-accurate
 //      up to the tensor core's accumulation; blocks stream through shared memory by TMA;
-//   2. each thread keeps its token's 16 best approximate scores as 32-bit keys (the
-//      score's order-preserving bits with the row in the low bits, so one unsigned
-//      max/min pair inserts), reading 32 TMEM columns at a time and skipping any 32
-//      whose maximum is below the 16th;
+//   2. each thread keeps its token's k + 4 (2k above 256 rows) best approximate scores
+//      as 32-bit keys (the score's order-preserving bits with the row in the low bits,
+//      so an insert is one unsigned max/min pair per entry, all entries at once): the
+//      first 32 scores by a
+//      sorting network, then 32 TMEM columns at a time, skipping any 32 whose maximum
+//      is below the last listed score;
 //   3. exactness: with |approx - exact| <= delta (delta = c * sum|k| * max|W|, c
 //      covering the split residual, the accumulation and the sequential-sum error)
 //      and the keys' truncation below eps, two rows whose listed scores differ by more
@@ -21,7 +23,7 @@
 //      sequential fp32 order of the CPU oracle (each product and sum rounded
 //      separately) and ranked with the lower-index-first tie order
 //      (src/cpp/engine/src/deltagrid_math.cpp:155-167), so indices are exact; a chain
-//      that runs past the 16th candidate rescans every row;
+//      that runs past the last listed candidate rescans every row;
 //   4. u_k (the top scores, exact where rescored, else the listed ones: relative error
 //      below 2^(bits of G - 23), inside the outputs' 16-bit rounding), u_q (each query
 //      dot split over eight lanes, so a warp reads whole router rows), normalisation,
@@ -35,7 +37,7 @@ namespace {
 
 constexpr int RT_M = 128;        // tokens per CTA
 constexpr int RT_NMAX = 128;     // router rows per MMA block (256 TMEM columns per CTA: two CTAs per SM)
-constexpr int RT_E = 16;         // approximate candidates kept per token and axis
+constexpr int RT_E = 16;         // most approximate candidates kept per token and axis (top-k + 4)
 constexpr int RT_DH = 64;
 
 constexpr uint32_t SM_KT = 0;                              // K tile: 128 rows x 128 B, 128B swizzle
@@ -78,6 +80,25 @@ __device__ __forceinline__ uint32_t cand_key(float s, int row, uint32_t imask) {
     const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
     return (o & ~imask) | (imask - (uint32_t)row);
 }
+// a[0 .. N) sorted descending by a bitonic network (compile-time compare-exchanges)
+template <int N>
+__device__ __forceinline__ void bitonic_sort_desc(uint32_t* a) {
+#pragma unroll
+    for (int k = 2; k <= N; k <<= 1)
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1)
+#pragma unroll
+            for (int i = 0; i < N; ++i) {
+                const int l = i ^ j;
+                if (l > i) {
+                    const uint32_t x = a[i], y = a[l];
+                    const bool desc = (i & k) == 0;
+                    a[i] = desc ? max(x, y) : min(x, y);
+                    a[l] = desc ? min(x, y) : max(x, y);
+                }
+            }
+}
+
 // the truncated score of a key (never above the score itself); keys below every finite
 // score (the empty list's zeros) give -inf
 __device__ __forceinline__ float key_value(uint32_t k, uint32_t imask) {
@@ -159,7 +180,7 @@ __device__ __forceinline__ void unpack8(uint4 v, float (&x)[8]) {
 
 // 256 threads: warps 0-3 route axis 0, warps 4-7 axis 1, of the same 128 tokens
 // (thread t of a group owns token t and TMEM lane t; each axis owns 256 TMEM columns).
-template <typename T, int K>
+template <typename T, int K, int E>
 __global__ void __launch_bounds__(2 * RT_M, 2)
     router_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmhi,
                      const __grid_constant__ CUtensorMap tmlo, RtParams p) {
@@ -238,12 +259,14 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
         for (int e = 0; e < 8; ++e) kabs += fabsf(x[e]);
     }
 
-    // running approximate top-RT_E as descending keys
+    // running approximate top-E as descending keys (E >= k + 4: room for the narrow-gap
+    // chains of the exactness step below)
+    static_assert(E >= K + 4 && E <= RT_E, "candidate list length");
     const int ib = 32 - __clz(G - 1);
     const uint32_t imask = (1u << ib) - 1u;
-    uint32_t lk[RT_E];
+    uint32_t lk[E];
 #pragma unroll
-    for (int i = 0; i < RT_E; ++i) lk[i] = 0u;
+    for (int i = 0; i < E; ++i) lk[i] = 0u;
     float thr = -INFINITY;                         // truncated score of the 16th key
     uint32_t* st = stash + ax * 16 * RT_M;
 
@@ -267,9 +290,36 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
             uint32_t r[32];
             tc::tmem_ld32(tacc + (uint32_t)c0, r);
             tc::tmem_wait_ld();
-            float mx = __uint_as_float(r[0]);
+            if (j == 0 && c0 == 0) {
+                // the first 32 scores: the list is their top 16, by a sorting network
 #pragma unroll
-            for (int i = 1; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+                for (int i = 0; i < 32; ++i) r[i] = cand_key(__uint_as_float(r[i]), i, imask);
+                bitonic_sort_desc<16>(r);
+                bitonic_sort_desc<16>(r + 16);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) r[i] = max(r[i], r[31 - i]);       // a bitonic sequence
+#pragma unroll
+                for (int jj = 8; jj > 0; jj >>= 1)
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        if ((i ^ jj) > i) {
+                            const uint32_t x = r[i], y = r[i ^ jj];
+                            r[i] = max(x, y);
+                            r[i ^ jj] = min(x, y);
+                        }
+#pragma unroll
+                for (int i = 0; i < E; ++i) lk[i] = r[i];
+                thr = key_value(lk[E - 1], imask);
+                continue;
+            }
+            float mt[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) mt[i] = fmaxf(__uint_as_float(r[i]), __uint_as_float(r[i + 16]));
+#pragma unroll
+            for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+                for (int i = 0; i < w; ++i) mt[i] = fmaxf(mt[i], mt[i + w]);
+            const float mx = mt[0];
             if (!(mx >= thr)) continue;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -283,15 +333,14 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
                 while (m != 0u) {
                     const int i = __ffs(m) - 1;
                     m &= m - 1;
-                    uint32_t key = cand_key(__uint_as_float(st[i * RT_M + t]), gbase + c0 + 16 * h + i, imask);
+                    const uint32_t key = cand_key(__uint_as_float(st[i * RT_M + t]), gbase + c0 + 16 * h + i, imask);
+                    // sorted insert without a dependency chain: entry q becomes
+                    // max(old q, min(key, old q-1))
 #pragma unroll
-                    for (int q = 0; q < RT_E; ++q) {
-                        const uint32_t hi = max(lk[q], key);
-                        key = min(lk[q], key);
-                        lk[q] = hi;
-                    }
+                    for (int q = E - 1; q > 0; --q) lk[q] = max(lk[q], min(key, lk[q - 1]));
+                    lk[0] = max(lk[0], key);
                 }
-                thr = key_value(lk[RT_E - 1], imask);
+                thr = key_value(lk[E - 1], imask);
                 }
             }
         }
@@ -299,10 +348,10 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
         asm volatile("bar.sync %0, 128;" ::"r"(1 + ax) : "memory");      // accumulator free for the next block
         tc::tc_fence_after();
     }
-    float lv[RT_E];
-    int li[RT_E];
+    float lv[E];
+    int li[E];
 #pragma unroll
-    for (int i = 0; i < RT_E; ++i) {
+    for (int i = 0; i < E; ++i) {
         lv[i] = key_value(lk[i], imask);
         const int row = (int)(imask - (lk[i] & imask));
         li[i] = lk[i] < 0x00800000u || row >= G ? 0 : row;     // an unfilled entry (non-finite scores)
@@ -316,10 +365,10 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
     const float* W = ax ? p.wk[1] : p.wk[0];
     const float delta = p.delta_scale * kabs * __uint_as_float(p.wmax[ax]);
     // plus the keys' truncation (below 2^ib units in the last place of any listed score)
-    const float d2 = 2.f * delta + ldexpf(fmaxf(fabsf(lv[0]), fabsf(lv[RT_E - 1])), ib - 22) + 1e-30f;
+    const float d2 = 2.f * delta + ldexpf(fmaxf(fabsf(lv[0]), fabsf(lv[E - 1])), ib - 22) + 1e-30f;
     uint32_t need = 0;                                    // list positions to rescore
 #pragma unroll
-    for (int i = 0; i < RT_E - 1; ++i) {
+    for (int i = 0; i < E - 1; ++i) {
         const bool narrow = !(lv[i] - lv[i + 1] > d2);    // (also when scores are equal or not finite)
         if (i < K) {
             if (narrow) need |= 3u << i;
@@ -348,7 +397,7 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
                 g = sw ? b : g;
             }
         };
-        if ((need >> (RT_E - 1)) & 1u) {                  // the narrow chain runs past the list: every row
+        if ((need >> (E - 1)) & 1u) {                  // the narrow chain runs past the list: every row
 #pragma unroll 1
             for (int i0 = 0; i0 < G; i0 += 8) {
                 const float* wr[8];
@@ -367,7 +416,7 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
             uint32_t* srow = st;
             float* sval = res + 2 * 3 * 8 * RT_M + ax * RT_E * RT_M;
 #pragma unroll
-            for (int q = 0; q < RT_E; ++q) {
+            for (int q = 0; q < E; ++q) {
                 srow[q * RT_M + t] = (uint32_t)li[q];
                 sval[q * RT_M + t] = lv[q];
             }
@@ -389,11 +438,11 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
                     if (pos[j] >= 0) sval[pos[j] * RT_M + t] = sc[j];
             }
 #pragma unroll
-            for (int q = 0; q < RT_E; ++q) lv[q] = sval[q * RT_M + t];
+            for (int q = 0; q < E; ++q) lv[q] = sval[q * RT_M + t];
             // rank: rows outside the chains keep their approximate scores, which differ from
             // every neighbour's by more than 2 delta, so the mixed comparison is exact
 #pragma unroll
-            for (int q = 0; q < RT_E; ++q) keep(lv[q], li[q]);
+            for (int q = 0; q < E; ++q) keep(lv[q], li[q]);
         }
     }
     // u_k = normalize(top scores); u_q = normalize(W_q[top] q), the K query dots interleaved
@@ -414,7 +463,7 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
     {
         const float* WQ = ax ? p.wq[1] : p.wq[0];
         const int lane = tid & 31, sub8 = lane & 7;
-#pragma unroll 1
+#pragma unroll 2
         for (int it = 0; it < 8; ++it) {
             const int tw = (warp & 3) * 32 + 4 * it + (lane >> 3);       // token of this lane's group
             const int64_t nn = n0 + tw < p.N ? n0 + tw : 0;
@@ -566,10 +615,10 @@ bool make_map_2d(CUtensorMap* m, const void* base, int64_t rows, int box_rows, b
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename T, int K>
+template <typename T, int K, int E>
 int launch_tc(const RtParams& p0, const CUtensorMap& mk, const CUtensorMap& mhi, const CUtensorMap& mlo,
               cudaStream_t s) {
-    auto kern = router_tc_kernel<T, K>;
+    auto kern = router_tc_kernel<T, K, E>;
     const int smem = (int)SM_BYTES + 1024;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return dg_host::record_cuda_error(e);
@@ -632,8 +681,16 @@ int route_tc(int dtype, int64_t N, int H, int T, int g0, int g1, int top_k, cons
         // sequential sum's own rounding, with a factor 2 margin (2^-15 f16, 2^-14 bf16)
         RtParams p{k, q, {rk0, rk1}, {rq0, rq1}, q_scale, wmax, wk, wq, idx, N, H, T, nr, {g0, g1},
                    bf16 ? 6.103515625e-05f : 3.0517578125e-05f, nullptr};
-        if (bf16) rc = top_k == 8 ? launch_tc<__nv_bfloat16, 8>(p, mk, mhi, mlo, s) : launch_tc<__nv_bfloat16, 4>(p, mk, mhi, mlo, s);
-        else rc = top_k == 8 ? launch_tc<__half, 8>(p, mk, mhi, mlo, s) : launch_tc<__half, 4>(p, mk, mhi, mlo, s);
+        // list length: k + 4 for small grids; 2k above 256 rows per axis (measured faster there)
+        const bool wide = g0 > 256 || g1 > 256;
+        if (bf16)
+            rc = top_k == 4 ? launch_tc<__nv_bfloat16, 4, 8>(p, mk, mhi, mlo, s)
+                 : wide     ? launch_tc<__nv_bfloat16, 8, 16>(p, mk, mhi, mlo, s)
+                            : launch_tc<__nv_bfloat16, 8, 12>(p, mk, mhi, mlo, s);
+        else
+            rc = top_k == 4 ? launch_tc<__half, 4, 8>(p, mk, mhi, mlo, s)
+                 : wide     ? launch_tc<__half, 8, 16>(p, mk, mhi, mlo, s)
+                            : launch_tc<__half, 8, 12>(p, mk, mhi, mlo, s);
     }
     e = cudaFreeAsync(ws, s);
     if (rc != DG_OK) return rc;
