@@ -30,6 +30,8 @@
 //      and the K x K Kronecker outputs written with 16-byte stores.
 #include <cuda.h>
 
+#include <mutex>
+
 #include "dg_common.cuh"
 #include "tc_util.cuh"
 
@@ -626,6 +628,19 @@ int launch_tc(const RtParams& p0, const CUtensorMap& mk, const CUtensorMap& mhi,
     return dg_host::check_launch();
 }
 
+// The split router (hi, lo parts and the two max|W| words) lives in a per-device buffer
+// kept across calls: a stream-ordered allocation per call costs a remap of the pool
+// (~0.25 ms) whenever the stream has drained in between.  `done` is recorded after each
+// call's last kernel; the next call's stream waits for it, so calls on different streams
+// take turns on the buffer.  Calls under stream capture allocate from the graph instead.
+struct SplitWs {
+    void* p = nullptr;
+    size_t bytes = 0;
+    cudaEvent_t done = nullptr;
+};
+SplitWs g_split[64];
+std::mutex g_split_mu;
+
 }  // namespace
 
 namespace dg_host {
@@ -652,9 +667,42 @@ int route_tc(int dtype, int64_t N, int H, int T, int g0, int g1, int top_k, cons
     const bool bf16 = dtype == DG_DTYPE_BF16;
     const int64_t wn = (int64_t)(g0 + g1) * RT_DH;
     const size_t bytes = (size_t)wn * 2 * 2 + 64;
-    void* ws = nullptr;
-    cudaError_t e = cudaMallocAsync(&ws, bytes, s);          // stream-ordered, from the device's default pool
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(s, &cs);
     if (e != cudaSuccess) return record_cuda_error(e);
+    int dev = 0;
+    e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    const bool cached = cs == cudaStreamCaptureStatusNone && dev >= 0 && dev < 64;
+    std::unique_lock<std::mutex> lock(g_split_mu, std::defer_lock);
+    void* ws = nullptr;
+    if (cached) {
+        lock.lock();
+        SplitWs& w = g_split[dev];
+        if (!w.done) {
+            e = cudaEventCreateWithFlags(&w.done, cudaEventDisableTiming);
+            if (e != cudaSuccess) { w.done = nullptr; return record_cuda_error(e); }
+        }
+        if (w.bytes < bytes) {
+            if (w.p) {
+                e = cudaEventSynchronize(w.done);               // the last call has finished with it
+                if (e == cudaSuccess) e = cudaFree(w.p);
+                w.p = nullptr;
+                w.bytes = 0;
+                if (e != cudaSuccess) return record_cuda_error(e);
+            }
+            e = cudaMalloc(&w.p, bytes);
+            if (e != cudaSuccess) { w.p = nullptr; return record_cuda_error(e); }
+            w.bytes = bytes;
+        } else {
+            e = cudaStreamWaitEvent(s, w.done, 0);
+            if (e != cudaSuccess) return record_cuda_error(e);
+        }
+        ws = w.p;
+    } else {
+        e = cudaMallocAsync(&ws, bytes, s);                    // stream-ordered (a graph allocation under capture)
+        if (e != cudaSuccess) return record_cuda_error(e);
+    }
     uint8_t* hi = static_cast<uint8_t*>(ws);
     uint8_t* lo = hi + wn * 2;
     unsigned* wmax = reinterpret_cast<unsigned*>(lo + wn * 2);
@@ -692,7 +740,7 @@ int route_tc(int dtype, int64_t N, int H, int T, int g0, int g1, int top_k, cons
                  : wide     ? launch_tc<__half, 8, 16>(p, mk, mhi, mlo, s)
                             : launch_tc<__half, 8, 12>(p, mk, mhi, mlo, s);
     }
-    e = cudaFreeAsync(ws, s);
+    e = cached ? cudaEventRecord(g_split[dev].done, s) : cudaFreeAsync(ws, s);
     if (rc != DG_OK) return rc;
     return e == cudaSuccess ? DG_OK : record_cuda_error(e);
 }
