@@ -60,6 +60,12 @@ WORKLOADS = {
     "cfg5p": dict(kind="dense", B=256, H=12, T=2048, S=256, Dh=64, L=12, dtype="bfloat16",
                   desc="LM prefill recurrence: 12 layers x dense forward, B=256 H=12 T=2048 slots=256 Dh=64 bf16"),
 }
+# the fifth BASELINE config whole: the reference's DeltaGridLM (its blocks, MLPs and LM
+# head, from the reference package installed in baseline/_ref) with its recurrence on
+# this drop-in (`deltagrid_b200.install()`), prefill then greedy decode, batch sharded
+LM_CFG = dict(vocab=32000, d_model=768, layers=12, heads=12, slots=256, prefill=2048, decode=512, batch=256,
+              desc="DeltaGridLM 12 layers d_model=768 12 heads slots=256 vocab=32000 bf16: prefill 2048 + "
+                   "greedy decode 512 at batch 256")
 METRIC = "recurrence tokens/sec"
 UNIT = "tokens/s"
 
@@ -435,12 +441,153 @@ def _routed_pkm(w, d, ext, torch, stream, steps):
             "path": "pkm_fused_forward: router_tc_kernel -> pkm_hazard_kernel -> pkm_ws_kernel (wk, wq, idx via HBM)"}
 
 
+def _reference_lm_package():
+    """The reference's Python package (DeltaGridLM and its blocks) from baseline/_ref.
+    Its __init__ imports a weight-export tool that its setup.py does not install; that
+    one name is stubbed (it plays no part in running the model)."""
+    import types
+    site = os.path.join(HERE, "baseline", "_ref")
+    if not os.path.isfile(os.path.join(site, "deltagrid", "__init__.py")):
+        return None
+    if "deltagrid" not in sys.modules:
+        for name in ("deltagrid.cpp", "deltagrid.cpp.engine", "deltagrid.cpp.engine.tools"):
+            sys.modules.setdefault(name, types.ModuleType(name))
+        stub = types.ModuleType("deltagrid.cpp.engine.tools.export_deltagrid_binary")
+
+        def export_deltagrid_to_bin(*a, **k):
+            raise NotImplementedError("weight export is not part of this run")
+
+        stub.export_deltagrid_to_bin = export_deltagrid_to_bin
+        sys.modules[stub.__name__] = stub
+        if site not in sys.path:
+            sys.path.insert(0, site)
+    import deltagrid
+    return deltagrid
+
+
+def lm_main(args):
+    """cfg5 whole: prefill 2048 random token ids, then 512 greedy decode steps, for this
+    rank's share of the batch of 256 (strong scaling; --scaling weak: 256 per rank).
+    A step is prefill plus decode; the timed region includes the copy of the token ids
+    from pinned host memory and the read back of the last generated tokens.  With
+    --impl reference the same model runs on the reference's CUDA extension (built from
+    its sources into oracle/_ref) instead of this drop-in."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+    c = LM_CFG
+    if args.impl == "reference":
+        from oracle.build_ref_cuda import load_prebuilt
+        ext = load_prebuilt()
+        if ext is None:
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "reference CUDA extension not built (oracle/_ref)"}))
+            return
+        sys.modules["hsru_delta_cuda"] = ext
+    else:
+        import deltagrid_b200
+        ext = deltagrid_b200.install()
+    DG = _reference_lm_package()
+    if DG is None:
+        if rank == 0:
+            print(json.dumps({"impl": args.impl, "unavailable": "reference package (baseline/_ref) not installed"}))
+        return
+    from deltagrid.ops import _backend
+    _backend._CUDA_EXT, _backend._CHECKED = ext, True
+    torch.manual_seed(0)
+    model = DG.DeltaGridLM(vocab_size=c["vocab"], d_model=c["d_model"], num_layers=c["layers"], num_heads=c["heads"],
+                           num_slots=c["slots"])
+    with torch.no_grad():
+        for prm in model.parameters():
+            if prm.dim() >= 2:
+                prm.normal_(0.0, 0.02)
+    model = model.to(device=device, dtype=torch.bfloat16).eval()
+    B = c["batch"] // world if args.scaling == "strong" else c["batch"]
+    if args.batch > 0:
+        B = args.batch
+    P, D = (args.seq or c["prefill"]), c["decode"]
+    g = torch.Generator().manual_seed(100 + rank)
+    ids_host = torch.randint(0, c["vocab"], (B, P), generator=g).pin_memory()
+    ids = torch.empty_like(ids_host, device=device)
+    out_host = torch.empty((B, 1), dtype=torch.int64, pin_memory=True)
+    stream = torch.cuda.current_stream(device)
+
+    def step(evs=None):
+        with torch.no_grad():
+            if evs:
+                evs[0].record(stream)
+            ids.copy_(ids_host, non_blocking=True)
+            out = model(ids, return_state=True)
+            tok = out.logits[:, -1].argmax(-1, keepdim=True)
+            states = out.state
+            del out
+            if evs:
+                evs[1].record(stream)
+            for i in range(D):
+                lg, states = model.step(tok, states=states, seq_offset=P + i)
+                tok = lg[:, -1].argmax(-1, keepdim=True)
+            out_host.copy_(tok, non_blocking=True)
+            if evs:
+                evs[2].record(stream)
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    steps = max(1, args.steps)
+    times = []
+    with Clocks(local) as clk:
+        for _ in range(steps):
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            step(evs)
+            torch.cuda.synchronize(device)
+            times.append((evs[0].elapsed_time(evs[1]), evs[1].elapsed_time(evs[2])))
+    pre = statistics.mean(t[0] for t in times)
+    dec = statistics.mean(t[1] for t in times)
+    if world > 1:
+        tt = torch.tensor([pre, dec, pre + dec], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        pre, dec, tot = (float(x) for x in tt.tolist())
+        dist.barrier()
+        dist.destroy_process_group()
+    else:
+        tot = pre + dec
+    if rank != 0:
+        return
+    Bg = B * world
+    toks = Bg * (P + D)
+    line = {
+        "metric": "LM tokens/sec (prefill + decode)", "value": toks / (tot / 1e3), "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": max(1, min(args.warmup, 2)), "ms_per_step": tot, "higher_is_better": True,
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16", "impl": args.impl,
+        "data": "synthetic: uniform random token ids, weights ~ N(0, 0.02) (random init)",
+        "config": {"workload": "cfg5lm: " + c["desc"], "global_batch": Bg, "per_gpu_batch": B, "prefill": P,
+                   "decode": D, "parallelism": f"dp{world} (batch shards, {args.scaling} scaling)"},
+        "prefill": {"ms": pre, "tokens_per_s": Bg * P / (pre / 1e3)},
+        "decode": {"ms": dec, "tokens_per_s": Bg * D / (dec / 1e3), "ms_per_token": dec / D},
+        "e2e": {"value": toks / (tot / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(ids_host.numel() * 8),
+                "d2h_bytes_per_step": int(out_host.numel() * 8)},
+        "clocks": clk.summary(),
+        "model_code": "reference DeltaGridLM (baseline/_ref) with its recurrence on "
+                      + ("the reference CUDA extension" if args.impl == "reference" else "deltagrid_b200"),
+    }
+    print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS) + ["cfg5lm"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--algo", type=int, default=0,
                     help="kernel selector: dense 0 auto, 1 sequential, 2 chunked tcgen05 (state columns on TMEM "
@@ -454,6 +601,8 @@ def main():
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
                     help="strong: the global batch is split over the ranks; weak: every rank runs the full batch")
     args = ap.parse_args()
+    if args.workload == "cfg5lm":
+        return lm_main(args)
     args.warmup = max(3, args.warmup)
     w = dict(WORKLOADS[args.workload])
     if args.batch > 0:
