@@ -27,15 +27,19 @@
 //       cp.async (8 lanes per 128 bytes) of the rows coded "gather" into the
 //       step's ring slot; other rows copy 0 bytes (zero-fill), so the issue
 //       loop has no branches.
-//   slices (KPAR warps per 16-column slice, taking turns by step)
-//       per step s, for the slice's 16 columns: y and pred as a tensor-core GEMV,
-//       mma.sync m16n8k16 with A = the gathered rows transposed (ldmatrix.trans,
-//       one row address per lane, so forwarded rows need no copy; columns are the
-//       M dimension) and B = [wq, wk] (2 of 8 N columns used), four MMAs for 64
-//       rows; r = beta (v - pred); then the new rows (fp32 math, packed f32x2, one
-//       rounding), written to the ring slot (for forwarding) and to global memory
-//       with 16-byte stores; y is staged for coalesced stores.  A warp waits only
-//       for the warps of its slice that wrote a row it forwards.
+//   step warps (KPAR groups of NSL warps, the groups taking turns by step)
+//       per step s, each warp of the group first takes a 16-column slice: y and
+//       pred as a tensor-core GEMV, mma.sync m16n8k16 with A = the gathered rows
+//       transposed (ldmatrix.trans, one row address per lane, so forwarded rows need
+//       no copy; columns are the M dimension) and B = [wq, wk] (2 of 8 N columns
+//       used), four MMAs for 64 rows; r = beta (v - pred) into the step's r row in
+//       shared memory.  Once every slice's r is there (an mbarrier per ring step),
+//       each warp takes a block of 64 / NSL rows and forms the new rows over the whole
+//       row part (fp32 math, packed f32x2, one rounding), written to the ring slot
+//       (for forwarding) and to global memory with 16-byte stores, a row part per
+//       group of lanes, so each store instruction writes whole rows; y is staged for
+//       coalesced stores.  A step that forwards a row waits for the writer step's
+//       update to finish.
 //
 // Ordering argument: a row gathered from global memory for step t has its last
 // writer w <= t-D, and the gather is issued only after the update of step t-D
@@ -110,8 +114,8 @@ __host__ __device__ inline MetaLayout meta_layout(int A, int Dh) {
 struct SmemLayout {
     int bars, misc, rows, zrow, rbuf, ystage, meta, total;
 };
-// mbarriers of the recurrence kernel: full[R], done[R], dsl[R][NSL], mfull[NC], mfree[NC]
-__host__ __device__ constexpr int ws_barriers(int PB, int D) { return 2 * (2 * D) + (2 * D) * (PB / 32) + 2 * NC; }
+// mbarriers of the recurrence kernel: full[R], done[R], rready[R], mfull[NC], mfree[NC]
+__host__ __device__ constexpr int ws_barriers(int PB, int D) { return 3 * (2 * D) + 2 * NC; }
 
 __host__ __device__ inline SmemLayout smem_layout(int PB, int D, int A, int Dh) {
     SmemLayout L;
@@ -121,7 +125,7 @@ __host__ __device__ inline SmemLayout smem_layout(int PB, int D, int A, int Dh) 
     L.misc = o;   o += 16;
     L.rows = o;   o += R * 64 * RS;
     L.zrow = o;   o += RS;
-    L.rbuf = o;   o += 16 * 64 * 4;
+    L.rbuf = o;   o += R * (PB / 2) * 4;     // r of each ring step's columns (fp32)
     L.ystage = o; o += 2 * CHS * PB;     // y rows of two chunks (by chunk parity)
     o = (o + 127) / 128 * 128;
     L.meta = o;   o += NC * meta_layout(A, Dh).bytes;
@@ -378,13 +382,13 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
     const MetaLayout ML = meta_layout(p.A, p.Dh);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + SL.bars);   // [R] rows of step landed
     uint64_t* done = full + R;                                      // [R] every slice finished the step
-    uint64_t* dsl = done + R;                                       // [R][NSL] one slice finished the step
-    uint64_t* mfull = dsl + R * NSL;                                // [NC] metadata chunk landed
+    uint64_t* rready = done + R;                                    // [R] every slice's r of the step written
+    uint64_t* mfull = rready + R;                                   // [NC] metadata chunk landed
     uint64_t* mfree = mfull + NC;                                   // [NC] chunk's last step done by every warp
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SL.misc);
     uint8_t* rows = smem + SL.rows;
     uint8_t* zrow = smem + SL.zrow;
-    float* rbuf = reinterpret_cast<float*>(smem + SL.rbuf);        // [KPAR * NSL warps][16] r of the warp's columns
+    float* rbuf = reinterpret_cast<float*>(smem + SL.rbuf);        // [R][PB / 2] r of the step's columns
     uint8_t* ystage = smem + SL.ystage;
     uint8_t* meta = smem + SL.meta;
 
@@ -401,7 +405,7 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
         for (int i = 0; i < R; ++i) {
             tc::mbar_init(full + i, 2 * NGATH);
             tc::mbar_init(done + i, NSL * 32);
-            for (int k = 0; k < NSL; ++k) tc::mbar_init(dsl + i * NSL + k, 32);
+            tc::mbar_init(rready + i, NSL);
         }
         for (int i = 0; i < NC; ++i) {
             tc::mbar_init(mfull + i, NLOAD);
@@ -486,17 +490,25 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
     } else {
-        // ========================= column-slice warps =========================
+        // ============================== step warps ==============================
+        // The NSL warps of a step (one par group) split it twice: the GEMV by 16-column
+        // slices (warp q: columns 16q .. 16q+15 of the part, all 64 rows), then, once every
+        // slice's r is in shared memory, the update by rows (warp q: rows q RW .. q RW +
+        // RW - 1, whole row parts), so that each row is stored to global memory as whole
+        // 16-byte chunks of one row part per lane group (LPR lanes a row).
+        constexpr int LPR = CH;                                // lanes per row part (16-byte chunks)
+        constexpr int RPI = 32 / LPR;                          // rows per update instruction
+        constexpr int RW = 64 / NSL;                           // rows per warp in the update
+        static_assert(RW == 4 * RPI, "four update iterations per warp");
         const int sw = warp - ROLE_WARPS;                      // 0 .. KPAR*NSL-1
-        const int sli = sw % NSL;                              // columns sli*16 .. sli*16+15 of the part
+        const int q = sw % NSL;                                // GEMV slice and update row block
         const int par = sw / NSL;                              // steps s with s % KPAR == par
         const int g = lane >> 2, tig = lane & 3;
         const int kk = ((lane >> 4) & 1) * 8 + (lane & 7);     // ldmatrix row of this lane in a K block
-        const uint32_t colb = (uint32_t)(sli * 32 + ((lane >> 3) & 1) * 16);
-        const int mr = lane & 15, cc = lane >> 4;              // update: rows mr + 16 j, 16-byte chunk cc of the slice
+        const uint32_t colb = (uint32_t)(q * 32 + ((lane >> 3) & 1) * 16);
+        const int ur = lane / LPR, uc = lane % LPR;            // update: rows q RW + ur + RPI i, chunk uc
         const uint32_t rows_u = tc::smem_u32(rows);
         const uint32_t zrow_u = tc::smem_u32(zrow);
-        float* rw = rbuf + sw * 16;
         T* gout = static_cast<T*>(p.out);
         const float alpha_static = p.dynamic_decay ? 1.f : dg::to_f(static_cast<const T*>(p.decay)[lane_bh % p.H]);
         for (int s = par; s < T_; s += KPAR) {
@@ -506,45 +518,24 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
             bool ok = ws_wait(full + sl, (s / R) & 1, abort_flag, p.status, p.wait_ns);
             if (!__all_sync(DG_FULL_MASK, ok)) break;
             const int16_t* fw = reinterpret_cast<const int16_t*>(mc + ML.code) + ts * 64;
-            // rows forwarded from a step another warp of this slice took: that warp must
-            // have finished it (this warp's own earlier steps precede this one in program order)
+            // rows forwarded from an earlier step in the window: that step's update (by all
+            // of its warps, whatever rows each took) must have finished
             {
                 const int c0 = fw[lane], c1 = fw[lane + 32];
                 uint32_t dm = 0;
                 if (c0 >= 0) dm |= 1u << (c0 >> 6);
                 if (c1 >= 0) dm |= 1u << (c1 >> 6);
-                constexpr uint32_t kOwn = KPAR == 4 ? 0x11111111u : KPAR == 3 ? 0x49249249u : 0x55555555u;   // distances that are multiples of KPAR
-                dm = __reduce_or_sync(DG_FULL_MASK, dm) & ~kOwn;
+                dm = __reduce_or_sync(DG_FULL_MASK, dm);
                 while (dm != 0u && ok) {
                     const int d = __ffs(dm) - 1;
                     dm &= dm - 1;
                     const int w = s - d;
-                    ok = ws_wait(dsl + (w % R) * NSL + sli, (w / R) & 1, abort_flag, p.status, p.wait_ns);
+                    ok = ws_wait(done + (w % R), (w / R) & 1, abort_flag, p.status, p.wait_ns);
                     ok = __all_sync(DG_FULL_MASK, ok);
                 }
                 if (!ok) break;
             }
             const uint32_t own = rows_u + sl * SLOT;
-            // ---- update inputs that do not depend on r ----
-            const int64_t* midx = reinterpret_cast<const int64_t*>(mc + ML.idx) + ts * A;
-            const T* mwk = reinterpret_cast<const T*>(mc + ML.wk) + ts * A;
-            int ucd[4];
-            int64_t ux[4];
-            float uwk[4];
-            uint4 uraw[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int m = mr + 16 * j;                     // rows >= A carry code -2 and are skipped
-                const int mcl = min(m, A - 1);
-                const int cd = fw[m];
-                const int w = s - (cd >> 6);
-                const uint32_t fwd_row = rows_u + (uint32_t)((w % R) * SLOT + (cd & 63) * RS);
-                const uint32_t src = (cd >= 0) ? fwd_row : own + (uint32_t)(m * RS);
-                ucd[j] = cd;
-                ux[j] = midx[mcl];
-                uwk[j] = dg::to_f(mwk[mcl]);
-                uraw[j] = *reinterpret_cast<const uint4*>(rows + (src - rows_u) + sli * 32 + cc * 16);
-            }
             // ---- GEMV: y and pred of the slice's 16 columns ----
             const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(
                 reinterpret_cast<const uint16_t*>(mc + (g == 0 ? ML.wq : ML.wk)) + ts * A);
@@ -575,8 +566,9 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
             for (int kb = 0; kb < 4; ++kb)
                 if (kb < nkb) MmaOp<T>::run(acc, a[kb], b[kb][0], b[kb][1]);
             // lanes with tig == 0: acc = {y, pred} of column g and {y, pred} of column g + 8
+            float* rstep = rbuf + sl * (PB / 2);
             if (tig == 0) {
-                const int col0 = sli * 16 + g;                 // column within the part
+                const int col0 = q * 16 + g;                   // column within the part
                 const float bta = dg::to_f(reinterpret_cast<const T*>(mc + ML.beta)[ts]);
                 const T* mv = reinterpret_cast<const T*>(mc + ML.v) + ts * Dh + part * (PB / 2);
                 // y rows are staged per chunk parity: the same row of the next chunk may
@@ -585,53 +577,74 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
                 T* yrow = reinterpret_cast<T*>(ystage + ((cn & 1) * CHS + ts) * PB);
                 yrow[col0] = dg::from_f<T>(acc[0]);
                 yrow[col0 + 8] = dg::from_f<T>(acc[2]);
-                rw[g] = bta * (dg::to_f(mv[col0]) - acc[1]);
-                rw[g + 8] = bta * (dg::to_f(mv[col0 + 8]) - acc[3]);
+                rstep[col0] = bta * (dg::to_f(mv[col0]) - acc[1]);
+                rstep[col0 + 8] = bta * (dg::to_f(mv[col0 + 8]) - acc[3]);
             }
             __syncwarp();
-            const float4 ra = reinterpret_cast<const float4*>(rw + cc * 8)[0];
-            const float4 rb = reinterpret_cast<const float4*>(rw + cc * 8)[1];
+            if (lane == 0) mbar_arrive(rready + sl);
+            ok = ws_wait(rready + sl, (s / R) & 1, abort_flag, p.status, p.wait_ns);
+            if (!__all_sync(DG_FULL_MASK, ok)) break;
+            // ---- update: whole row parts, new rows (fp32, one rounding) to the ring slot
+            // and to global memory ----
+            const float4 ra = reinterpret_cast<const float4*>(rstep + uc * 8)[0];
+            const float4 rb = reinterpret_cast<const float4*>(rstep + uc * 8)[1];
             const float br[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
             const float al = p.dynamic_decay ? dg::to_f(reinterpret_cast<const T*>(mc + ML.alpha)[ts]) : alpha_static;
             const unsigned long long al2 = f2pack(al, al);
-            // ---- update: new rows (fp32, one rounding) to the ring slot and to global memory ----
+            const int64_t* midx = reinterpret_cast<const int64_t*>(mc + ML.idx) + ts * A;
+            const T* mwk = reinterpret_cast<const T*>(mc + ML.wk) + ts * A;
             uint8_t* slot = rows + sl * SLOT;
+            int ucd[4];
+            int64_t ux[4];
+            float uwk[4];
+            uint4 uraw[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int m = mr + 16 * j;
+            for (int i = 0; i < 4; ++i) {
+                const int m = q * RW + ur + RPI * i;           // rows >= A carry code -2 and are skipped
+                const int mcl = min(m, A - 1);
+                const int cd = fw[m];
+                const int w = s - (cd >> 6);
+                const uint32_t fwd_row = rows_u + (uint32_t)((w % R) * SLOT + (cd & 63) * RS);
+                const uint32_t src = (cd >= 0) ? fwd_row : own + (uint32_t)(m * RS);
+                ucd[i] = cd;
+                ux[i] = midx[mcl];
+                uwk[i] = dg::to_f(mwk[mcl]);
+                uraw[i] = *reinterpret_cast<const uint4*>(rows + (src - rows_u) + uc * 16);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int m = q * RW + ur + RPI * i;
                 // rows as gathered (zeros for an index out of range: its ring row was zero-filled)
                 if (p.saved != nullptr && m < A)
-                    dg::st16(static_cast<uint8_t*>(p.saved) + ((lt0 + s) * A + m) * row_bytes + part * PB + sli * 32 +
-                                 cc * 16,
-                             uraw[j]);
-                if (ucd[j] == -2) continue;
-                const uint32_t in[4] = {uraw[j].x, uraw[j].y, uraw[j].z, uraw[j].w};
+                    dg::st16(static_cast<uint8_t*>(p.saved) + ((lt0 + s) * A + m) * row_bytes + part * PB + uc * 16,
+                             uraw[i]);
+                if (ucd[i] == -2) continue;
+                const uint32_t in[4] = {uraw[i].x, uraw[i].y, uraw[i].z, uraw[i].w};
                 uint32_t o[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float2 sv = unpack2(in[i], T());
-                    const unsigned long long u = mul_f32x2(f2pack(br[2 * i], br[2 * i + 1]), f2pack(uwk[j], uwk[j]));
+                for (int e = 0; e < 4; ++e) {
+                    const float2 sv = unpack2(in[e], T());
+                    const unsigned long long u = mul_f32x2(f2pack(br[2 * e], br[2 * e + 1]), f2pack(uwk[i], uwk[i]));
                     const float2 nv = f2unpack(fma_f32x2(al2, f2pack(sv.x, sv.y), u));
-                    o[i] = pack2(nv.x, nv.y, T());
+                    o[e] = pack2(nv.x, nv.y, T());
                 }
                 const uint4 nv4 = make_uint4(o[0], o[1], o[2], o[3]);
-                *reinterpret_cast<uint4*>(slot + m * RS + sli * 32 + cc * 16) = nv4;
-                dg::st16(gstate + ux[j] * row_bytes + sli * 32 + cc * 16, nv4);
+                *reinterpret_cast<uint4*>(slot + m * RS + uc * 16) = nv4;
+                dg::st16(gstate + ux[i] * row_bytes + uc * 16, nv4);
             }
             __syncwarp();
-            mbar_arrive(dsl + sl * NSL + sli);
             mbar_arrive(done + sl);
             const int t0c = s - ts;
             const int cend = min(t0c + CHS, T_);
             if (s + KPAR >= cend) {                           // this warp's last step of the chunk
                 mbar_arrive(mfree + (cn % NC));
-                // this warp's rows of the chunk: steps s = par (mod KPAR), i.e. rows j0, j0 + KPAR, ...
+                // this warp's y columns of the chunk: steps s = par (mod KPAR), i.e. rows j0, j0 + KPAR, ...
                 const int j0 = ((par - t0c) % KPAR + KPAR) % KPAR;
                 const int nj = (cend - t0c - j0 + KPAR - 1) / KPAR;
                 for (int i = lane; i < 2 * nj; i += 32) {
                     const int jj = j0 + KPAR * (i >> 1), hh = i & 1;
-                    const uint4 val = *reinterpret_cast<const uint4*>(ystage + ((cn & 1) * CHS + jj) * PB + sli * 32 + hh * 16);
-                    dg::st16(reinterpret_cast<uint8_t*>(gout + (lt0 + t0c + jj) * Dh) + part * PB + sli * 32 + hh * 16,
+                    const uint4 val = *reinterpret_cast<const uint4*>(ystage + ((cn & 1) * CHS + jj) * PB + q * 32 + hh * 16);
+                    dg::st16(reinterpret_cast<uint8_t*>(gout + (lt0 + t0c + jj) * Dh) + part * PB + q * 32 + hh * 16,
                              val);
                 }
                 __syncwarp();

@@ -67,6 +67,7 @@ struct RtParams {
     int G[2];
     float delta_scale;
     int32_t* status;
+    uint32_t wait_limit;         // polls of each bounded wait
 };
 
 __device__ __forceinline__ bool ranks_before(float a, int ia, float b, int ib) {
@@ -250,7 +251,11 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
         tc::mma_commit(bar_a + ax);
     };
 
-    bool bad = !tc::mbar_wait(bar_kt, 0);
+    bool bad = !tc::mbar_wait(bar_kt, 0, p.wait_limit);
+    const bool kt_pending = bad;
+    // the issuer's copy and MMA batch in flight (parity of the phase still awaited, or -1),
+    // drained before the TMEM is freed when a wait gives up
+    int pend_w = issuer ? 0 : -1, pend_a = -1;
     // sum |k| of this token, for the error bound
     float kabs = 0.f;
 #pragma unroll
@@ -275,16 +280,25 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
     for (int j = 0; j < nb; ++j) {
         const uint32_t ph = (uint32_t)j & 1u;
         if (issuer) {
-            if (!bad && tc::mbar_wait(bar_w + ax, ph)) {
+            if (!bad && tc::mbar_wait(bar_w + ax, ph, p.wait_limit)) {
+                pend_w = -1;
                 tc::tc_fence_after();
                 issue();
+                pend_a = (int)ph;
             } else {
                 bad = true;
             }
         }
-        bad = bad || !tc::mbar_wait(bar_a + ax, ph);
+        if (!bad && tc::mbar_wait(bar_a + ax, ph, p.wait_limit)) {
+            pend_a = -1;
+        } else {
+            bad = true;
+        }
         tc::tc_fence_after();
-        if (issuer && j + 1 < nb && !bad) load_w(j + 1);          // the MMAs have read the router buffer
+        if (issuer && j + 1 < nb && !bad) {
+            load_w(j + 1);                                        // the MMAs have read the router buffer
+            pend_w = (int)((j + 1) & 1);
+        }
         // 32 scores per TMEM read; a score enters the list only if it is at least the
         // 16th's truncated score, which after the first columns few are
         const int gbase = j * nrows;
@@ -566,7 +580,28 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
             }
         }
     }
+    if (bad && n < p.N) {
+        // a wait gave up: the tile's tokens get index -1 (out of range: the recurrence
+        // skips such rows and flags them in its status word) and zero weights
+        constexpr int A = K * K, NE = K / 2 * K;
+        T* owk = static_cast<T*>(p.out_wk) + n * A + ax * NE;
+        T* owq = static_cast<T*>(p.out_wq) + n * A + ax * NE;
+        int64_t* oix = p.out_idx + n * A + ax * NE;
+        for (int e = 0; e < NE; ++e) {
+            owk[e] = dg::from_f<T>(0.f);
+            owq[e] = dg::from_f<T>(0.f);
+            oix[e] = -1;
+        }
+    }
     if (bad && tid == 0) dg::flag_status(p.status, DG_DEVCHK_TIMEOUT);
+    if (bad) {
+        // let the copies and MMAs this CTA issued finish before its shared memory and
+        // TMEM are released (bounded too)
+        constexpr uint32_t DRAIN = 1u << 22;
+        if (tid == 0 && kt_pending) tc::mbar_wait(bar_kt, 0, DRAIN);
+        if (pend_w >= 0) tc::mbar_wait(bar_w + ax, (uint32_t)pend_w, DRAIN);
+        if (pend_a >= 0) tc::mbar_wait(bar_a + ax, (uint32_t)pend_a, DRAIN);
+    }
     tc::tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -644,6 +679,8 @@ std::mutex g_split_mu;
 }  // namespace
 
 namespace dg_host {
+
+uint32_t wait_limit();
 
 // Whether the tensor-core router covers the call (else the CUDA-core router runs).
 bool route_tc_supports(int dtype, int dh, int g0, int g1, int top_k, const void* k, const void* q,
@@ -728,7 +765,7 @@ int route_tc(int dtype, int64_t N, int H, int T, int g0, int g1, int top_k, cons
         // |approx - exact| <= c * sum|k| * max|w|: split residual, accumulation and the
         // sequential sum's own rounding, with a factor 2 margin (2^-15 f16, 2^-14 bf16)
         RtParams p{k, q, {rk0, rk1}, {rq0, rq1}, q_scale, wmax, wk, wq, idx, N, H, T, nr, {g0, g1},
-                   bf16 ? 6.103515625e-05f : 3.0517578125e-05f, nullptr};
+                   bf16 ? 6.103515625e-05f : 3.0517578125e-05f, nullptr, wait_limit()};
         // list length: k + 4 for small grids; 2k above 256 rows per axis (measured faster there)
         const bool wide = g0 > 256 || g1 > 256;
         if (bf16)

@@ -103,3 +103,26 @@ def test_tensor_core_router_ties_and_crowded_threshold(dtype):
     wk, wq, idx = pkm_route(k.cuda(), q.cuda(), [w.cuda(), w.cuda()], [w.cuda(), w.cuda()], K)
     _, _, idxo, _ = O.pkm_route(k.float().numpy(), q.float().numpy(), w.numpy(), w.numpy(), w.numpy(), w.numpy(), K)
     np.testing.assert_array_equal(idx.cpu().numpy(), idxo)
+
+
+def test_router_wait_timeout_marks_tokens():
+    """With the wait budget at zero the tensor-core router's first wait gives up: it
+    drains the copies and MMAs it issued, writes index -1 (out of range) and zero
+    weights for every token, and returns; the next call with the normal budget is
+    exact again."""
+    B, H, T, Dh, G, K = 2, 2, 200, 64, 128, 8
+    g = torch.Generator().manual_seed(21)
+    k = torch.nn.functional.normalize(torch.randn(B, H, T, Dh, generator=g), dim=-1).half().cuda()
+    q = torch.randn(B, H, T, Dh, generator=g).half().cuda()
+    w = [x.cuda() for x in _routers(G, G, Dh, 5)]
+    old = ext.set_wait_limit(0)
+    try:
+        wk, wq, idx = pkm_route(k, q, w[:2], w[2:], K)
+        torch.cuda.synchronize()
+    finally:
+        ext.set_wait_limit(old)
+    assert bool((idx == -1).all()) and float(wk.abs().max()) == 0.0 and float(wq.abs().max()) == 0.0
+    wk, wq, idx = pkm_route(k, q, w[:2], w[2:], K)
+    wko, wqo, idxo, _ = O.pkm_route(k.float().cpu().numpy(), q.float().cpu().numpy(),
+                                    *[x.cpu().numpy() for x in w], K)
+    np.testing.assert_array_equal(idx.cpu().numpy(), idxo)
