@@ -42,6 +42,7 @@ _SIGS = {
     "dg_pkm_step": [_I, _I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P],
     "dg_read_device_status": [_P, _I, _P, _P],
     "dg_pkm_route": [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
+    "dg_dense_route": [_I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     "dg_fxp_dense_forward": [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P],
     "dg_fxp_pkm_forward": [_I, _I, _I, _I64, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     "dg_dense_backward_workspace_size": [_I, _I, _I, _I],

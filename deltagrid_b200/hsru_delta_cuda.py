@@ -102,18 +102,23 @@ def dense_fused_forward(k: torch.Tensor, q: torch.Tensor, v: torch.Tensor, beta:
     k, q, v [B,H,T,Dh]; beta [B,H,T]; slot_proj_k / slot_proj_q [slots, Dh] (the
     layer's nn.Linear weights) or None when slots == Dh; q_scale [H] or None.
     wk = L2-normalise(k P_k^T) and wq = (q P_q^T) q_scale (memory.py:233-236,
-    :489-491), formed by library GEMMs and kept in HBM for the recurrence kernel;
-    returns forward's [out, s_final, err_out, s_final_f].
+    :490-492), formed by the slot-routing kernel (route.dense_route: 16-bit k, Dh = 64,
+    slots a multiple of 64 up to 512; other shapes use torch's GEMMs) and kept in HBM
+    for the recurrence kernel; returns forward's [out, s_final, err_out, s_final_f].
     """
+    from .route import dense_route, dense_route_covers
     if (slot_proj_k is None) != (slot_proj_q is None):
         raise RuntimeError("dense_fused_forward: give both slot projections or neither")
-    if slot_proj_k is not None:
-        wk = F.normalize(F.linear(k, slot_proj_k.to(k.dtype)), p=2, dim=-1)
-        wq = F.linear(q, slot_proj_q.to(q.dtype))
+    if slot_proj_k is not None and dense_route_covers(k, slot_proj_k):
+        wk, wq = dense_route(k, q, slot_proj_k, slot_proj_q, q_scale)
     else:
-        wk, wq = k, q
-    if q_scale is not None:
-        wq = wq * q_scale.to(dtype=q.dtype).view(1, -1, 1, 1)
+        if slot_proj_k is not None:
+            wk = F.normalize(F.linear(k, slot_proj_k.to(k.dtype)), p=2, dim=-1)
+            wq = F.linear(q, slot_proj_q.to(q.dtype))
+        else:
+            wk, wq = k, q
+        if q_scale is not None:
+            wq = wq * q_scale.to(dtype=q.dtype).view(1, -1, 1, 1)
     return forward(q, k, v, beta, wk, wq, decay, s_init, save_for_backward)
 
 

@@ -11,8 +11,11 @@ the two layers unchanged.  What differs is how the recurrence is reached:
   compaction of the touched slots and no per-step saved rows are made, where the
   reference's autograd function (src/ops/_autograd.py:88-177) clones the state (or
   runs torch.unique over every index) and saves [B,H,T,64,Dh] rows on every call --
-  about 69 GB at the 1024 x 1024 grid's bench shape.  Dense mode calls the sequence
-  forward with the state as s_init and returns the new state.
+  about 69 GB at the 1024 x 1024 grid's bench shape.  Dense mode with slot
+  projections on 16-bit keys (Dh = 64, slots a multiple of 64 up to 512) forms wk and
+  wq with the slot-routing kernel (dg_dense_route: memory.py:233-236 and the q_scale
+  of :490-492), then calls the sequence forward with the state as s_init and returns
+  the new state.
 * Training: autograd functions over this package's forward (saving what its backward
   needs) and backward kernels.  The PKM one runs on a copy of the touched slots of
   the state, so the caller's state is left as it was, as in the reference.
@@ -32,7 +35,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import hsru_delta_cuda as ext
-from .route import pkm_route
+from .route import dense_route, dense_route_covers, pkm_route
 
 
 class _DenseRecurrence(torch.autograd.Function):
@@ -272,8 +275,13 @@ class DeltaGridLayer(nn.Module):
                 else:
                     y, state, _ = ext.pkm_forward(*args, state, False)
         else:
-            wk, wq = self._route_dense(k, q)
-            wq = wq * self.q_scale.to(dt).view(1, H, 1, 1)
+            if not grad and self.slot_proj_k is not None and dense_route_covers(k, self.slot_proj_k.weight):
+                # inference: the slot-routing kernel (projection, normalisation, q_scale)
+                wk, wq = dense_route(k.to(dt), q.to(dt), self.slot_proj_k.weight, self.slot_proj_q.weight,
+                                     self.q_scale)
+            else:
+                wk, wq = self._route_dense(k, q)
+                wq = wq * self.q_scale.to(dt).view(1, H, 1, 1)
             s0 = state.to(dt) if state is not None else None
             args = (q.contiguous(), v.contiguous(), beta.contiguous(), wk.to(dt).contiguous(), wq.to(dt).contiguous(),
                     decay)

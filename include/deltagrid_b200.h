@@ -265,6 +265,23 @@ int dg_fxp_pkm_forward(int lanes, int T, int active, int64_t total_slots, int dh
                        const int32_t* alpha, int32_t* state, int32_t* y, int32_t* dev_status, void* stream);
 
 /*
+ * Dense slot routing, one kernel (tcgen05): wk = L2-normalise(k P_k^T) and
+ * wq = (q P_q^T) * q_scale[h].  Replaces DeltaGridLayer._route_dense's linear-projection
+ * branch (src/modules/memory.py:233-236, bias-free nn.Linear slot projections, :192-193)
+ * and the q_scale multiply of memory.py:490-492.
+ *   k, q [B,H,T,dh] (storage dtype `dtype`: f16 or bf16; dh = 64)
+ *   slot_proj_k, slot_proj_q [slots, dh] (the nn.Linear weights, same dtype; slots a
+ *   multiple of 64 up to 512);  q_scale [H] fp32 or NULL
+ *   wk, wq [B,H,T,slots] (same dtype); every pointer 16-byte aligned
+ * The products accumulate in fp32; the norm is the fp32 sum of squares, eps 1e-12 as
+ * F.normalize; each output is rounded once.  Other shapes: DG_ERR_UNSUPPORTED.
+ * dev_status (or NULL) gets DG_DEVCHK_TIMEOUT if a bounded wait gave up.
+ */
+int dg_dense_route(int dtype, int B, int H, int T, int dh, int slots, const void* k, const void* q,
+                   const void* slot_proj_k, const void* slot_proj_q, const float* q_scale, void* wk, void* wq,
+                   int32_t* dev_status, void* stream);
+
+/*
  * Two-axis product-key router for Sparse Delta-PKM, fused (one kernel).
  * Replaces DeltaGridLayer._route_sparse_pkm (src/modules/memory.py:240-289) for two
  * axes without subspace slicing, and the q_scale multiply of memory.py:453-455.
