@@ -4,8 +4,7 @@
     python oracle/build_ref_cuda.py
 
 Compiles src/cpp/binding.cpp and src/cpp/delta_kernel.cu where they lie in the
-reference checkout (located by ``oracle/refpath.py``: DELTAGRID_REF, else
-``oracle/reference.cfg``) with
+reference checkout (the directory in ``DELTAGRID_REF``, ``oracle/refpath.py``) with
 torch.utils.cpp_extension for sm_100a, under the module name
 ``ref_hsru_delta_cuda`` (binding.cpp:523 registers TORCH_EXTENSION_NAME, so the
 rename needs no source change).  All outputs go to oracle/_ref/, which is

@@ -2,10 +2,11 @@
 
 The checkers that are built from the reference's own sources (``oracle/_ref``) and
 the scripts that generate golden fixtures need the reference project's sources.
-Their location is taken from the environment variable ``DELTAGRID_REF``; when it
-is unset, from the one-line file ``oracle/reference.cfg``, a path relative to the
-repository root.  Nothing on the product path, in the GPU tests, in ``smoke()`` or
-in ``bench.py`` reads it: the checkers travel prebuilt in ``oracle/_ref/``.
+Their location is taken from the environment variable ``DELTAGRID_REF`` alone; when
+it is unset they stop with an error that says so (``__graft_entry__.build()`` then
+keeps the prebuilt checkers).  Nothing on the product path, in the GPU tests, in
+``smoke()`` or in ``bench.py`` reads it: the checkers travel prebuilt in
+``oracle/_ref/``.
 
     python oracle/refpath.py      # prints the resolved directory, or exits 1
 """
@@ -16,26 +17,17 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
-CFG = os.path.join(HERE, "reference.cfg")
 
 
 def reference_root(required: bool = True) -> str | None:
     """The reference checkout directory, or None (``required=False``) when it cannot be found."""
     path = os.environ.get("DELTAGRID_REF")
-    how = "DELTAGRID_REF"
-    if not path and os.path.exists(CFG):
-        with open(CFG) as f:
-            rel = f.read().strip()
-        if rel:
-            path = os.path.normpath(os.path.join(REPO, rel))
-            how = f"oracle/reference.cfg ({rel!r} relative to the repository root)"
     if path and os.path.isdir(os.path.join(path, "src")):
         return path
     if required:
         raise RuntimeError(
-            "reference checkout not found: set DELTAGRID_REF to the reference project's root "
-            f"(tried {how}: {path!r})" if path else
-            "reference checkout not found: set DELTAGRID_REF to the reference project's root")
+            f"DELTAGRID_REF={path!r} is not a reference checkout (no src/ under it)" if path else
+            "DELTAGRID_REF is unset: set it to the reference project's root")
     return None
 
 

@@ -1,8 +1,8 @@
 """Generate the engine-file fixtures under tests/golden/engine_files/ from the
 reference itself.
 
-Run where the reference project is importable (located by ``oracle/refpath.py``:
-``DELTAGRID_REF``, else ``oracle/reference.cfg``) and ``oracle/_ref/libdg_ref_engine.so`` is built
+Run with ``DELTAGRID_REF`` set to the reference project's root (``oracle/refpath.py``) and
+``oracle/_ref/libdg_ref_engine.so`` built
 (``make -C oracle ref``):
 
     python tests/golden/make_engine_files.py

@@ -1,7 +1,6 @@
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
-Run in a checkout where the reference project is importable (located by
-``oracle/refpath.py``: ``DELTAGRID_REF``, else ``oracle/reference.cfg``) and where
+Run with ``DELTAGRID_REF`` set to the reference project's root (``oracle/refpath.py``) and where
 ``oracle/_ref/libdg_ref_engine.so`` has been built (``make -C oracle ref``):
 
     python tests/golden/make_golden.py
