@@ -719,38 +719,39 @@ def main():
     elif not args.no_e2e:
         # the config's inputs k, q, v, beta cross PCIe and the routing runs on the device:
         # slot projections (dense_fused_forward) or the product-key router (pkm_fused_forward)
-        # (the write stream's queries are its keys: copied once)
+        # (the write stream's queries are its keys: copied once).  The step runs in pieces
+        # so that the copy in of piece i+1 and the copy out of piece i-1 (their own streams)
+        # overlap piece i's compute: dense by batch rows (lanes are independent; each piece
+        # still gets whole CTAs, and eight pieces' compute stays under the copies), PKM by
+        # steps (the state is carried in place from piece to piece, which is how the
+        # recurrence treats consecutive calls anyway: rows are rounded to the storage type
+        # every step, so the pieces give the unsplit call's results bit for bit).
         names = ("kr", "v", "beta") if w.get("writes") else ("kr", "qr", "v", "beta")
-        host = {n: d[n].to("cpu").pin_memory() for n in names}
-        h2d = sum(t.numel() * t.element_size() for t in host.values())
-        dev_in = {n: torch.empty_like(d[n]) for n in names}
-        outs = step()
-        # result read back each step: y and the final state (dense); y (PKM: the state stays resident)
-        n_res = 2 if w["kind"] == "dense" else 1
-        res_host = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs[:n_res]]
-        d2h = sum(t.numel() * t.element_size() for t in res_host)
-
-        # the step in pieces of the batch (lanes are independent): the copy in of piece i+1
-        # and the copy out of piece i-1 run on their own streams while piece i computes.
-        # Only where a call spans several waves of CTAs (dense: one CTA per lane), so that a
-        # piece costs a share of the compute; a PKM call is one wave of lanes that each run
-        # the whole sequence, and pieces of it would run one after another.
-        npc = 1
         if w["kind"] == "dense":
-            waves = -(-w["B"] * w["H"] // torch.cuda.get_device_properties(device).multi_processor_count)
-            npc = next(n for n in (4, 2, 1) if n <= waves and w["B"] % n == 0)
-        bs = w["B"] // npc
-        s_h2d, s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+            npc = next(n for n in (8, 4, 2, 1) if w["B"] % n == 0)
+            cut = lambda t, i: t[i * (w["B"] // npc):(i + 1) * (w["B"] // npc)]
+        else:
+            npc = next(n for n in (4, 2, 1) if w["T"] % (8 * n) == 0)
+            cut = lambda t, i: t[:, :, i * (w["T"] // npc):(i + 1) * (w["T"] // npc)]
+        # pinned host inputs and device buffers, one contiguous block per piece
+        host = {n: [cut(d[n], i).to("cpu").contiguous().pin_memory() for i in range(npc)] for n in names}
+        h2d = sum(t.numel() * t.element_size() for ts in host.values() for t in ts)
+        dev_in = {n: [torch.empty_like(t, device=device) for t in ts] for n, ts in host.items()}
 
-        def compute(dd):
+        def compute(i):
+            dd = {n: dev_in[n][i] for n in names}
             if w["kind"] == "dense":
                 for _ in range(w.get("L", 1)):
-                    o = ext.dense_fused_forward(dd["kr"], dd["qr"], dd["v"], dd["beta"], dd["P"], dd["P"], None,
-                                                dd["decay"])
-                return o
+                    o = ext.dense_fused_forward(dd["kr"], dd["qr"], dd["v"], dd["beta"], d["P"], d["P"], None,
+                                                d["decay"])
+                return o[:2]                      # y and the final state of these lanes
             qr = dd["kr"] if w.get("writes") else dd["qr"]
-            return ext.pkm_fused_forward(dd["kr"], qr, dd["v"], dd["beta"], dd["routers"], dd["routers"], None,
-                                         dd["decay"], dd["state"], top_k=w["K"])
+            return ext.pkm_fused_forward(dd["kr"], qr, dd["v"], dd["beta"], d["routers"], d["routers"], None,
+                                         d["decay"], d["state"], top_k=w["K"])[:1]     # y of these steps
+        first = compute(0)
+        res_host = [[torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in first] for _ in range(npc)]
+        d2h = sum(t.numel() * t.element_size() for rs in res_host for t in rs)
+        s_h2d, s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
 
         def e2e_step():
             go = torch.cuda.Event()
@@ -759,27 +760,21 @@ def main():
             landed = []
             with torch.cuda.stream(s_h2d):
                 for i in range(npc):
-                    sl = slice(i * bs, (i + 1) * bs)
                     for n in names:
-                        dev_in[n][sl].copy_(host[n][sl], non_blocking=True)
+                        dev_in[n][i].copy_(host[n][i], non_blocking=True)
                     e = torch.cuda.Event()
                     e.record(s_h2d)
                     landed.append(e)
             for i in range(npc):
-                sl = slice(i * bs, (i + 1) * bs)
                 stream.wait_event(landed[i])
-                dd = dict(d)
-                dd.update({n: t[sl] for n, t in dev_in.items()})
-                if "state" in d:
-                    dd["state"] = d["state"][sl]
-                o = compute(dd)
+                o = compute(i)
                 e = torch.cuda.Event()
                 e.record(stream)
                 s_d2h.wait_event(e)
                 with torch.cuda.stream(s_d2h):
-                    for src, dst in zip(o[:n_res], res_host):
+                    for src, dst in zip(o, res_host[i]):
                         src.record_stream(s_d2h)
-                        dst[sl].copy_(src, non_blocking=True)
+                        dst.copy_(src, non_blocking=True)
             fin = torch.cuda.Event()
             fin.record(s_d2h)
             stream.wait_event(fin)
@@ -802,7 +797,8 @@ def main():
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             e_ms = float(tt.item())
         e2e = {"value": tokens_per_step / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "steps": k2}
+               "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "steps": k2,
+               "pieces": f"{npc} ({'batch rows' if w['kind'] == 'dense' else 'steps'})"}
 
     # verification (outside the timed region): per-rank checksums of the last
     # step's outputs gathered over NCCL; no collective touches the data path
