@@ -10,7 +10,17 @@ the PKM sequence forward ``pkm_forward`` (cfg3/cfg4) or 12 layers of the decode
 B=32 H=16 T=4096 Dh=64 slots=512, fp16 storage, fp32 accumulation), the
 configuration the headline metric is quoted on.  At N = 1 the line also carries
 a ``workloads`` record: the same device timing and roofline for cfg1, cfg3,
-cfg4, cfg5 and cfg5p.
+cfg4, cfg5 and cfg5p; PKM workloads add ``with_routing``, the step timed with its
+routing (``pkm_fused_forward``: router, pre-pass, recurrence) and the router alone.
+
+``e2e`` is the step through the public routed entry points (``dense_fused_forward``,
+``pkm_fused_forward``) from pinned host inputs k, q, v, beta, with the result read
+back, in pieces whose copies overlap the compute of their neighbours (batch rows
+for dense, steps for PKM with the state carried in place).
+
+``--workload cfg5lm`` runs the fifth config whole: the reference's DeltaGridLM
+(its blocks and LM head, from baseline/_ref) with its recurrence on this drop-in,
+prefill 2048 and greedy decode 512 of the batch of 256 (sharded over the ranks).
 
 Multi-GPU (torchrun, one process per GPU): strong scaling by default -- the
 workload's global batch is split into contiguous batch shards, one per rank,
