@@ -39,7 +39,7 @@ namespace {
 
 constexpr int RT_M = 128;        // tokens per CTA
 constexpr int RT_NMAX = 128;     // router rows per MMA block (256 TMEM columns per CTA: two CTAs per SM)
-constexpr int RT_E = 16;         // most approximate candidates kept per token and axis (top-k + 4)
+constexpr int RT_E = 16;         // most approximate candidates kept per token and axis (k + 4, or 2k above 256 rows)
 constexpr int RT_DH = 64;
 
 constexpr uint32_t SM_KT = 0;                              // K tile: 128 rows x 128 B, 128B swizzle
@@ -146,31 +146,6 @@ __device__ __forceinline__ void halve_sum(float (&v)[NV], int off, bool upper) {
         const float send = upper ? v[i] : v[i + CNT];
         const float keep = upper ? v[i + CNT] : v[i];
         v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-}
-
-// NC fp32 dots over 64 with fused multiply-adds (values only; no ranking depends on them)
-template <int NC, typename LoadX>
-__device__ __forceinline__ void fast_dots(LoadX load_x, const float* const (&w)[NC], float (&out)[NC]) {
-#pragma unroll
-    for (int j = 0; j < NC; ++j) out[j] = 0.f;
-#pragma unroll 2
-    for (int c = 0; c < 8; ++c) {
-        float xv[8];
-        load_x(c, xv);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            float4 wv[NC];
-#pragma unroll
-            for (int j = 0; j < NC; ++j) wv[j] = __ldg(reinterpret_cast<const float4*>(w[j] + 8 * c + 4 * h));
-#pragma unroll
-            for (int j = 0; j < NC; ++j) {
-                out[j] = fmaf(wv[j].x, xv[4 * h + 0], out[j]);
-                out[j] = fmaf(wv[j].y, xv[4 * h + 1], out[j]);
-                out[j] = fmaf(wv[j].z, xv[4 * h + 2], out[j]);
-                out[j] = fmaf(wv[j].w, xv[4 * h + 3], out[j]);
-            }
-        }
     }
 }
 
