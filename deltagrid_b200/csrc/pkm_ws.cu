@@ -21,7 +21,10 @@
 //   roles run concurrently on a ring of R = 2D row slots, synchronised by
 //   mbarriers:
 //   loader (1 warp)  metadata (idx, wk, wq, v, beta, alpha, codes) 16 steps at a
-//       time into a 3-chunk ring, each chunk reloaded once its last update is done.
+//       time into a 3-chunk ring, each chunk reloaded once its last update is done;
+//       once a chunk has landed it turns the codes into each row's shared address (own
+//       ring row, the forwarding writer's row, or the zero row) and each step's
+//       forwarding distances, so the step warps read one word per row.
 //   gather (2 warps for 128-byte row parts, 4 for 64-byte parts)  per step t,
 //       D steps ahead of the update: row-coalesced
 //       cp.async (8 lanes per 128 bytes) of the rows coded "gather" into the
@@ -93,7 +96,7 @@ struct WsParams {
 };
 
 struct MetaLayout {
-    int idx, wk, wq, v, beta, alpha, code, bytes;
+    int idx, wk, wq, v, beta, alpha, code, addr, dmask, bytes;
 };
 
 __host__ __device__ inline MetaLayout meta_layout(int A, int Dh) {
@@ -106,6 +109,8 @@ __host__ __device__ inline MetaLayout meta_layout(int A, int Dh) {
     L.beta = o;  o += 32;
     L.alpha = o; o += 32;
     L.code = o;  o += CHS * 64 * 2;
+    L.addr = o;  o += CHS * 64 * 4;    // per row: shared address of its data for the GEMV and update (loader-made)
+    L.dmask = o; o += CHS * 4;         // per step: distances of the rows it forwards (bit d)
     L.bytes = (o + 127) / 128 * 128;
     return L;
 }
@@ -114,8 +119,8 @@ __host__ __device__ inline MetaLayout meta_layout(int A, int Dh) {
 struct SmemLayout {
     int bars, misc, rows, zrow, rbuf, ystage, meta, total;
 };
-// mbarriers of the recurrence kernel: full[R], done[R], rready[R], mfull[NC], mfree[NC]
-__host__ __device__ constexpr int ws_barriers(int PB, int D) { return 3 * (2 * D) + 2 * NC; }
+// mbarriers of the recurrence kernel: full[R], done[R], rready[R], mfull[NC], mfree[NC], mready[NC]
+__host__ __device__ constexpr int ws_barriers(int PB, int D) { return 3 * (2 * D) + 3 * NC; }
 
 __host__ __device__ inline SmemLayout smem_layout(int PB, int D, int A, int Dh) {
     SmemLayout L;
@@ -385,6 +390,7 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
     uint64_t* rready = done + R;                                    // [R] every slice's r of the step written
     uint64_t* mfull = rready + R;                                   // [NC] metadata chunk landed
     uint64_t* mfree = mfull + NC;                                   // [NC] chunk's last step done by every warp
+    uint64_t* mready = mfree + NC;                                  // [NC] chunk's row-address table written
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SL.misc);
     uint8_t* rows = smem + SL.rows;
     uint8_t* zrow = smem + SL.zrow;
@@ -410,6 +416,7 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
         for (int i = 0; i < NC; ++i) {
             tc::mbar_init(mfull + i, NLOAD);
             tc::mbar_init(mfree + i, KPAR * NSL * 32);
+            tc::mbar_init(mready + i, 1);
         }
         *abort_flag = 0;
     }
@@ -441,15 +448,57 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
             copy(mc + ML.code, p.codes + bt * 64, n * 128);
             cp_async_arrive_noinc(mfull + (c % NC));
         };
+        // once chunk c has landed: each row's shared address for the GEMV and the update
+        // (its own ring row, the forwarding writer's row, or the zero row with bit 0 set
+        // when there is no row) and each step's forwarding distances, so that the step
+        // warps read one word instead of decoding the code
+        const uint32_t rows_u = tc::smem_u32(rows), zrow_u = tc::smem_u32(zrow);
+        auto table = [&](int c) -> bool {
+            const bool ok = ws_wait(mfull + (c % NC), (c / NC) & 1, abort_flag, p.status, p.wait_ns);
+            if (!__all_sync(DG_FULL_MASK, ok)) return false;
+            uint8_t* mc = meta + (c % NC) * ML.bytes;
+            const int t0 = c * CHS, n = min(CHS, T_ - t0);
+            const int16_t* code = reinterpret_cast<const int16_t*>(mc + ML.code);
+            uint32_t* addr = reinterpret_cast<uint32_t*>(mc + ML.addr);
+            uint32_t* dmask = reinterpret_cast<uint32_t*>(mc + ML.dmask);
+            for (int ts = 0; ts < n; ++ts) {
+                const int t = t0 + ts;
+                uint32_t dm = 0;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int m = lane + 32 * h;
+                    const int cd = code[ts * 64 + m];
+                    uint32_t a;
+                    if (cd >= 0) {
+                        const int w = t - (cd >> 6);
+                        a = rows_u + (uint32_t)((w % R) * SLOT + (cd & 63) * RS);
+                        dm |= 1u << (cd >> 6);
+                    } else {
+                        a = cd == -1 ? rows_u + (uint32_t)((t % R) * SLOT + m * RS) : (zrow_u | 1u);
+                    }
+                    addr[ts * 64 + m] = a;
+                }
+                dm = __reduce_or_sync(DG_FULL_MASK, dm);
+                if (lane == 0) dmask[ts] = dm;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(mready + (c % NC));
+            return true;
+        };
         load_chunk(0);
         if (nchunks > 1) load_chunk(1);
-        for (int c = 0; c + 2 < nchunks; ++c) {
-            // chunk c+2 reuses the buffer of chunk c-1
-            if (c >= 1) {
-                const bool ok = ws_wait(mfree + ((c - 1) % NC), ((c - 1) / NC) & 1, abort_flag, p.status, p.wait_ns);
-                if (!__all_sync(DG_FULL_MASK, ok)) break;
+        bool tok = nchunks > 0 ? table(0) : true;
+        for (int c = 0; c + 1 < nchunks && tok; ++c) {
+            tok = table(c + 1);
+            if (!tok) break;
+            if (c + 2 < nchunks) {
+                // chunk c+2 reuses the buffer of chunk c-1
+                if (c >= 1) {
+                    const bool ok = ws_wait(mfree + ((c - 1) % NC), ((c - 1) / NC) & 1, abort_flag, p.status, p.wait_ns);
+                    if (!__all_sync(DG_FULL_MASK, ok)) break;
+                }
+                load_chunk(c + 2);
             }
-            load_chunk(c + 2);
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
     } else if (warp < ROLE_WARPS) {
@@ -459,7 +508,7 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
             const int sl = t % R;
             const int c = t / CHS, ts = t % CHS;
             bool ok = true;
-            if (ts == 0) ok = ws_wait(mfull + (c % NC), (c / NC) & 1, abort_flag, p.status, p.wait_ns);
+            if (ts == 0) ok = ws_wait(mready + (c % NC), (c / NC) & 1, abort_flag, p.status, p.wait_ns);
             if (ok && t >= D) ok = ws_wait(done + ((t - D) % R), ((t - D) / R) & 1, abort_flag, p.status, p.wait_ns);
             if (!ok) break;
             const uint8_t* mc = meta + (c % NC) * ML.bytes;
@@ -517,15 +566,11 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
             const uint8_t* mc = meta + (cn % NC) * ML.bytes;
             bool ok = ws_wait(full + sl, (s / R) & 1, abort_flag, p.status, p.wait_ns);
             if (!__all_sync(DG_FULL_MASK, ok)) break;
-            const int16_t* fw = reinterpret_cast<const int16_t*>(mc + ML.code) + ts * 64;
+            const uint32_t* raddr = reinterpret_cast<const uint32_t*>(mc + ML.addr) + ts * 64;
             // rows forwarded from an earlier step in the window: that step's update (by all
             // of its warps, whatever rows each took) must have finished
             {
-                const int c0 = fw[lane], c1 = fw[lane + 32];
-                uint32_t dm = 0;
-                if (c0 >= 0) dm |= 1u << (c0 >> 6);
-                if (c1 >= 0) dm |= 1u << (c1 >> 6);
-                dm = __reduce_or_sync(DG_FULL_MASK, dm);
+                uint32_t dm = reinterpret_cast<const uint32_t*>(mc + ML.dmask)[ts];
                 while (dm != 0u && ok) {
                     const int d = __ffs(dm) - 1;
                     dm &= dm - 1;
@@ -535,7 +580,6 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
                 }
                 if (!ok) break;
             }
-            const uint32_t own = rows_u + sl * SLOT;
             // ---- GEMV: y and pred of the slice's 16 columns ----
             const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(
                 reinterpret_cast<const uint16_t*>(mc + (g == 0 ? ML.wq : ML.wk)) + ts * A);
@@ -550,12 +594,7 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
                 b[kb][0] = bl ? w0 : 0u;
                 b[kb][1] = bl ? w1 : 0u;
                 const int k = kc * 16 + kk;
-                const int cd = fw[k];
-                const int w = s - (cd >> 6);
-                const uint32_t fwd_row = rows_u + (uint32_t)((w % R) * SLOT + (cd & 63) * RS);
-                uint32_t bs = (cd == -1) ? own + (uint32_t)(k * RS) : zrow_u;
-                bs = (cd >= 0) ? fwd_row : bs;
-                base[kb] = bs + colb;
+                base[kb] = (raddr[k] & ~15u) + colb;
             }
             uint32_t a[4][4];
 #pragma unroll
@@ -602,11 +641,9 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
             for (int i = 0; i < 4; ++i) {
                 const int m = q * RW + ur + RPI * i;           // rows >= A carry code -2 and are skipped
                 const int mcl = min(m, A - 1);
-                const int cd = fw[m];
-                const int w = s - (cd >> 6);
-                const uint32_t fwd_row = rows_u + (uint32_t)((w % R) * SLOT + (cd & 63) * RS);
-                const uint32_t src = (cd >= 0) ? fwd_row : own + (uint32_t)(m * RS);
-                ucd[i] = cd;
+                const uint32_t a = raddr[m];
+                const uint32_t src = a & ~15u;
+                ucd[i] = (a & 1u) ? -2 : 0;
                 ux[i] = midx[mcl];
                 uwk[i] = dg::to_f(mwk[mcl]);
                 uraw[i] = *reinterpret_cast<const uint4*>(rows + (src - rows_u) + uc * 16);
