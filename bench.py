@@ -758,6 +758,10 @@ def main():
             qr = dd["kr"] if w.get("writes") else dd["qr"]
             return ext.pkm_fused_forward(dd["kr"], qr, dd["v"], dd["beta"], d["routers"], d["routers"], None,
                                          d["decay"], d["state"], top_k=w["K"])[:1]     # y of these steps
+        # the first piece's real inputs before the sizing call: PKM carries the state in
+        # place, so routing uninitialised keys would leave non-finite rows behind
+        for n in names:
+            dev_in[n][0].copy_(host[n][0])
         first = compute(0)
         res_host = [[torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in first] for _ in range(npc)]
         d2h = sum(t.numel() * t.element_size() for rs in res_host for t in rs)
