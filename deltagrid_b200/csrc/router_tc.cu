@@ -10,9 +10,10 @@
 //   2. each thread keeps its token's k + 4 (2k above 256 rows) best approximate scores
 //      as 32-bit keys (the score's order-preserving bits with the row in the low bits,
 //      so an insert is one unsigned max/min pair per entry, all entries at once): the
-//      first 32 scores by a
-//      sorting network, then 32 TMEM columns at a time, skipping any 32 whose maximum
-//      is below the last listed score;
+//      first 32 scores by a sorting network, then 32 TMEM columns at a time, skipping
+//      any 32 whose maximum is below the filter -- the last listed score, or if higher
+//      the (k+1)-th listed score less a margin of eight narrow-gap widths (step 3), so
+//      the list holds every score above that filter's final value;
 //   3. exactness: with |approx - exact| <= delta (delta = c * sum|k| * max|W|, c
 //      covering the split residual, the accumulation and the sequential-sum error)
 //      and the keys' truncation below eps, two rows whose listed scores differ by more
@@ -23,7 +24,8 @@
 //      sequential fp32 order of the CPU oracle (each product and sum rounded
 //      separately) and ranked with the lower-index-first tie order
 //      (src/cpp/engine/src/deltagrid_math.cpp:155-167), so indices are exact; a chain
-//      that runs past the last listed candidate rescans every row;
+//      that runs past the last listed candidate, or comes within one gap width of the
+//      filter's final value (below which the list may lack scores), rescans every row;
 //   4. u_k (the top scores, exact where rescored, else the listed ones: relative error
 //      below 2^(bits of G - 23), inside the outputs' 16-bit rounding), u_q (each query
 //      dot split over eight lanes, so a warp reads whole router rows), normalisation,
@@ -82,6 +84,11 @@ __device__ __forceinline__ uint32_t cand_key(float s, int row, uint32_t imask) {
     const uint32_t u = __float_as_uint(s);
     const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
     return (o & ~imask) | (imask - (uint32_t)row);
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
 }
 // a[0 .. N) sorted descending by a bitonic network (compile-time compare-exchanges)
 template <int N>
@@ -246,10 +253,14 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
     static_assert(E >= K + 4 && E <= RT_E, "candidate list length");
     const int ib = 32 - __clz(G - 1);
     const uint32_t imask = (1u << ib) - 1u;
+    // every score within mg below the (k+1)-th listed one is kept: mg is eight widths of
+    // the narrow gap (2 delta + the keys' truncation) at this token's largest |score|
+    const float wmx = __uint_as_float(p.wmax[ax]);
+    const float mg = 8.f * (2.f * p.delta_scale * kabs * wmx + ldexpf(kabs * wmx * 1.01f, ib - 22));
     uint32_t lk[E];
 #pragma unroll
     for (int i = 0; i < E; ++i) lk[i] = 0u;
-    float thr = -INFINITY;                         // truncated score of the 16th key
+    float thr = -INFINITY;                         // the filter: max(E-th key, (k+1)-th key - mg)
     uint32_t* st = stash + ax * 16 * RT_M;
 
     for (int j = 0; j < nb; ++j) {
@@ -275,7 +286,7 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
             pend_w = (int)((j + 1) & 1);
         }
         // 32 scores per TMEM read; a score enters the list only if it is at least the
-        // 16th's truncated score, which after the first columns few are
+        // filter, which after the first columns few are
         const int gbase = j * nrows;
         for (int c0 = 0; c0 < nrows && !bad; c0 += 32) {
             uint32_t r[32];
@@ -300,17 +311,19 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
                         }
 #pragma unroll
                 for (int i = 0; i < E; ++i) lk[i] = r[i];
-                thr = key_value(lk[E - 1], imask);
+                thr = fmaxf(key_value(lk[E - 1], imask), key_value(lk[K], imask) - mg);
                 continue;
             }
-            float mt[16];
+            // the 32 scores' maximum by three-input maxima (16 instead of 31)
+            float mt[12];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) mt[i] = fmaxf(__uint_as_float(r[i]), __uint_as_float(r[i + 16]));
+            for (int i = 0; i < 10; ++i)
+                mt[i] = fmax3(__uint_as_float(r[3 * i]), __uint_as_float(r[3 * i + 1]), __uint_as_float(r[3 * i + 2]));
+            mt[10] = __uint_as_float(r[30]);
+            mt[11] = __uint_as_float(r[31]);
 #pragma unroll
-            for (int w = 8; w > 0; w >>= 1)
-#pragma unroll
-                for (int i = 0; i < w; ++i) mt[i] = fmaxf(mt[i], mt[i + w]);
-            const float mx = mt[0];
+            for (int i = 0; i < 4; ++i) mt[i] = fmax3(mt[3 * i], mt[3 * i + 1], mt[3 * i + 2]);
+            const float mx = fmaxf(fmax3(mt[0], mt[1], mt[2]), mt[3]);
             if (!(mx >= thr)) continue;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -318,20 +331,27 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
 #pragma unroll
                 for (int i = 0; i < 16; ++i) m |= (__uint_as_float(r[16 * h + i]) >= thr ? 1u : 0u) << i;
                 if (m != 0u) {
+                // the half's 16 scores in this thread's 64-byte stash row, 16-byte chunks
+                // rotated by lane pair so that eight lanes' stores hit distinct banks
+                uint8_t* srb = reinterpret_cast<uint8_t*>(st) + t * 64;
+                const int sw = (t >> 1) & 3;
 #pragma unroll
-                for (int i = 0; i < 16; ++i) st[i * RT_M + t] = r[16 * h + i];
+                for (int c = 0; c < 4; ++c)
+                    *reinterpret_cast<uint4*>(srb + 16 * (c ^ sw)) =
+                        make_uint4(r[16 * h + 4 * c], r[16 * h + 4 * c + 1], r[16 * h + 4 * c + 2], r[16 * h + 4 * c + 3]);
 #pragma unroll 1
                 while (m != 0u) {
                     const int i = __ffs(m) - 1;
                     m &= m - 1;
-                    const uint32_t key = cand_key(__uint_as_float(st[i * RT_M + t]), gbase + c0 + 16 * h + i, imask);
+                    const uint32_t sv = *reinterpret_cast<const uint32_t*>(srb + 16 * ((i >> 2) ^ sw) + 4 * (i & 3));
+                    const uint32_t key = cand_key(__uint_as_float(sv), gbase + c0 + 16 * h + i, imask);
                     // sorted insert without a dependency chain: entry q becomes
                     // max(old q, min(key, old q-1))
 #pragma unroll
                     for (int q = E - 1; q > 0; --q) lk[q] = max(lk[q], min(key, lk[q - 1]));
                     lk[0] = max(lk[0], key);
                 }
-                thr = key_value(lk[E - 1], imask);
+                thr = fmaxf(key_value(lk[E - 1], imask), key_value(lk[K], imask) - mg);
                 }
             }
         }
@@ -358,13 +378,17 @@ __global__ void __launch_bounds__(2 * RT_M, 2)
     // plus the keys' truncation (below 2^ib units in the last place of any listed score)
     const float d2 = 2.f * delta + ldexpf(fmaxf(fabsf(lv[0]), fabsf(lv[E - 1])), ib - 22) + 1e-30f;
     uint32_t need = 0;                                    // list positions to rescore
+    // the list holds every score at or above ff (the scan kept all within mg of the
+    // final (k+1)-th); a chain that comes within d2 of ff may miss one: every row
+    const float ff = lv[K] - mg;
 #pragma unroll
     for (int i = 0; i < E - 1; ++i) {
         const bool narrow = !(lv[i] - lv[i + 1] > d2);    // (also when scores are equal or not finite)
         if (i < K) {
             if (narrow) need |= 3u << i;
-        } else if (narrow && ((need >> i) & 1u)) {
-            need |= 1u << (i + 1);
+        } else if ((need >> i) & 1u) {
+            if (!(lv[i] - d2 >= ff)) need |= 1u << (E - 1);
+            else if (narrow) need |= 1u << (i + 1);
         }
     }
     float tv[K];
@@ -666,7 +690,8 @@ bool route_tc_supports(int dtype, int dh, int g0, int g1, int top_k, const void*
     auto rows = [](int g) { return g <= RT_NMAX ? g : RT_NMAX; };
     if (rows(g0) != rows(g1)) return false;
     const int nr = rows(g0);
-    if (nr % 16 != 0 || g0 % nr != 0 || g1 % nr != 0 || nr < 32) return false;
+    // the scan reads the scores 32 columns at a time: whole 32-row groups per block
+    if (nr % 32 != 0 || g0 % nr != 0 || g1 % nr != 0) return false;
     // inputs for TMA and 16-byte loads; outputs for the 16-byte (top-8) / 8-byte stores
     const uintptr_t al = (uintptr_t)k | (uintptr_t)q | (uintptr_t)rk0 | (uintptr_t)rk1 | (uintptr_t)rq0 |
                          (uintptr_t)rq1 | (uintptr_t)wk | (uintptr_t)wq | (uintptr_t)idx;

@@ -21,7 +21,10 @@ def _routers(G0, G1, Dh, seed):
 
 
 @pytest.mark.parametrize("G,K,dtype", [(128, 8, torch.float16), (1024, 8, torch.float16),
-                                       (64, 4, torch.float32), (32, 8, torch.bfloat16)])
+                                       (64, 4, torch.float32), (32, 8, torch.bfloat16),
+                                       # grids of whole 16-row but not 32-row groups, and 32-row blocks
+                                       (48, 8, torch.float16), (80, 4, torch.bfloat16), (96, 8, torch.float16),
+                                       (160, 8, torch.float16)])
 def test_router_vs_oracle(G, K, dtype):
     B, H, T, Dh = 2, 3, 40, 64
     g = torch.Generator().manual_seed(G + K)
