@@ -606,6 +606,8 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (small profiling cases)")
     ap.add_argument("--seq", type=int, default=0, help="override the sequence length T (small profiling cases)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-pieces", type=int, default=0,
+                    help="pieces of the end-to-end step (dense: batch rows, PKM: steps); 0 picks the default")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-workloads", action="store_true", help="skip the other workloads' record (N = 1)")
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
@@ -731,18 +733,32 @@ def main():
         # slot projections (dense_fused_forward) or the product-key router (pkm_fused_forward)
         # (the write stream's queries are its keys: copied once).  The step runs in pieces
         # so that the copy in of piece i+1 and the copy out of piece i-1 (their own streams)
-        # overlap piece i's compute: dense by batch rows (lanes are independent; each piece
-        # still gets whole CTAs, and eight pieces' compute stays under the copies), PKM by
-        # steps (the state is carried in place from piece to piece, which is how the
-        # recurrence treats consecutive calls anyway: rows are rounded to the storage type
-        # every step, so the pieces give the unsplit call's results bit for bit).
+        # overlap piece i's compute; what stays exposed is the first piece's copy in and the
+        # last piece's compute and copy out.  Dense by batch rows: a piece's compute is one
+        # chain of chunks whatever its lanes, so the pieces are few, the first and the last
+        # small (B/16 rows) and the middle four even.  PKM by steps, eight even pieces (the
+        # state is carried in place from piece to piece, which is how the recurrence treats
+        # consecutive calls anyway: rows are rounded to the storage type every step, so the
+        # pieces give the unsplit call's results bit for bit).
         names = ("kr", "v", "beta") if w.get("writes") else ("kr", "qr", "v", "beta")
         if w["kind"] == "dense":
-            npc = next(n for n in (8, 4, 2, 1) if w["B"] % n == 0)
-            cut = lambda t, i: t[i * (w["B"] // npc):(i + 1) * (w["B"] // npc)]
+            Bp = w["B"]
+            if args.e2e_pieces:
+                npc = next(n for n in (args.e2e_pieces, 1) if Bp % n == 0)
+                sizes = [Bp // npc] * npc
+            elif Bp >= 16:
+                edge = Bp // 16
+                mid = Bp - 2 * edge
+                sizes = [edge] + [mid // 4 + (1 if i < mid % 4 else 0) for i in range(4)] + [edge]
+            else:
+                sizes = [1] * Bp
+            bounds = [(sum(sizes[:i]), sum(sizes[:i + 1])) for i in range(len(sizes))]
+            cut = lambda t, i: t[bounds[i][0]:bounds[i][1]]
         else:
-            npc = next(n for n in (4, 2, 1) if w["T"] % (8 * n) == 0)
-            cut = lambda t, i: t[:, :, i * (w["T"] // npc):(i + 1) * (w["T"] // npc)]
+            npc = next(n for n in ((args.e2e_pieces,) if args.e2e_pieces else (8, 4, 2, 1)) if w["T"] % (8 * n) == 0)
+            bounds = [(i * (w["T"] // npc), (i + 1) * (w["T"] // npc)) for i in range(npc)]
+            cut = lambda t, i: t[:, :, bounds[i][0]:bounds[i][1]]
+        npc = len(bounds)
         # pinned host inputs and device buffers, one contiguous block per piece
         host = {n: [cut(d[n], i).to("cpu").contiguous().pin_memory() for i in range(npc)] for n in names}
         h2d = sum(t.numel() * t.element_size() for ts in host.values() for t in ts)
@@ -758,12 +774,20 @@ def main():
             qr = dd["kr"] if w.get("writes") else dd["qr"]
             return ext.pkm_fused_forward(dd["kr"], qr, dd["v"], dd["beta"], d["routers"], d["routers"], None,
                                          d["decay"], d["state"], top_k=w["K"])[:1]     # y of these steps
+
+        def piece_shape(shape, i):
+            # the sizing call's output shapes with piece i's rows (dense, dim 0) or steps (PKM, dim 2)
+            dim = 0 if w["kind"] == "dense" else 2
+            shape = list(shape)
+            shape[dim] = bounds[i][1] - bounds[i][0]
+            return shape
         # the first piece's real inputs before the sizing call: PKM carries the state in
         # place, so routing uninitialised keys would leave non-finite rows behind
         for n in names:
             dev_in[n][0].copy_(host[n][0])
         first = compute(0)
-        res_host = [[torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in first] for _ in range(npc)]
+        res_host = [[torch.empty(piece_shape(o.shape, i), dtype=o.dtype, pin_memory=True) for o in first]
+                    for i in range(npc)]
         d2h = sum(t.numel() * t.element_size() for rs in res_host for t in rs)
         s_h2d, s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
 
@@ -812,7 +836,8 @@ def main():
             e_ms = float(tt.item())
         e2e = {"value": tokens_per_step / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "steps": k2,
-               "pieces": f"{npc} ({'batch rows' if w['kind'] == 'dense' else 'steps'})"}
+               "pieces": f"{npc} ({'batch rows' if w['kind'] == 'dense' else 'steps'}: "
+                         f"{[hi - lo for lo, hi in bounds]})"}
 
     # verification (outside the timed region): per-rank checksums of the last
     # step's outputs gathered over NCCL; no collective touches the data path
