@@ -5,7 +5,13 @@
 // r = beta (v - pred), scatter S[idx_t] = cast(alpha s + (r) wk), rows rounded to
 // the storage dtype every step.
 //
-// Two kernels, launched back to back on the caller's stream:
+// Two kernels.  For a short sequence, or when the recurrence fills every SM, they run
+// back to back on the caller's stream.  Otherwise the call runs in four step pieces:
+// the pre-pass of piece i + 1 runs on a low-priority side stream while the
+// recurrence of piece i runs on a high-priority one, on the SMs the recurrence leaves
+// free, so only the first piece's pre-pass stays on the critical path.  A piece
+// boundary only turns forwards into gathers (the previous piece's rows are in global
+// memory by then), so the pieces give the unsplit call's results bit for bit.
 //
 // pkm_hazard_kernel -- index-only pre-pass over all SMs.  For every row (t, m)
 //   of every lane it finds the last earlier step w in [t-D+1, t-1] that wrote
@@ -50,6 +56,8 @@
 // row whose last writer is in the window is read from the writer's ring slot,
 // which the slot's next gather (for step w+R, issued after update w+R-D >= w+D)
 // cannot overwrite before every reader (steps <= w+D-1) is done.
+#include <mutex>
+
 #include "dg_common.cuh"
 #include "tc_util.cuh"
 
@@ -93,6 +101,8 @@ struct WsParams {
     const int16_t* codes;       // [lanes, T, 64] from pkm_hazard_kernel
     void* saved;                // [lanes, T, A, Dh] rows as gathered at each step, or null
     uint64_t wait_ns;           // bound of one wait (wall time); 0 gives up without waiting
+    int64_t lstride;            // steps between lanes in the per-step arrays (the whole sequence's T)
+    int tbase;                  // first step of this call's piece; T counts the piece's steps
 };
 
 struct MetaLayout {
@@ -150,14 +160,15 @@ __device__ __forceinline__ uint32_t slot_home(uint32_t x) {
 }
 
 // ---------------------------------------------------------------------------
-// pre-pass: row codes of steps [blockIdx.x * HZ_STEPS, +HZ_STEPS) of lane blockIdx.y.
+// pre-pass: row codes of steps [blockIdx.x * HZ_STEPS, +HZ_STEPS) of lane blockIdx.y (of the piece).
 // The block's (slot, step, position) entries are bucket-sorted in shared memory
 // (one 32-bit atomicAdd per entry gives its rank in its bucket, a block prefix sum
 // the bucket starts), then every row scans its bucket for the latest earlier step
 // with the same slot.  Exact: there is no capacity limit to overflow.
 template <int A>
 __global__ void __launch_bounds__(HZ_THREADS, 3) pkm_hazard_kernel(const int64_t* __restrict__ idx, int16_t* codes,
-                                                                int32_t* status, int T, int64_t total, int D) {
+                                                                int32_t* status, int T, int64_t total, int D,
+                                                                int64_t lstride, int tbase) {
     extern __shared__ __align__(16) uint8_t hz_smem[];
     uint32_t* cnt = reinterpret_cast<uint32_t*>(hz_smem);                 // [HZ_BUCKETS] entries per bucket
     uint32_t* start = cnt + HZ_BUCKETS;                                    // [HZ_BUCKETS] first entry of a bucket
@@ -169,8 +180,9 @@ __global__ void __launch_bounds__(HZ_THREADS, 3) pkm_hazard_kernel(const int64_t
     const int tb = max(0, t0 - (D - 1));
     const int te = min(T, t0 + HZ_STEPS);
     const int nE = (te - tb) * A;
-    const int64_t* li = idx + ((int64_t)lid * T + tb) * A;
-    int16_t* lc = codes + (int64_t)lid * T * 64;
+    // steps [tbase, tbase + T) of a lane whose arrays hold lstride steps
+    const int64_t* li = idx + ((int64_t)lid * lstride + tbase + tb) * A;
+    int16_t* lc = codes + ((int64_t)lid * lstride + tbase) * 64;
     for (int i = tid; i < HZ_BUCKETS; i += HZ_THREADS) cnt[i] = 0u;
     uint32_t key[HZ_KMAX], bkt[HZ_KMAX];
 #pragma unroll
@@ -401,7 +413,7 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int lane_bh = blockIdx.y, part = blockIdx.x;
     const int A = p.A, Dh = p.Dh, T_ = p.T;
-    const int64_t lt0 = (int64_t)lane_bh * T_;
+    const int64_t lt0 = (int64_t)lane_bh * p.lstride + p.tbase;   // this lane's first step of the piece
     const int64_t row_bytes = (int64_t)Dh * 2;
     const int nchunks = (T_ + CHS - 1) / CHS;
     uint8_t* gstate = reinterpret_cast<uint8_t*>(p.state) + (int64_t)lane_bh * p.total * row_bytes + (int64_t)part * PB;
@@ -742,6 +754,37 @@ bool pkm_ws_supports(int dtype, int B, int H, int T, int A, int64_t total, int D
     return (al & 15) == 0;
 }
 
+namespace {
+
+// the pipelined call's streams and events, one set per device, created on first use
+struct SideStreams {
+    cudaStream_t pre = nullptr, rec = nullptr;   // pre-pass (lowest priority), recurrence (highest)
+    cudaEvent_t fork = nullptr, join = nullptr, ready[4] = {};
+};
+SideStreams g_side[64];
+std::mutex g_side_mu;
+
+int side_streams(int dev, SideStreams** out) {
+    SideStreams& ss = g_side[dev];
+    if (!ss.pre) {
+        int least = 0, greatest = 0;
+        cudaError_t e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+        if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&ss.pre, cudaStreamNonBlocking, least);
+        if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&ss.rec, cudaStreamNonBlocking, greatest);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming);
+        for (int i = 0; i < 4 && e == cudaSuccess; ++i) e = cudaEventCreateWithFlags(&ss.ready[i], cudaEventDisableTiming);
+        if (e != cudaSuccess) {
+            ss = SideStreams{};            // (a partial set is not reused; its handles are dropped)
+            return dg_host::record_cuda_error(e);
+        }
+    }
+    *out = &ss;
+    return DG_OK;
+}
+
+}  // namespace
+
 // workspace: pkm_ws_workspace_bytes(B, H, T) bytes, 16-byte aligned
 int pkm_forward_ws(int dtype, int B, int H, int T, int A, int64_t total, int Dh, const void* v, const void* beta,
                    const void* wk, const void* wq, const int64_t* idx, const void* decay, int dynamic_decay,
@@ -752,25 +795,79 @@ int pkm_forward_ws(int dtype, int B, int H, int T, int A, int64_t total, int Dh,
     const int lanes = B * H;
     int16_t* codes = static_cast<int16_t*>(workspace);
     const int hz_smem = (2 * HZ_BUCKETS + 32) * 4 + HZ_ENTRIES * 8;
-    const dim3 hz_grid((T + HZ_STEPS - 1) / HZ_STEPS, lanes);
     auto hz = A == 16 ? pkm_hazard_kernel<16> : A == 32 ? pkm_hazard_kernel<32> : A == 48 ? pkm_hazard_kernel<48>
                                                                                          : pkm_hazard_kernel<64>;
     cudaError_t e = cudaFuncSetAttribute(hz, cudaFuncAttributeMaxDynamicSharedMemorySize, hz_smem);
     if (e != cudaSuccess) return record_cuda_error(e);
-    hz<<<hz_grid, HZ_THREADS, hz_smem, stream>>>(idx, codes, status, T, total, D);
-    int rc = check_launch();
-    if (rc != DG_OK) return rc;
     // the default poll budget (2^22) maps to 2 s of waiting; 0 gives up at once
     const uint64_t wait_ns = (uint64_t)wait_limit() * 2000000000ull / (1ull << 22);
-    WsParams p{v, beta, wk, wq, idx, decay, state, out, status, H, T, A, Dh, parts, total, dynamic_decay, codes, saved,
-               wait_ns};
-    if (dtype == DG_DTYPE_F16)
-        return PB == 128 ? launch_ws<__half, 128, kDepthFull>(p, lanes, stream)
-                         : launch_ws<__half, 64, kDepthHalf>(p, lanes, stream);
-    if (dtype == DG_DTYPE_BF16)
-        return PB == 128 ? launch_ws<__nv_bfloat16, 128, kDepthFull>(p, lanes, stream)
-                         : launch_ws<__nv_bfloat16, 64, kDepthHalf>(p, lanes, stream);
-    return DG_ERR_UNSUPPORTED;
+    auto prepass = [&](int t0, int n, cudaStream_t s) -> int {
+        const dim3 hz_grid((n + HZ_STEPS - 1) / HZ_STEPS, lanes);
+        hz<<<hz_grid, HZ_THREADS, hz_smem, s>>>(idx, codes, status, n, total, D, (int64_t)T, t0);
+        return check_launch();
+    };
+    auto recurrence = [&](int t0, int n, cudaStream_t s) -> int {
+        WsParams p{v, beta, wk, wq, idx, decay, state, out, status, H, n, A, Dh, parts, total, dynamic_decay, codes,
+                   saved, wait_ns, (int64_t)T, t0};
+        if (dtype == DG_DTYPE_F16)
+            return PB == 128 ? launch_ws<__half, 128, kDepthFull>(p, lanes, s)
+                             : launch_ws<__half, 64, kDepthHalf>(p, lanes, s);
+        if (dtype == DG_DTYPE_BF16)
+            return PB == 128 ? launch_ws<__nv_bfloat16, 128, kDepthFull>(p, lanes, s)
+                             : launch_ws<__nv_bfloat16, 64, kDepthHalf>(p, lanes, s);
+        return DG_ERR_UNSUPPORTED;
+    };
+    // pipelined when the sequence is long and the recurrence leaves SMs free for the
+    // pre-pass (its CTAs and the recurrence's do not share an SM)
+    int dev = 0, sms = 0;
+    e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    int rc = sm_count(dev, &sms);
+    if (rc != DG_OK) return rc;
+    constexpr int NP = 4;
+    const bool pipelined = T >= 1024 && T % (NP * 8) == 0 && lanes * parts + 8 <= sms && dev >= 0 && dev < 64;
+    std::unique_lock<std::mutex> lock(g_side_mu, std::defer_lock);   // the device's events are reused call after call
+    SideStreams* ss = nullptr;
+    if (pipelined) {
+        lock.lock();
+        // the side streams are made on the device's first pipelined call; a first call
+        // made while the caller's stream is capturing runs unpipelined instead
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        e = cudaStreamIsCapturing(stream, &cs);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        if (g_side[dev].pre || cs == cudaStreamCaptureStatusNone) {
+            rc = side_streams(dev, &ss);
+            if (rc != DG_OK) return rc;
+        }
+    }
+    if (!ss) {
+        rc = prepass(0, T, stream);
+        return rc != DG_OK ? rc : recurrence(0, T, stream);
+    }
+    const int L = T / NP;                             // a multiple of 8
+    // fork: both side streams follow the work already on the caller's stream
+    e = cudaEventRecord(ss->fork, stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ss->pre, ss->fork, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ss->rec, ss->fork, 0);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    for (int i = 0; i < NP && rc == DG_OK; ++i) {
+        rc = prepass(i * L, L, ss->pre);
+        if (rc != DG_OK) break;
+        e = cudaEventRecord(ss->ready[i], ss->pre);
+        if (e != cudaSuccess) { rc = record_cuda_error(e); break; }
+    }
+    for (int i = 0; i < NP && rc == DG_OK; ++i) {
+        e = cudaStreamWaitEvent(ss->rec, ss->ready[i], 0);
+        if (e != cudaSuccess) { rc = record_cuda_error(e); break; }
+        rc = recurrence(i * L, L, ss->rec);
+    }
+    // join: the caller's stream follows both side streams, whatever happened above
+    e = cudaEventRecord(ss->fork, ss->pre);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, ss->fork, 0);
+    if (e == cudaSuccess) e = cudaEventRecord(ss->join, ss->rec);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, ss->join, 0);
+    if (rc != DG_OK) return rc;
+    return e == cudaSuccess ? DG_OK : record_cuda_error(e);
 }
 
 }  // namespace dg_host

@@ -150,6 +150,28 @@ def test_ws_crowded_chains_exact(crowd, period):
     assert rel_err(st.float().cpu().numpy(), so) < 1e-3
 
 
+def test_ws_step_pieces_exact():
+    """Long calls run as step pieces (the index pre-pass of the next piece beside the
+    recurrence of this one).  Crowded chains cross the piece boundaries; the result
+    matches the oracle, and splitting the call in two gives the same bits."""
+    d = _crowded_inputs(2048, 64, 1 << 16, 6, 4, seed=13)
+    out, st = _run(d, WS)
+    assert ext.device_status(clear=True) == 0
+    yo, so = _oracle(d, torch.float16)
+    assert rel_err(out.float().cpu().numpy(), yo) < 1e-3
+    assert rel_err(st.float().cpu().numpy(), so) < 1e-3
+    g = {n: t.cuda() for n, t in d.items()}
+    ys = []
+    state = g["state"].clone()
+    for a, b in ((0, 1024), (1024, 2048)):
+        y, state, _ = ext.pkm_forward_algo(*(g[n][:, :, a:b].contiguous() for n in ("v", "beta", "wk", "wq", "idx")),
+                                           g["decay"], state, False, WS)
+        ys.append(y)
+    torch.cuda.synchronize()
+    assert ext.device_status(clear=True) == 0
+    assert torch.equal(torch.cat(ys, dim=2), out) and torch.equal(state, st)
+
+
 def test_ws_rejects_uncovered_shapes():
     d = pkm_inputs(1, 1, 100, 8, 4, 64, torch.float16, seed=1)      # T % 8 != 0
     with pytest.raises(_lib.DeltaGridError):
