@@ -226,13 +226,28 @@ def make_inputs(w, torch, device, seed=0):
     return dict(v=v, beta=beta, wk=wk, wq=wq, idx=idx, decay=decay, state=state, kr=kr, qr=qr, routers=routers)
 
 
-def launches_per_step(w):
+def _sm_count():
+    try:
+        import torch
+        return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    except Exception:
+        return 148
+
+
+def launches_per_step(w, sms=None):
     """Kernels one step launches: the dense kernel; for 16-bit PKM the hazard pre-pass
-    and the recurrence (pkm_hazard_kernel, pkm_ws_kernel); for decode one step kernel
-    per layer (dense_step_vec_kernel)."""
+    and the recurrence (pkm_hazard_kernel, pkm_ws_kernel), four pieces of each when
+    the call is long and the recurrence leaves 8 SMs free (one CTA per lane for 120
+    lanes or more, else two: the rule of pkm_ws.cu); for decode one step kernel per
+    layer (dense_step_vec_kernel)."""
     if w["kind"] == "decode":
         return w["L"]
-    return 2 if w["kind"] == "pkm" and w["dtype"] != "float32" else w.get("L", 1)
+    if w["kind"] == "pkm" and w["dtype"] != "float32":
+        sms = sms if sms is not None else _sm_count()
+        lanes = w["B"] * w["H"]
+        ctas = lanes * (1 if lanes >= 120 else 2)
+        return 8 if w["T"] >= 1024 and w["T"] % 32 == 0 and ctas + 8 <= sms else 2
+    return w.get("L", 1)
 
 
 def run_step(ext, w, d, algo=0):
