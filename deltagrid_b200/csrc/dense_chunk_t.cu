@@ -220,6 +220,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (lane == 0) dst[256] = cs.atot;
         };
         if (warp == 0 && NC > 0) chunk_gates(0);
+        // chunk c's y (this thread's 32 steps of its row, packed in pairs) is formed once
+        // P4 and P5 are done and written to the y tile while chunk c + 1 waits for its
+        // [K;Q] S0 product, so the tile stores and the TMA store are off the chain
+        uint32_t ypk[16];
+        int ypend = -1;                          // first step of the chunk whose y awaits its store
+        auto y_store = [&]() {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const int t = cb + i;
+                const uint32_t pr = ypk[i >> 1];
+                const uint16_t hv = (i & 1) ? (uint16_t)(pr >> 16) : (uint16_t)(pr & 0xffffu);
+                *reinterpret_cast<uint16_t*>(yt + t * 128 + ((((row >> 3) ^ (t & 7))) << 4) + (row & 7) * 2) = hv;
+            }
+            tc::fence_proxy_async();
+            tc::group_sync(BAR_WG0);
+            if (tid == 0) {
+                tc::tma_store_3d(&tmy, yt, 0, ypend, lane_bh);
+                tc::bulk_commit_group();
+            }
+            ypend = -1;
+        };
         for (int c = 0; c < NC && !failed; ++c) {
             const int t0 = c * CH;
             const uint32_t par = (uint32_t)(c & 1);
@@ -266,6 +287,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 warp_arrive(bars + B_CV0 + g2, lane);
             }
             if (warp == 0 && c + 1 < NC) chunk_gates(c + 1);
+            // the previous chunk's y tile (its update has read the R'^T tile it shares)
+            if (ypend >= 0) y_store();
             // X^T = V^T - (K S0)^T diag(aprev) -> 16-bit P3 operand in TMEM
             bad = !wait_bar(bars + B_P2, par, lim, abort_flag) || !wait_bar(bars + B_V, par, lim, abort_flag);
             if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
@@ -335,20 +358,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tc::tmem_ld16x2_32(tq0 + Ly::D2 + 64, qs);
                 tc::tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int t = cb + i;
-                    *reinterpret_cast<TI*>(yt + t * 128 + ((((row >> 3) ^ (t & 7))) << 4) + (row & 7) * 2) =
-                        dg::from_f<TI>(fmaf(sc0[t], __uint_as_float(qs[i]), __uint_as_float(yi[i])));
+                for (int i = 0; i < 16; ++i) {
+                    const int t = cb + 2 * i;
+                    ypk[i] = Io<TI>::pack2(fmaf(sc0[t], __uint_as_float(qs[2 * i]), __uint_as_float(yi[2 * i])),
+                                           fmaf(sc0[t + 1], __uint_as_float(qs[2 * i + 1]), __uint_as_float(yi[2 * i + 1])));
                 }
             }
-            tc::fence_proxy_async();
-            tc::tc_fence_before();
-            tc::group_sync(BAR_WG0);
-            if (tid == 0) {
-                tc::tma_store_3d(&tmy, yt, 0, t0, lane_bh);
-                tc::bulk_commit_group();
-            }
+            ypend = t0;
         }
+        if (!failed && ypend >= 0) y_store();    // the last chunk's y
         if (tid == 0) tc::bulk_wait0();
         // final state: S^T -> s_final / s_final_f through a shared-memory transpose (the K/Q tiles are free)
         if (!failed && NC > 0) {
