@@ -289,8 +289,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (warp == 0 && c + 1 < NC) chunk_gates(c + 1);
             // the previous chunk's y tile (its update has read the R'^T tile it shares)
             if (ypend >= 0) y_store();
-            // X^T = V^T - (K S0)^T diag(aprev) -> 16-bit P3 operand in TMEM
-            bad = !wait_bar(bars + B_P2, par, lim, abort_flag) || !wait_bar(bars + B_V, par, lim, abort_flag);
+            // X^T = V^T - (K S0)^T diag(aprev) -> 16-bit P3 operand in TMEM.  This thread's V
+            // values and aprev are read while [K;Q] S0 is still in the tensor pipe
+            bad = !wait_bar(bars + B_V, par, lim, abort_flag);
+            if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
+            float xv[32], xa[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const int t = cb + i;
+                xv[i] = dg::to_f(*reinterpret_cast<const TI*>(vt + t * 128 + ((((row >> 3) ^ (t & 7))) << 4) + (row & 7) * 2));
+                xa[i] = sc0[t];
+            }
+            bad = !wait_bar(bars + B_P2, par, lim, abort_flag);
             if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
             tc::tc_fence_after();
             {
@@ -298,17 +308,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tc::tmem_ld16x2_32(tq0 + Ly::D2, r);
                 tc::tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int t = cb + 2 * i;
-                    const float v0 = dg::to_f(*reinterpret_cast<const TI*>(vt + t * 128 + ((((row >> 3) ^ (t & 7))) << 4) + (row & 7) * 2));
-                    const float v1 = dg::to_f(*reinterpret_cast<const TI*>(vt + (t + 1) * 128 + ((((row >> 3) ^ ((t + 1) & 7))) << 4) + (row & 7) * 2));
-                    pk[i] = pack_h2(v0 - sc0[t] * __uint_as_float(r[2 * i]), v1 - sc0[t + 1] * __uint_as_float(r[2 * i + 1]));
-                }
+                for (int i = 0; i < 16; ++i)
+                    pk[i] = pack_h2(xv[2 * i] - xa[2 * i] * __uint_as_float(r[2 * i]),
+                                    xv[2 * i + 1] - xa[2 * i + 1] * __uint_as_float(r[2 * i + 1]));
                 tc::tmem_st16x2_16(tq0 + Ly::XA, pk);
                 tc::tmem_wait_st();
             }
             warp_arrive(bars + B_XD, lane);
-            // residuals: err_out, R'^T (update operand, smem), (beta R)^T (P4 operand, TMEM)
+            // residuals: err_out, R'^T (update operand, smem), (beta R)^T (P4 operand, TMEM); the
+            // chunk scalars they take are read while R^T = X^T T^T is in the tensor pipe
+            float rg[32], rb[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                rg[i] = sc0[128 + cb + i] * sc0[64 + cb + i];
+                rb[i] = sc0[64 + cb + i];
+            }
             bad = !wait_bar(bars + B_P3, par, lim, abort_flag);
             if (tid == 0) tc::bulk_wait_read0();      // the previous chunk's y store has read the shared tile
             if (tc::group_sync_or(BAR_WG0, bad)) { failed = true; break; }
@@ -329,10 +343,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {
-                    const int t = cb + 8 * cc;
                     float rp[8];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) rp[e] = sc0[128 + t + e] * sc0[64 + t + e] * rr[8 * cc + e];
+                    for (int e = 0; e < 8; ++e) rp[e] = rg[8 * cc + e] * rr[8 * cc + e];
                     *reinterpret_cast<uint4*>(rt + tc::sw128(row, 4 * half + cc)) =
                         make_uint4(Io<TI>::pack2(rp[0], rp[1]), Io<TI>::pack2(rp[2], rp[3]),
                                    Io<TI>::pack2(rp[4], rp[5]), Io<TI>::pack2(rp[6], rp[7]));
@@ -343,7 +356,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
 #pragma unroll
                 for (int i = 0; i < 16; ++i)
-                    pk[i] = pack_h2(sc0[64 + cb + 2 * i] * rr[2 * i], sc0[64 + cb + 2 * i + 1] * rr[2 * i + 1]);
+                    pk[i] = pack_h2(rb[2 * i] * rr[2 * i], rb[2 * i + 1] * rr[2 * i + 1]);
                 tc::tmem_st16x2_16(tq0 + Ly::BA, pk);
                 tc::tmem_wait_st();
             }
