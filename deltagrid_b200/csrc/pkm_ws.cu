@@ -572,131 +572,269 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
         const uint32_t zrow_u = tc::smem_u32(zrow);
         T* gout = static_cast<T*>(p.out);
         const float alpha_static = p.dynamic_decay ? 1.f : dg::to_f(static_cast<const T*>(p.decay)[lane_bh % p.H]);
-        for (int s = par; s < T_; s += KPAR) {
-            const int sl = s % R;
-            const int cn = s / CHS, ts = s % CHS;
-            const uint8_t* mc = meta + (cn % NC) * ML.bytes;
-            bool ok = ws_wait(full + sl, (s / R) & 1, abort_flag, p.status, p.wait_ns);
-            if (!__all_sync(DG_FULL_MASK, ok)) break;
-            const uint32_t* raddr = reinterpret_cast<const uint32_t*>(mc + ML.addr) + ts * 64;
-            // rows forwarded from an earlier step in the window: that step's update (by all
-            // of its warps, whatever rows each took) must have finished
-            {
-                uint32_t dm = reinterpret_cast<const uint32_t*>(mc + ML.dmask)[ts];
-                while (dm != 0u && ok) {
-                    const int d = __ffs(dm) - 1;
-                    dm &= dm - 1;
-                    const int w = s - d;
-                    ok = ws_wait(done + (w % R), (w / R) & 1, abort_flag, p.status, p.wait_ns);
-                    ok = __all_sync(DG_FULL_MASK, ok);
+        // Two copies of the step loop.  With 128-byte parts (one CTA a lane, 15 warps)
+        // each step reads its GEMV's weights and row addresses before waiting for its
+        // forwarding writers, and its update's operands before waiting for the other
+        // slices' r.  With 64-byte parts the loop is kept as it was: the early reads, and
+        // even the restructured code around them, measured slower there.
+        if constexpr (PB == 128) {
+            for (int s = par; s < T_; s += KPAR) {
+                const int sl = s % R;
+                const int cn = s / CHS, ts = s % CHS;
+                const uint8_t* mc = meta + (cn % NC) * ML.bytes;
+                bool ok = ws_wait(full + sl, (s / R) & 1, abort_flag, p.status, p.wait_ns);
+                if (!__all_sync(DG_FULL_MASK, ok)) break;
+                const uint32_t* raddr = reinterpret_cast<const uint32_t*>(mc + ML.addr) + ts * 64;
+                // ---- GEMV: y and pred of the slice's 16 columns; its weights and row addresses
+                // are read before any wait for a forwarding writer ----
+                const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(
+                    reinterpret_cast<const uint16_t*>(mc + (g == 0 ? ML.wq : ML.wk)) + ts * A);
+                const bool bl = g < 2;
+                const int nkb = A >> 4;
+                uint32_t b[4][2], base[4];
+#pragma unroll
+                for (int kb = 0; kb < 4; ++kb) {
+                    const int kc = min(kb, nkb - 1);                  // in-bounds for every lane; unused blocks skipped below
+                    const uint32_t w0 = wsrc[kc * 8 + tig];
+                    const uint32_t w1 = wsrc[kc * 8 + 4 + tig];
+                    b[kb][0] = bl ? w0 : 0u;
+                    b[kb][1] = bl ? w1 : 0u;
+                    const int k = kc * 16 + kk;
+                    base[kb] = (raddr[k] & ~15u) + colb;
                 }
-                if (!ok) break;
-            }
-            // ---- GEMV: y and pred of the slice's 16 columns ----
-            const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(
-                reinterpret_cast<const uint16_t*>(mc + (g == 0 ? ML.wq : ML.wk)) + ts * A);
-            const bool bl = g < 2;
-            const int nkb = A >> 4;
-            uint32_t b[4][2], base[4];
-#pragma unroll
-            for (int kb = 0; kb < 4; ++kb) {
-                const int kc = min(kb, nkb - 1);                  // in-bounds for every lane; unused blocks skipped below
-                const uint32_t w0 = wsrc[kc * 8 + tig];
-                const uint32_t w1 = wsrc[kc * 8 + 4 + tig];
-                b[kb][0] = bl ? w0 : 0u;
-                b[kb][1] = bl ? w1 : 0u;
-                const int k = kc * 16 + kk;
-                base[kb] = (raddr[k] & ~15u) + colb;
-            }
-            uint32_t a[4][4];
-#pragma unroll
-            for (int kb = 0; kb < 4; ++kb)
-                if (kb < nkb) ldsm_x4_trans(base[kb], a[kb][0], a[kb][1], a[kb][2], a[kb][3]);
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int kb = 0; kb < 4; ++kb)
-                if (kb < nkb) MmaOp<T>::run(acc, a[kb], b[kb][0], b[kb][1]);
-            // lanes with tig == 0: acc = {y, pred} of column g and {y, pred} of column g + 8
-            float* rstep = rbuf + sl * (PB / 2);
-            if (tig == 0) {
-                const int col0 = q * 16 + g;                   // column within the part
-                const float bta = dg::to_f(reinterpret_cast<const T*>(mc + ML.beta)[ts]);
-                const T* mv = reinterpret_cast<const T*>(mc + ML.v) + ts * Dh + part * (PB / 2);
-                // y rows are staged per chunk parity: the same row of the next chunk may
-                // belong to another warp of the slice (KPAR need not divide CHS), which can
-                // be up to D < CHS steps ahead of this warp's flush
-                T* yrow = reinterpret_cast<T*>(ystage + ((cn & 1) * CHS + ts) * PB);
-                yrow[col0] = dg::from_f<T>(acc[0]);
-                yrow[col0 + 8] = dg::from_f<T>(acc[2]);
-                rstep[col0] = bta * (dg::to_f(mv[col0]) - acc[1]);
-                rstep[col0 + 8] = bta * (dg::to_f(mv[col0 + 8]) - acc[3]);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(rready + sl);
-            ok = ws_wait(rready + sl, (s / R) & 1, abort_flag, p.status, p.wait_ns);
-            if (!__all_sync(DG_FULL_MASK, ok)) break;
-            // ---- update: whole row parts, new rows (fp32, one rounding) to the ring slot
-            // and to global memory ----
-            const float4 ra = reinterpret_cast<const float4*>(rstep + uc * 8)[0];
-            const float4 rb = reinterpret_cast<const float4*>(rstep + uc * 8)[1];
-            const float br[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
-            const float al = p.dynamic_decay ? dg::to_f(reinterpret_cast<const T*>(mc + ML.alpha)[ts]) : alpha_static;
-            const unsigned long long al2 = f2pack(al, al);
-            const int64_t* midx = reinterpret_cast<const int64_t*>(mc + ML.idx) + ts * A;
-            const T* mwk = reinterpret_cast<const T*>(mc + ML.wk) + ts * A;
-            uint8_t* slot = rows + sl * SLOT;
-            int ucd[4];
-            int64_t ux[4];
-            float uwk[4];
-            uint4 uraw[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int m = q * RW + ur + RPI * i;           // rows >= A carry code -2 and are skipped
-                const int mcl = min(m, A - 1);
-                const uint32_t a = raddr[m];
-                const uint32_t src = a & ~15u;
-                ucd[i] = (a & 1u) ? -2 : 0;
-                ux[i] = midx[mcl];
-                uwk[i] = dg::to_f(mwk[mcl]);
-                uraw[i] = *reinterpret_cast<const uint4*>(rows + (src - rows_u) + uc * 16);
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int m = q * RW + ur + RPI * i;
-                // rows as gathered (zeros for an index out of range: its ring row was zero-filled)
-                if (p.saved != nullptr && m < A)
-                    dg::st16(static_cast<uint8_t*>(p.saved) + ((lt0 + s) * A + m) * row_bytes + part * PB + uc * 16,
-                             uraw[i]);
-                if (ucd[i] == -2) continue;
-                const uint32_t in[4] = {uraw[i].x, uraw[i].y, uraw[i].z, uraw[i].w};
-                uint32_t o[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 sv = unpack2(in[e], T());
-                    const unsigned long long u = mul_f32x2(f2pack(br[2 * e], br[2 * e + 1]), f2pack(uwk[i], uwk[i]));
-                    const float2 nv = f2unpack(fma_f32x2(al2, f2pack(sv.x, sv.y), u));
-                    o[e] = pack2(nv.x, nv.y, T());
+                // rows forwarded from an earlier step in the window: that step's update (by all
+                // of its warps, whatever rows each took) must have finished
+                {
+                    uint32_t dm = reinterpret_cast<const uint32_t*>(mc + ML.dmask)[ts];
+                    while (dm != 0u && ok) {
+                        const int d = __ffs(dm) - 1;
+                        dm &= dm - 1;
+                        const int w = s - d;
+                        ok = ws_wait(done + (w % R), (w / R) & 1, abort_flag, p.status, p.wait_ns);
+                        ok = __all_sync(DG_FULL_MASK, ok);
+                    }
+                    if (!ok) break;
                 }
-                const uint4 nv4 = make_uint4(o[0], o[1], o[2], o[3]);
-                *reinterpret_cast<uint4*>(slot + m * RS + uc * 16) = nv4;
-                dg::st16(gstate + ux[i] * row_bytes + uc * 16, nv4);
-            }
-            __syncwarp();
-            mbar_arrive(done + sl);
-            const int t0c = s - ts;
-            const int cend = min(t0c + CHS, T_);
-            if (s + KPAR >= cend) {                           // this warp's last step of the chunk
-                mbar_arrive(mfree + (cn % NC));
-                // this warp's y columns of the chunk: steps s = par (mod KPAR), i.e. rows j0, j0 + KPAR, ...
-                const int j0 = ((par - t0c) % KPAR + KPAR) % KPAR;
-                const int nj = (cend - t0c - j0 + KPAR - 1) / KPAR;
-                for (int i = lane; i < 2 * nj; i += 32) {
-                    const int jj = j0 + KPAR * (i >> 1), hh = i & 1;
-                    const uint4 val = *reinterpret_cast<const uint4*>(ystage + ((cn & 1) * CHS + jj) * PB + q * 32 + hh * 16);
-                    dg::st16(reinterpret_cast<uint8_t*>(gout + (lt0 + t0c + jj) * Dh) + part * PB + q * 32 + hh * 16,
-                             val);
+                uint32_t a[4][4];
+#pragma unroll
+                for (int kb = 0; kb < 4; ++kb)
+                    if (kb < nkb) ldsm_x4_trans(base[kb], a[kb][0], a[kb][1], a[kb][2], a[kb][3]);
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int kb = 0; kb < 4; ++kb)
+                    if (kb < nkb) MmaOp<T>::run(acc, a[kb], b[kb][0], b[kb][1]);
+                // lanes with tig == 0: acc = {y, pred} of column g and {y, pred} of column g + 8
+                float* rstep = rbuf + sl * (PB / 2);
+                if (tig == 0) {
+                    const int col0 = q * 16 + g;                   // column within the part
+                    const float bta = dg::to_f(reinterpret_cast<const T*>(mc + ML.beta)[ts]);
+                    const T* mv = reinterpret_cast<const T*>(mc + ML.v) + ts * Dh + part * (PB / 2);
+                    // y rows are staged per chunk parity: the same row of the next chunk may
+                    // belong to another warp of the slice (KPAR need not divide CHS), which can
+                    // be up to D < CHS steps ahead of this warp's flush
+                    T* yrow = reinterpret_cast<T*>(ystage + ((cn & 1) * CHS + ts) * PB);
+                    yrow[col0] = dg::from_f<T>(acc[0]);
+                    yrow[col0 + 8] = dg::from_f<T>(acc[2]);
+                    rstep[col0] = bta * (dg::to_f(mv[col0]) - acc[1]);
+                    rstep[col0 + 8] = bta * (dg::to_f(mv[col0 + 8]) - acc[3]);
                 }
                 __syncwarp();
+                if (lane == 0) mbar_arrive(rready + sl);
+                // ---- update: whole row parts, new rows (fp32, one rounding) to the ring slot
+                // and to global memory.  Its rows, indices and weights do not depend on the
+                // barrier (which orders only r, and the row writes after every slice's GEMV
+                // reads): they are read while the other slices finish ----
+                const float al = p.dynamic_decay ? dg::to_f(reinterpret_cast<const T*>(mc + ML.alpha)[ts]) : alpha_static;
+                const unsigned long long al2 = f2pack(al, al);
+                const int64_t* midx = reinterpret_cast<const int64_t*>(mc + ML.idx) + ts * A;
+                const T* mwk = reinterpret_cast<const T*>(mc + ML.wk) + ts * A;
+                uint8_t* slot = rows + sl * SLOT;
+                int ucd[4];
+                int64_t ux[4];
+                float uwk[4];
+                uint4 uraw[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int m = q * RW + ur + RPI * i;           // rows >= A carry code -2 and are skipped
+                    const int mcl = min(m, A - 1);
+                    const uint32_t a = raddr[m];
+                    const uint32_t src = a & ~15u;
+                    ucd[i] = (a & 1u) ? -2 : 0;
+                    ux[i] = midx[mcl];
+                    uwk[i] = dg::to_f(mwk[mcl]);
+                    uraw[i] = *reinterpret_cast<const uint4*>(rows + (src - rows_u) + uc * 16);
+                }
+                ok = ws_wait(rready + sl, (s / R) & 1, abort_flag, p.status, p.wait_ns);
+                if (!__all_sync(DG_FULL_MASK, ok)) break;
+                const float4 ra = reinterpret_cast<const float4*>(rstep + uc * 8)[0];
+                const float4 rb = reinterpret_cast<const float4*>(rstep + uc * 8)[1];
+                const float br[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int m = q * RW + ur + RPI * i;
+                    // rows as gathered (zeros for an index out of range: its ring row was zero-filled)
+                    if (p.saved != nullptr && m < A)
+                        dg::st16(static_cast<uint8_t*>(p.saved) + ((lt0 + s) * A + m) * row_bytes + part * PB + uc * 16,
+                                 uraw[i]);
+                    if (ucd[i] == -2) continue;
+                    const uint32_t in[4] = {uraw[i].x, uraw[i].y, uraw[i].z, uraw[i].w};
+                    uint32_t o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 sv = unpack2(in[e], T());
+                        const unsigned long long u = mul_f32x2(f2pack(br[2 * e], br[2 * e + 1]), f2pack(uwk[i], uwk[i]));
+                        const float2 nv = f2unpack(fma_f32x2(al2, f2pack(sv.x, sv.y), u));
+                        o[e] = pack2(nv.x, nv.y, T());
+                    }
+                    const uint4 nv4 = make_uint4(o[0], o[1], o[2], o[3]);
+                    *reinterpret_cast<uint4*>(slot + m * RS + uc * 16) = nv4;
+                    dg::st16(gstate + ux[i] * row_bytes + uc * 16, nv4);
+                }
+                __syncwarp();
+                mbar_arrive(done + sl);
+                const int t0c = s - ts;
+                const int cend = min(t0c + CHS, T_);
+                if (s + KPAR >= cend) {                           // this warp's last step of the chunk
+                    mbar_arrive(mfree + (cn % NC));
+                    // this warp's y columns of the chunk: steps s = par (mod KPAR), i.e. rows j0, j0 + KPAR, ...
+                    const int j0 = ((par - t0c) % KPAR + KPAR) % KPAR;
+                    const int nj = (cend - t0c - j0 + KPAR - 1) / KPAR;
+                    for (int i = lane; i < 2 * nj; i += 32) {
+                        const int jj = j0 + KPAR * (i >> 1), hh = i & 1;
+                        const uint4 val = *reinterpret_cast<const uint4*>(ystage + ((cn & 1) * CHS + jj) * PB + q * 32 + hh * 16);
+                        dg::st16(reinterpret_cast<uint8_t*>(gout + (lt0 + t0c + jj) * Dh) + part * PB + q * 32 + hh * 16,
+                                 val);
+                    }
+                    __syncwarp();
+                }
+            }
+        } else {
+            for (int s = par; s < T_; s += KPAR) {
+                const int sl = s % R;
+                const int cn = s / CHS, ts = s % CHS;
+                const uint8_t* mc = meta + (cn % NC) * ML.bytes;
+                bool ok = ws_wait(full + sl, (s / R) & 1, abort_flag, p.status, p.wait_ns);
+                if (!__all_sync(DG_FULL_MASK, ok)) break;
+                const uint32_t* raddr = reinterpret_cast<const uint32_t*>(mc + ML.addr) + ts * 64;
+                // rows forwarded from an earlier step in the window: that step's update (by all
+                // of its warps, whatever rows each took) must have finished
+                {
+                    uint32_t dm = reinterpret_cast<const uint32_t*>(mc + ML.dmask)[ts];
+                    while (dm != 0u && ok) {
+                        const int d = __ffs(dm) - 1;
+                        dm &= dm - 1;
+                        const int w = s - d;
+                        ok = ws_wait(done + (w % R), (w / R) & 1, abort_flag, p.status, p.wait_ns);
+                        ok = __all_sync(DG_FULL_MASK, ok);
+                    }
+                    if (!ok) break;
+                }
+                // ---- GEMV: y and pred of the slice's 16 columns ----
+                const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(
+                    reinterpret_cast<const uint16_t*>(mc + (g == 0 ? ML.wq : ML.wk)) + ts * A);
+                const bool bl = g < 2;
+                const int nkb = A >> 4;
+                uint32_t b[4][2], base[4];
+#pragma unroll
+                for (int kb = 0; kb < 4; ++kb) {
+                    const int kc = min(kb, nkb - 1);                  // in-bounds for every lane; unused blocks skipped below
+                    const uint32_t w0 = wsrc[kc * 8 + tig];
+                    const uint32_t w1 = wsrc[kc * 8 + 4 + tig];
+                    b[kb][0] = bl ? w0 : 0u;
+                    b[kb][1] = bl ? w1 : 0u;
+                    const int k = kc * 16 + kk;
+                    base[kb] = (raddr[k] & ~15u) + colb;
+                }
+                uint32_t a[4][4];
+#pragma unroll
+                for (int kb = 0; kb < 4; ++kb)
+                    if (kb < nkb) ldsm_x4_trans(base[kb], a[kb][0], a[kb][1], a[kb][2], a[kb][3]);
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int kb = 0; kb < 4; ++kb)
+                    if (kb < nkb) MmaOp<T>::run(acc, a[kb], b[kb][0], b[kb][1]);
+                // lanes with tig == 0: acc = {y, pred} of column g and {y, pred} of column g + 8
+                float* rstep = rbuf + sl * (PB / 2);
+                if (tig == 0) {
+                    const int col0 = q * 16 + g;                   // column within the part
+                    const float bta = dg::to_f(reinterpret_cast<const T*>(mc + ML.beta)[ts]);
+                    const T* mv = reinterpret_cast<const T*>(mc + ML.v) + ts * Dh + part * (PB / 2);
+                    // y rows are staged per chunk parity: the same row of the next chunk may
+                    // belong to another warp of the slice (KPAR need not divide CHS), which can
+                    // be up to D < CHS steps ahead of this warp's flush
+                    T* yrow = reinterpret_cast<T*>(ystage + ((cn & 1) * CHS + ts) * PB);
+                    yrow[col0] = dg::from_f<T>(acc[0]);
+                    yrow[col0 + 8] = dg::from_f<T>(acc[2]);
+                    rstep[col0] = bta * (dg::to_f(mv[col0]) - acc[1]);
+                    rstep[col0 + 8] = bta * (dg::to_f(mv[col0 + 8]) - acc[3]);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(rready + sl);
+                ok = ws_wait(rready + sl, (s / R) & 1, abort_flag, p.status, p.wait_ns);
+                if (!__all_sync(DG_FULL_MASK, ok)) break;
+                // ---- update: whole row parts, new rows (fp32, one rounding) to the ring slot
+                // and to global memory ----
+                const float4 ra = reinterpret_cast<const float4*>(rstep + uc * 8)[0];
+                const float4 rb = reinterpret_cast<const float4*>(rstep + uc * 8)[1];
+                const float br[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+                const float al = p.dynamic_decay ? dg::to_f(reinterpret_cast<const T*>(mc + ML.alpha)[ts]) : alpha_static;
+                const unsigned long long al2 = f2pack(al, al);
+                const int64_t* midx = reinterpret_cast<const int64_t*>(mc + ML.idx) + ts * A;
+                const T* mwk = reinterpret_cast<const T*>(mc + ML.wk) + ts * A;
+                uint8_t* slot = rows + sl * SLOT;
+                int ucd[4];
+                int64_t ux[4];
+                float uwk[4];
+                uint4 uraw[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int m = q * RW + ur + RPI * i;           // rows >= A carry code -2 and are skipped
+                    const int mcl = min(m, A - 1);
+                    const uint32_t a = raddr[m];
+                    const uint32_t src = a & ~15u;
+                    ucd[i] = (a & 1u) ? -2 : 0;
+                    ux[i] = midx[mcl];
+                    uwk[i] = dg::to_f(mwk[mcl]);
+                    uraw[i] = *reinterpret_cast<const uint4*>(rows + (src - rows_u) + uc * 16);
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int m = q * RW + ur + RPI * i;
+                    // rows as gathered (zeros for an index out of range: its ring row was zero-filled)
+                    if (p.saved != nullptr && m < A)
+                        dg::st16(static_cast<uint8_t*>(p.saved) + ((lt0 + s) * A + m) * row_bytes + part * PB + uc * 16,
+                                 uraw[i]);
+                    if (ucd[i] == -2) continue;
+                    const uint32_t in[4] = {uraw[i].x, uraw[i].y, uraw[i].z, uraw[i].w};
+                    uint32_t o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 sv = unpack2(in[e], T());
+                        const unsigned long long u = mul_f32x2(f2pack(br[2 * e], br[2 * e + 1]), f2pack(uwk[i], uwk[i]));
+                        const float2 nv = f2unpack(fma_f32x2(al2, f2pack(sv.x, sv.y), u));
+                        o[e] = pack2(nv.x, nv.y, T());
+                    }
+                    const uint4 nv4 = make_uint4(o[0], o[1], o[2], o[3]);
+                    *reinterpret_cast<uint4*>(slot + m * RS + uc * 16) = nv4;
+                    dg::st16(gstate + ux[i] * row_bytes + uc * 16, nv4);
+                }
+                __syncwarp();
+                mbar_arrive(done + sl);
+                const int t0c = s - ts;
+                const int cend = min(t0c + CHS, T_);
+                if (s + KPAR >= cend) {                           // this warp's last step of the chunk
+                    mbar_arrive(mfree + (cn % NC));
+                    // this warp's y columns of the chunk: steps s = par (mod KPAR), i.e. rows j0, j0 + KPAR, ...
+                    const int j0 = ((par - t0c) % KPAR + KPAR) % KPAR;
+                    const int nj = (cend - t0c - j0 + KPAR - 1) / KPAR;
+                    for (int i = lane; i < 2 * nj; i += 32) {
+                        const int jj = j0 + KPAR * (i >> 1), hh = i & 1;
+                        const uint4 val = *reinterpret_cast<const uint4*>(ystage + ((cn & 1) * CHS + jj) * PB + q * 32 + hh * 16);
+                        dg::st16(reinterpret_cast<uint8_t*>(gout + (lt0 + t0c + jj) * Dh) + part * PB + q * 32 + hh * 16,
+                                 val);
+                    }
+                    __syncwarp();
+                }
             }
         }
     }
