@@ -585,8 +585,12 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
                 bool ok = ws_wait(full + sl, (s / R) & 1, abort_flag, p.status, p.wait_ns);
                 if (!__all_sync(DG_FULL_MASK, ok)) break;
                 const uint32_t* raddr = reinterpret_cast<const uint32_t*>(mc + ML.addr) + ts * 64;
-                // ---- GEMV: y and pred of the slice's 16 columns; its weights and row addresses
-                // are read before any wait for a forwarding writer ----
+                // ---- GEMV: y and pred of the slice's 16 columns; its weights and row addresses,
+                // and the step's beta and v for r, are read before any wait for a forwarding
+                // writer ----
+                const float bta = dg::to_f(reinterpret_cast<const T*>(mc + ML.beta)[ts]);
+                const T* mv = reinterpret_cast<const T*>(mc + ML.v) + ts * Dh + part * (PB / 2);
+                const float v0 = dg::to_f(mv[q * 16 + g]), v8 = dg::to_f(mv[q * 16 + g + 8]);
                 const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(
                     reinterpret_cast<const uint16_t*>(mc + (g == 0 ? ML.wq : ML.wk)) + ts * A);
                 const bool bl = g < 2;
@@ -627,16 +631,14 @@ __global__ void __launch_bounds__(32 * (GatherCfg<PB>::ROLE_WARPS + GatherCfg<PB
                 float* rstep = rbuf + sl * (PB / 2);
                 if (tig == 0) {
                     const int col0 = q * 16 + g;                   // column within the part
-                    const float bta = dg::to_f(reinterpret_cast<const T*>(mc + ML.beta)[ts]);
-                    const T* mv = reinterpret_cast<const T*>(mc + ML.v) + ts * Dh + part * (PB / 2);
                     // y rows are staged per chunk parity: the same row of the next chunk may
                     // belong to another warp of the slice (KPAR need not divide CHS), which can
                     // be up to D < CHS steps ahead of this warp's flush
                     T* yrow = reinterpret_cast<T*>(ystage + ((cn & 1) * CHS + ts) * PB);
                     yrow[col0] = dg::from_f<T>(acc[0]);
                     yrow[col0 + 8] = dg::from_f<T>(acc[2]);
-                    rstep[col0] = bta * (dg::to_f(mv[col0]) - acc[1]);
-                    rstep[col0 + 8] = bta * (dg::to_f(mv[col0 + 8]) - acc[3]);
+                    rstep[col0] = bta * (v0 - acc[1]);
+                    rstep[col0 + 8] = bta * (v8 - acc[3]);
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(rready + sl);
