@@ -226,6 +226,29 @@ def make_inputs(w, torch, device, seed=0):
     return dict(v=v, beta=beta, wk=wk, wq=wq, idx=idx, decay=decay, state=state, kr=kr, qr=qr, routers=routers)
 
 
+def e2e_pieces(w, override=0):
+    """[(start, end)] of the end-to-end leg's pieces: batch rows for dense (a piece's
+    compute is one chain of chunks whatever its lanes, so few pieces, the first and the
+    last small: B/16 rows each and the middle in four, or one row each below 16 rows),
+    steps for PKM (eight even pieces in whole 8-step groups, else four, two, one);
+    `override` asks for that many even pieces."""
+    if w["kind"] == "dense":
+        B = w["B"]
+        if override:
+            n = next(k for k in (override, 1) if B % k == 0)
+            sizes = [B // n] * n
+        elif B >= 16:
+            edge = B // 16
+            mid = B - 2 * edge
+            sizes = [edge] + [mid // 4 + (1 if i < mid % 4 else 0) for i in range(4)] + [edge]
+        else:
+            sizes = [1] * B
+        return [(sum(sizes[:i]), sum(sizes[:i + 1])) for i in range(len(sizes))]
+    T = w["T"]
+    n = next(k for k in ((override,) if override else (8, 4, 2, 1)) if T % (8 * k) == 0)
+    return [(i * (T // n), (i + 1) * (T // n)) for i in range(n)]
+
+
 def _sm_count():
     try:
         import torch
@@ -756,22 +779,10 @@ def main():
         # consecutive calls anyway: rows are rounded to the storage type every step, so the
         # pieces give the unsplit call's results bit for bit).
         names = ("kr", "v", "beta") if w.get("writes") else ("kr", "qr", "v", "beta")
+        bounds = e2e_pieces(w, args.e2e_pieces)
         if w["kind"] == "dense":
-            Bp = w["B"]
-            if args.e2e_pieces:
-                npc = next(n for n in (args.e2e_pieces, 1) if Bp % n == 0)
-                sizes = [Bp // npc] * npc
-            elif Bp >= 16:
-                edge = Bp // 16
-                mid = Bp - 2 * edge
-                sizes = [edge] + [mid // 4 + (1 if i < mid % 4 else 0) for i in range(4)] + [edge]
-            else:
-                sizes = [1] * Bp
-            bounds = [(sum(sizes[:i]), sum(sizes[:i + 1])) for i in range(len(sizes))]
             cut = lambda t, i: t[bounds[i][0]:bounds[i][1]]
         else:
-            npc = next(n for n in ((args.e2e_pieces,) if args.e2e_pieces else (8, 4, 2, 1)) if w["T"] % (8 * n) == 0)
-            bounds = [(i * (w["T"] // npc), (i + 1) * (w["T"] // npc)) for i in range(npc)]
             cut = lambda t, i: t[:, :, bounds[i][0]:bounds[i][1]]
         npc = len(bounds)
         # pinned host inputs and device buffers, one contiguous block per piece

@@ -62,3 +62,28 @@ def test_reference_arm_prints_the_contract_line():
     assert line["cpu_baseline"]["kind"] == "reference" and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
     assert "engine_q16" in line["cpu_legs"]
+
+
+@pytest.mark.parametrize("B", [1, 2, 4, 5, 8, 16, 32, 256])
+def test_dense_e2e_pieces_cover_the_batch_once(B):
+    w = dict(bench.WORKLOADS["cfg2"], B=B)
+    b = bench.e2e_pieces(w)
+    assert b[0][0] == 0 and b[-1][1] == B and all(x[1] == y[0] for x, y in zip(b, b[1:]))
+    assert all(hi > lo for lo, hi in b)
+    if B >= 16:       # small first and last pieces, the middle in four
+        assert len(b) == 6 and b[0][1] - b[0][0] == B // 16 == b[-1][1] - b[-1][0]
+    assert bench.e2e_pieces(w, 4) == ([(i * B // 4, (i + 1) * B // 4) for i in range(4)] if B % 4 == 0 else [(0, B)])
+
+
+def test_pkm_e2e_pieces_and_launch_counts():
+    for name in ("cfg3", "cfg4"):
+        w = bench.WORKLOADS[name]
+        b = bench.e2e_pieces(w)
+        assert len(b) == 8 and b[-1][1] == w["T"] and all((hi - lo) % 8 == 0 for lo, hi in b)
+        # four step pieces of pre-pass and recurrence when 8 SMs stay free, else one of each
+        assert bench.launches_per_step(w, sms=148) == 8
+        assert bench.launches_per_step(w, sms=128) == 2
+    w = dict(bench.WORKLOADS["cfg3"], T=512)
+    assert bench.launches_per_step(w, sms=148) == 2
+    assert bench.launches_per_step(bench.WORKLOADS["cfg2"], sms=148) == 1
+    assert bench.launches_per_step(bench.WORKLOADS["cfg5"], sms=148) == 12
