@@ -291,10 +291,12 @@ int dg_dense_route(int dtype, int B, int H, int T, int dh, int slots, const void
  *   wk, wq [B,H,T,top_k^2] (storage dtype), idx [B,H,T,top_k^2] int64 = i0*g1 + i1
  * Scores are fp32 dot products in increasing dh order; equal scores keep the
  * lower index first (src/cpp/engine/src/deltagrid_math.cpp:155-167).
- * The tensor-core form (16-bit k, dh = 64, top_k 4 or 8) keeps a split copy of the
- * router weights in a per-device buffer allocated on first use and reused by later
- * calls, which wait for the previous call's kernels (calls under stream capture
- * allocate their copy from the stream instead).
+ * The tensor-core form (16-bit k, dh = 64, top_k 4 or 8; both axes of one size of
+ * 32, 64, 96 or 128 rows, or each a multiple of 128 rows) keeps a split
+ * copy of the router weights in a per-device buffer allocated on first use and
+ * reused by later calls, which wait for the previous call's kernels (calls under
+ * stream capture allocate their copy from the stream instead).  Other shapes run
+ * the CUDA-core form, with the same results.
  */
 int dg_pkm_route(int dtype, int B, int H, int T, int dh, int g0, int g1, int top_k, const void* k,
                  const void* q, const float* router_k0, const float* router_k1, const float* router_q0,
